@@ -1,0 +1,506 @@
+#!/usr/bin/env python
+"""bench.py -- the headline measurement of lyth_b200 on B200.
+
+Metric: 33-qubit state-vector gates/s at 1-8 GPUs, and HBM GB/s (% of the
+measured B200 peak) per kernel class.
+
+One JSON line on rank 0:
+  * value      whole-job gates/s of the layered circuit (H on every qubit, CU(phase) on adjacent
+               pairs, SWAP on a random pairing; 81 gates per layer at 33 qubits) from a seeded
+               random normalised state resident in HBM; one step = one layer; strong scaling
+               (33 qubits at every N, sharded on the high qubits). Device time (CUDA events on
+               the engine's stream), max over ranks.
+  * roofline   the dominant kernel (the in-place 1-qubit pass): algorithmic bytes (16 B per
+               amplitude) / its average device duration inside the timed region.
+  * e2e        the same metric through the public API with host buffers: each step uploads the
+               shard from pinned host memory, applies the layer, and reads the shard back.
+  * cpu_baseline  the host evaluator port (oracle/) on a bounded sample, rank 0, N = 1.
+  * per_kernel HBM GB/s of every other kernel class at its BASELINE config (rank 0, N = 1).
+
+``--impl reference`` times the reference's algorithm on the host cores instead (the oracle
+port: the reference is Rust and cannot be built in this image) and prints the same line.
+
+Run: python bench.py [--gpus N] [--steps K] [--warmup W]; N > 1 under torch.distributed.run.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}
+METRIC = "33-qubit statevector gates/s (HBM GB/s per kernel alongside)"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def args_():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--qubits", type=int, default=33)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--skip-kernels", action="store_true", help="omit the per-kernel table")
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--cpu-qubits", type=int, default=25)
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.lines: list[str] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_id_for(dev_index: int) -> str:
+    import torch
+
+    try:
+        u = str(torch.cuda.get_device_properties(dev_index).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            return vis.split(",")[dev_index]
+        return str(dev_index)
+
+
+# --------------------------------------------------------------------------- distributed
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self):
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def bcast_bytes(self, b: bytes | None) -> bytes:
+        if not self.pg:
+            return b
+        obj = [b]
+        self.pg.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.pg:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
+# --------------------------------------------------------------------------- CPU baseline
+def cpu_sample(qubits: int, budget_s: float = 15.0) -> dict:
+    """The oracle port applying the layered circuit's gates on a 2^qubits state, all host cores,
+    for about budget_s; gates/s scaled to the 33-qubit state (work is linear in the state)."""
+    import numpy as np
+
+    from lyth_b200 import circuit as cc
+    from oracle import oracle as orc
+
+    gates = cc.layered(qubits, 2, cc.Rng(cc.BENCH_SEED))
+    re, im = orc.random_state(3, qubits)
+    done, t0 = 0, time.perf_counter()
+    for g in gates:
+        if isinstance(g, cc.U):
+            orc.gate_q(1 << g.q, cc.f32s(g.m), re, im, inplace=True)
+        elif isinstance(g, cc.CU):
+            wc, wt = orc.widths_ct(g.c, g.t)
+            orc.cu_q(wc, wt, cc.f32s(g.m), re, im, inplace=True)
+        else:
+            wc, wt = orc.widths_ct(g.a, g.b)
+            orc.swap_q(wc, wt, re, im, inplace=True)
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    gps = done / dt
+    del np
+    return {"gates": done, "seconds": dt, "gates_per_s_at_sample": gps,
+            "gates_per_s_at_33": gps / float(1 << (33 - qubits)), "cores": orc.threads(),
+            "sample": f"{done} gates of the layered circuit on a {qubits}-qubit state (oracle port, unfused, "
+                      f"in place), scaled to 33 qubits by 2^-{33 - qubits} (each gate is one pass over the state)"}
+
+
+def reference_arm(a, dist: Dist) -> None:
+    """--impl reference: the reference's algorithm on the host cores (the oracle port; the Rust
+    reference cannot be built here). Rank 0 only; the other ranks exit without work."""
+    if dist.rank != 0:
+        return
+    steps = []
+    for _ in range(a.warmup):
+        cpu_sample(a.cpu_qubits, budget_s=2.0)
+    for _ in range(a.steps):
+        steps.append(cpu_sample(a.cpu_qubits, budget_s=8.0))
+    v = sum(s["gates"] for s in steps) / sum(s["seconds"] for s in steps) / float(1 << (33 - a.cpu_qubits))
+    cores = steps[0]["cores"]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "gates/s", "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 * 81 / v if v else None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: SplitMix64-seeded normalised random state, layered circuit seed 20260930",
+        "config": {"workload": "statevector layered circuit, 33 qubits, 81 gates per layer (one step = one layer)",
+                   "qubits": 33, "gates_per_step": 81},
+        "cpu_baseline": {"value": v, "unit": "gates/s", "cores": cores, "kind": "port",
+                         "sample": steps[0]["sample"]},
+        "e2e": {"value": v, "unit": "gates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "QuantumDrizzy/LYTH is Rust (no cargo/rustc in this image); its host evaluator is timed "
+                "through this repository's C restatement of it (oracle/lythref.c)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- per-kernel table
+def per_kernel(pk: dict) -> dict:
+    """HBM GB/s of each kernel class at its BASELINE config, CUDA events on the current stream,
+    L2 flushed (a 256 MiB write) before every timed launch, median of the reps."""
+    import numpy as np
+    import torch
+
+    import lyth_b200 as lb
+
+    dev = torch.device("cuda")
+    hbm = pk["hbm_gbs"]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    out = {}
+
+    def timeit(fn, reps=10, warm=3):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(reps):
+            flush.fill_(1.0)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            ts.append(s.elapsed_time(e))
+        return statistics.median(ts)
+
+    def row(name, byts, ms, extra=None):
+        gbs = byts / (ms * 1e-3) / 1e9
+        r = {"GB_s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4), "ms": round(ms, 5), "bytes": int(byts)}
+        if extra:
+            r.update(extra)
+        out[name] = r
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    # saxpy sweep 2^20 .. 2^30 (12 B/elem)
+    for p in (20, 22, 24, 26, 28, 30):
+        n = 1 << p
+        x = torch.rand(n, device=dev, generator=g)
+        y = torch.rand(n, device=dev, generator=g)
+        row(f"saxpy_2^{p}", 12.0 * n, timeit(lambda: lb.saxpy(2.5, x, y)))
+        del x, y
+    n = 1 << 28
+    x = torch.rand(n, device=dev, generator=g)
+    y = torch.rand(n, device=dev, generator=g)
+    z = torch.empty_like(x)
+    row("axpby_2^28", 12.0 * n, timeit(lambda: lb.axpby(1.5, 0.5, x, y)))
+    row("lerp_2^28", 12.0 * n, timeit(lambda: lb.lerp(0.3, x, y, z)))
+    row("horner_2^28", 8.0 * n, timeit(lambda: lb.horner(0.1, 0.2, 0.3, 0.4, x, z)))
+    row("sum_2^28", 4.0 * n, timeit(lambda: lb.reduce_partials(lb.SUM, x)))
+    row("max_2^28", 4.0 * n, timeit(lambda: lb.reduce_partials(lb.MAX, x)))
+    row("dot_2^28", 8.0 * n, timeit(lambda: lb.reduce_partials(lb.SUM, x, y)))
+    del x, y, z
+    # transposes 4096^2 (8 B/elem payload)
+    a = torch.rand(4096, 4096, device=dev, generator=g)
+    b = torch.empty(4096, 4096, device=dev)
+    nn = 4096 * 4096
+    row("transpose_tiled_4096", 8.0 * nn, timeit(lambda: lb.transpose_tiled(a, b)))
+    row("copy2d_4096", 8.0 * nn, timeit(lambda: lb.copy2d(a, b)))
+    row("transpose_naive_4096", 8.0 * nn, timeit(lambda: lb.transpose_naive(a, b)))
+    del a, b
+    # gate_proj GEMV, 4096 -> 14336, group 64
+    rows, k, grp = 14336, 4096, 64
+    w = torch.randint(0, 256, (rows, k // 2), dtype=torch.uint8, device=dev, generator=g)
+    sc = (torch.rand(rows * (k // grp), device=dev, generator=g) * 0.02).half()
+    xv = torch.randn(k, device=dev, generator=g).half()
+    yv = torch.empty(rows, dtype=torch.float16, device=dev)
+    gbytes = rows * k / 2 + rows * (k // grp) * 2 + k * 2 + rows * 2
+    row("gemv_int4_4096x14336", gbytes, timeit(lambda: lb.gemv_q4(lb.GEMV_INT4, w, sc, xv, yv, grp), reps=20))
+    row("gemv_nf4_4096x14336", gbytes, timeit(lambda: lb.gemv_q4(lb.GEMV_NF4, w, sc, xv, yv, grp), reps=20))
+    del w, sc, xv, yv
+    # f32 contraction 4096^3 (FP32 pipe: TFLOP/s against the nominal FFMA rate at the max clock)
+    m = 4096
+    A = torch.randn(m, m, device=dev, generator=g) / 64.0
+    B = torch.randn(m, m, device=dev, generator=g) / 64.0
+    Cm = torch.empty(m, m, device=dev)
+    ffma_peak = 148 * 128 * 2 * pk.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
+    for exact in (False, True):
+        ms = timeit(lambda: lb.matmul_f32(A, B, Cm, exact=exact), reps=5, warm=2)
+        tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
+        out["matmul_f32_4096" + ("_exact" if exact else "_ffma")] = {
+            "TFLOP_s": round(tf, 2), "frac_fp32_nominal": round(tf / ffma_peak, 4), "ms": round(ms, 4),
+            "fp32_nominal_tflops": round(ffma_peak, 1)}
+    try:
+        Ab, Bb = A.bfloat16(), B.bfloat16()
+        ms = timeit(lambda: lb.matmul_bf16(Ab, Bb, Cm), reps=10, warm=3)
+        tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
+        out["matmul_bf16_4096"] = {"TFLOP_s": round(tf, 1), "frac_bf16_measured": round(tf / pk["bf16_tflops"], 4),
+                                   "ms": round(ms, 4)}
+    except Exception as e:  # the tensor-core path refuses shapes it does not take
+        out["matmul_bf16_4096"] = {"unavailable": str(e)[:120]}
+    del A, B, Cm, flush
+    torch.cuda.empty_cache()
+    del np
+    return out
+
+
+# --------------------------------------------------------------------------- our arm
+def ours(a, dist: Dist) -> None:
+    import numpy as np
+    import torch
+
+    import lyth_b200 as lb
+    from lyth_b200 import circuit as cc
+    from lyth_b200.statevector import gates_array
+
+    pk, pk_kind = peaks()
+    q = a.qubits
+    nid = lb.unique_id() if (dist.world > 1 and dist.rank == 0) else None
+    nid = dist.bcast_bytes(nid)
+    sv = lb.StateVector(q, device=dist.local, rank=dist.rank, nranks=dist.world, nccl_id=nid)
+    total_layers = a.warmup + a.steps
+    gates = cc.layered(q, total_layers, cc.Rng(cc.BENCH_SEED))
+    per = len(gates) // total_layers
+    layers = [gates_array(gates[i * per:(i + 1) * per]) for i in range(total_layers)]
+    sv.init_random(cc.BENCH_SEED)
+    for i in range(a.warmup):
+        lb.check(lb.lib.lyth_sv_apply(sv._h, layers[i], per), "apply")
+    sv.sync()
+    stream = torch.cuda.ExternalStream(sv.stream)
+    clocks = Clocks(gpu_id_for(dist.local))
+    launches0 = sv.stats()["launches"]
+    sv.reset_timing()
+    sv.set_timing(True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(a.warmup, total_layers):
+        lb.check(lb.lib.lyth_sv_apply(sv._h, layers[i], per), "apply")
+    t_end.record(stream)
+    sv.sync()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    ms_local = t_start.elapsed_time(t_end)
+    ms = dist.max(ms_local)
+    sv.set_timing(False)
+    tim = sv.timing()
+    launches = dist.sum(float(sv.stats()["launches"] - launches0))
+    st = sv.stats()
+    gates_timed = a.steps * per
+    value = gates_timed / (ms * 1e-3)
+
+    # roofline of the dominant kernel: the in-place 1-qubit pass, 16 B per local amplitude.
+    u_n, u_ms = tim["u"]
+    cu_n, cu_ms = tim["cu"]
+    ex_n, ex_ms = tim["exchange"]
+    u_bytes = 16.0 * sv.local_len
+    u_avg = u_ms / u_n if u_n else float("nan")
+    achieved = u_bytes / (u_avg * 1e-3) / 1e9 if u_n else None
+    peak = pk["hbm_gbs"]
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4) if achieved else None, "traffic": None,
+                "peak_source": pk_kind, "kernel": "gate_q_kernel (in-place 1-qubit pass)",
+                "algorithmic_bytes_per_launch": int(u_bytes), "avg_launch_ms": round(u_avg, 4),
+                "launches_timed": u_n,
+                "cu_pass": {"launches": cu_n, "avg_ms": round(cu_ms / cu_n, 4) if cu_n else None,
+                            "GB_s": round(8.0 * sv.local_len / (cu_ms / cu_n * 1e-3) / 1e9, 1) if cu_n else None},
+                "exchange": {"gates": ex_n, "avg_ms": round(ex_ms / ex_n, 4) if ex_n else None}}
+    traffic_ratio = os.environ.get("LYTH_GATE_TRAFFIC_RATIO")
+    if traffic_ratio:
+        roofline["traffic"] = int(float(traffic_ratio) * u_bytes)
+
+    # e2e: upload the shard from pinned host memory, apply one layer, read the shard back.
+    e2e = None
+    if not a.skip_e2e:
+        hre = torch.empty(sv.local_len, dtype=torch.float32, pin_memory=True)
+        him = torch.empty(sv.local_len, dtype=torch.float32, pin_memory=True)
+        sv.get_local(hre.data_ptr(), him.data_ptr())
+        order = [a.warmup + (i % a.steps) for i in range(1 + a.e2e_steps)]
+        times = []
+        for j, li in enumerate(order):
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            sv.set_local(hre.data_ptr(), him.data_ptr())
+            lb.check(lb.lib.lyth_sv_apply(sv._h, layers[li], per), "apply")
+            sv.get_local(hre.data_ptr(), him.data_ptr())
+            e1.record(stream)
+            e1.synchronize()
+            dist.barrier()
+            if j > 0:
+                times.append(dist.max(e0.elapsed_time(e1)))
+            else:
+                dist.max(0.0)
+        e_ms = sum(times) / len(times)
+        nbytes = 8 * sv.local_len * dist.world
+        e2e = {"value": per / (e_ms * 1e-3), "unit": "gates/s", "h2d_bytes_per_step": nbytes,
+               "d2h_bytes_per_step": nbytes, "ms_per_step": round(e_ms, 2), "steps": len(times),
+               "what": "lyth_sv_set_local (pinned host -> HBM), lyth_sv_apply (one layer), lyth_sv_get_local "
+                       "(qubit map undone, HBM -> pinned host)"}
+        del hre, him
+    sv.close()
+    torch.cuda.empty_cache()
+
+    cpu = None
+    kernels = None
+    if dist.rank == 0 and dist.world == 1:
+        if not a.skip_kernels:
+            kernels = per_kernel(pk)
+        if not a.skip_cpu:
+            cpu = cpu_sample(a.cpu_qubits)
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "gates/s", "n_gpus": dist.world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: SplitMix64-seeded normalised random complex64 state (split re/im f32); "
+                    "layered circuit from circuits::Rng seed 20260930",
+            "config": {"workload": f"statevector layered circuit, {q} qubits, {per} gates per layer "
+                                   "(H on every qubit, CU(phase) on adjacent pairs, SWAP on a random pairing), "
+                                   "one step = one layer",
+                       "qubits": q, "gates_per_step": per, "global_qubits": q - (sv.local_len.bit_length() - 1),
+                       "parallelism": f"sharded on the high {int(np.log2(dist.world))} qubits" if dist.world > 1
+                       else "1 GPU, in place",
+                       "l2": f"inputs larger than L2: the state is {8 * (1 << q) / 2**30:.0f} GiB"},
+            "roofline": roofline,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"]},
+            "engine": {"passes": st["passes"], "exchanges": st["exchanges"], "bytes_sent": st["bytes_sent"]},
+        }
+        if cpu:
+            line["cpu_baseline"] = {"value": cpu["gates_per_s_at_33"], "unit": "gates/s", "cores": cpu["cores"],
+                                    "kind": "port", "sample": cpu["sample"]}
+        if kernels:
+            line["per_kernel"] = kernels
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    a = args_()
+    dist = Dist()
+    if a.impl == "reference":
+        reference_arm(a, dist)
+        return
+    dist.init()
+    try:
+        ours(a, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,513 @@
+/*
+ * lyth_b200.h -- the C ABI of liblyth_b200.so, a B200 (sm_100a) execution back end for the
+ * kernel classes LYTH's `.lyth` compiler lowers to.
+ *
+ * Two surfaces:
+ *
+ *  1. The ADR-0016 callable surface, per kernel, with the exact names, signatures and
+ *     contract macros LYTH's C binding generator emits (reference:
+ *     crates/lyth/src/bind_c.rs:39-395; worked example crates/lyth/tests/generated/saxpy.h:17-38).
+ *     `lyth_<k>_load` hands out the precompiled sm_100a kernel instead of JIT-loading PTX;
+ *     `lyth_<k>_launch` / `_launch_with` launch it with cuLaunchKernel on stream 0, as the
+ *     generated bodies do (bind_c.rs:345-395). LYTH never owns memory (ADR-0016 rule 1):
+ *     every buffer is the caller's device pointer.
+ *
+ *  2. The B200 surface `lyth_b200_*` / `lyth_sv_*`: the same kernels with 64-bit sizes and an
+ *     explicit stream, the kernel classes the reference only costs (INT4/NF4 GEMV, bf16
+ *     tensor-core contraction), and the sharded state vector (no reference counterpart: the
+ *     reference has no multi-GPU code). Status: 0 = ok, > 0 = a cudaError_t passed through,
+ *     < 0 = a LYTH refusal (below).
+ *
+ * Nothing here allocates except lyth_sv_create (the state vector it owns) and the one-time
+ * module set-up inside the CUDA runtime. There is no CPU fallback: without a device every
+ * launch returns the CUDA error.
+ */
+#ifndef LYTH_B200_H
+#define LYTH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------------------ */
+/* Status codes of the B200 surface. CUDA errors pass through as their positive value.   */
+#define LYTH_OK 0
+/* A split launch refused: a width of 0, or 2*width not dividing the level's length
+ * (crates/lyth-lang/src/ir.rs:164-184, split_pairs ir.rs:202-261). Nothing ran. */
+#define LYTH_E_SPLIT (-1)
+/* A shape or parameter the kernel class does not take (mirrors EmitError, lyth-ptx/src/lib.rs:48-62). */
+#define LYTH_E_UNSUPPORTED (-2)
+/* A null pointer, an extent of zero where one is needed, or a size past a 32-bit index. */
+#define LYTH_E_INVALID (-3)
+/* A bounded device-side wait ran out; the kernel returned without finishing. */
+#define LYTH_E_TIMEOUT (-4)
+/* NCCL reported an error (or a peer failed) during a state-vector exchange. */
+#define LYTH_E_NCCL (-5)
+/* The NCCL library could not be loaded for a multi-rank state vector. */
+#define LYTH_E_NO_NCCL (-6)
+/* A state-vector allocation failed. */
+#define LYTH_E_OOM (-7)
+
+/* A human-readable name for any status above (LYTH or CUDA). Never NULL. */
+const char *lyth_b200_error_string(int status);
+/* ABI version of this header: major * 10000 + minor * 100 + patch. */
+int lyth_b200_version(void);
+
+/* ==================================================================================== */
+/* 1. ADR-0016 surface (bind_c.rs). `MACHINE` names the image this library carries.        */
+/* ==================================================================================== */
+
+/* ---- saxpy: examples/saxpy.lyth, y = a*x + y -> fma(a, x, y) ------------------------- */
+#define LYTH_SAXPY_KERNEL "saxpy"
+#define LYTH_SAXPY_MACHINE "sm_100a"
+#define LYTH_SAXPY_BLOCK 256u
+#define LYTH_SAXPY_SHARED_BYTES 0u
+#define LYTH_SAXPY_MAX_GRID 1048576u
+#define LYTH_SAXPY_DERIVED_INTENSITY 0.16666666666666666
+#define LYTH_SAXPY_FLOPS_PER_ELEMENT 2.0
+#define LYTH_SAXPY_BYTES_PER_ELEMENT 12.0
+#define LYTH_SAXPY_COALESCENCE 1.0
+unsigned int lyth_saxpy_elements(unsigned int n);
+unsigned int lyth_saxpy_grid(unsigned int n);
+/* The kernel writes: y. */
+CUresult lyth_saxpy_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_saxpy_launch(CUfunction fn, unsigned int n, float a, CUdeviceptr x, CUdeviceptr y);
+CUresult lyth_saxpy_launch_with(CUfunction fn, unsigned int grid, unsigned int n, float a, CUdeviceptr x, CUdeviceptr y);
+
+/* ---- axpby: examples/axpby.lyth, y = a*x + b*y -> fma(a, x, mul(b, y)) --------------- */
+#define LYTH_AXPBY_KERNEL "axpby"
+#define LYTH_AXPBY_MACHINE "sm_100a"
+#define LYTH_AXPBY_BLOCK 256u
+#define LYTH_AXPBY_SHARED_BYTES 0u
+#define LYTH_AXPBY_MAX_GRID 1048576u
+#define LYTH_AXPBY_DERIVED_INTENSITY 0.25
+#define LYTH_AXPBY_FLOPS_PER_ELEMENT 3.0
+#define LYTH_AXPBY_BYTES_PER_ELEMENT 12.0
+#define LYTH_AXPBY_COALESCENCE 1.0
+unsigned int lyth_axpby_elements(unsigned int n);
+unsigned int lyth_axpby_grid(unsigned int n);
+/* The kernel writes: y. */
+CUresult lyth_axpby_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_axpby_launch(CUfunction fn, unsigned int n, float a, float b, CUdeviceptr x, CUdeviceptr y);
+CUresult lyth_axpby_launch_with(CUfunction fn, unsigned int grid, unsigned int n, float a, float b, CUdeviceptr x, CUdeviceptr y);
+
+/* ---- lerp: examples/lerp.lyth, z = x + t*(y - x) -> fma(t, sub(y, x), x) ------------- */
+#define LYTH_LERP_KERNEL "lerp"
+#define LYTH_LERP_MACHINE "sm_100a"
+#define LYTH_LERP_BLOCK 256u
+#define LYTH_LERP_SHARED_BYTES 0u
+#define LYTH_LERP_MAX_GRID 1048576u
+#define LYTH_LERP_DERIVED_INTENSITY 0.25
+#define LYTH_LERP_FLOPS_PER_ELEMENT 3.0
+#define LYTH_LERP_BYTES_PER_ELEMENT 12.0
+#define LYTH_LERP_COALESCENCE 1.0
+unsigned int lyth_lerp_elements(unsigned int n);
+unsigned int lyth_lerp_grid(unsigned int n);
+/* The kernel writes: z. */
+CUresult lyth_lerp_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_lerp_launch(CUfunction fn, unsigned int n, float t, CUdeviceptr x, CUdeviceptr y, CUdeviceptr z);
+CUresult lyth_lerp_launch_with(CUfunction fn, unsigned int grid, unsigned int n, float t, CUdeviceptr x, CUdeviceptr y, CUdeviceptr z);
+
+/* ---- horner: examples/horner.lyth, y = fma(fma(fma(c3, x, c2), x, c1), x, c0) -------- */
+#define LYTH_HORNER_KERNEL "horner"
+#define LYTH_HORNER_MACHINE "sm_100a"
+#define LYTH_HORNER_BLOCK 256u
+#define LYTH_HORNER_SHARED_BYTES 0u
+#define LYTH_HORNER_MAX_GRID 1048576u
+#define LYTH_HORNER_DERIVED_INTENSITY 0.75
+#define LYTH_HORNER_FLOPS_PER_ELEMENT 6.0
+#define LYTH_HORNER_BYTES_PER_ELEMENT 8.0
+#define LYTH_HORNER_COALESCENCE 1.0
+unsigned int lyth_horner_elements(unsigned int n);
+unsigned int lyth_horner_grid(unsigned int n);
+/* The kernel writes: y. */
+CUresult lyth_horner_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_horner_launch(CUfunction fn, unsigned int n, float c0, float c1, float c2, float c3, CUdeviceptr x, CUdeviceptr y);
+CUresult lyth_horner_launch_with(CUfunction fn, unsigned int grid, unsigned int n, float c0, float c1, float c2, float c3, CUdeviceptr x, CUdeviceptr y);
+
+/* ---- copy2d: examples/copy2d.lyth, b[i, j] = a[i, j] (the coalesced control) --------- */
+#define LYTH_COPY2D_KERNEL "copy2d"
+#define LYTH_COPY2D_MACHINE "sm_100a"
+#define LYTH_COPY2D_BLOCK 256u
+#define LYTH_COPY2D_SHARED_BYTES 0u
+#define LYTH_COPY2D_MAX_GRID 1048576u
+#define LYTH_COPY2D_DERIVED_INTENSITY 0.0
+#define LYTH_COPY2D_FLOPS_PER_ELEMENT 0.0
+#define LYTH_COPY2D_BYTES_PER_ELEMENT 8.0
+#define LYTH_COPY2D_COALESCENCE 1.0
+unsigned int lyth_copy2d_elements(unsigned int rows, unsigned int cols);
+unsigned int lyth_copy2d_grid(unsigned int rows, unsigned int cols);
+/* The kernel writes: b. */
+CUresult lyth_copy2d_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_copy2d_launch(CUfunction fn, unsigned int rows, unsigned int cols, CUdeviceptr a, CUdeviceptr b);
+CUresult lyth_copy2d_launch_with(CUfunction fn, unsigned int grid, unsigned int rows, unsigned int cols, CUdeviceptr a, CUdeviceptr b);
+
+/* ---- transpose: examples/transpose.lyth, b[j, i] = a[i, j], untiled (the strided control) */
+#define LYTH_TRANSPOSE_KERNEL "transpose"
+#define LYTH_TRANSPOSE_MACHINE "sm_100a"
+#define LYTH_TRANSPOSE_BLOCK 256u
+#define LYTH_TRANSPOSE_SHARED_BYTES 0u
+#define LYTH_TRANSPOSE_MAX_GRID 1048576u
+#define LYTH_TRANSPOSE_DERIVED_INTENSITY 0.0
+#define LYTH_TRANSPOSE_FLOPS_PER_ELEMENT 0.0
+#define LYTH_TRANSPOSE_BYTES_PER_ELEMENT 8.0
+#define LYTH_TRANSPOSE_COALESCENCE 0.2222222222222222
+unsigned int lyth_transpose_elements(unsigned int rows, unsigned int cols);
+unsigned int lyth_transpose_grid(unsigned int rows, unsigned int cols);
+/* The kernel writes: b. */
+CUresult lyth_transpose_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_transpose_launch(CUfunction fn, unsigned int rows, unsigned int cols, CUdeviceptr a, CUdeviceptr b);
+CUresult lyth_transpose_launch_with(CUfunction fn, unsigned int grid, unsigned int rows, unsigned int cols, CUdeviceptr a, CUdeviceptr b);
+
+/* ---- transpose_tiled: examples/transpose-tiled.lyth, the same body staged through a
+ * bank-skewed shared tile. The reference's tile is 32x32 with stride 33 (ir.rs:2056-2062,
+ * block 1024, 4224 B); this image keeps the derived rule (stride = the tile width padded to be
+ * coprime with 32 banks) at a 64x64 tile, stride 65, 256 threads, 16640 B. One block per
+ * tile, as the Tiled grid rule says (manifest.rs:176-181). */
+#define LYTH_TRANSPOSE_TILED_KERNEL "transpose_tiled"
+#define LYTH_TRANSPOSE_TILED_MACHINE "sm_100a"
+#define LYTH_TRANSPOSE_TILED_TILE 64u
+#define LYTH_TRANSPOSE_TILED_SKEWED_STRIDE 65u
+#define LYTH_TRANSPOSE_TILED_BLOCK 256u
+#define LYTH_TRANSPOSE_TILED_SHARED_BYTES 16640u
+#define LYTH_TRANSPOSE_TILED_MAX_GRID 2147483647u
+#define LYTH_TRANSPOSE_TILED_DERIVED_INTENSITY 0.0
+#define LYTH_TRANSPOSE_TILED_FLOPS_PER_ELEMENT 0.0
+#define LYTH_TRANSPOSE_TILED_BYTES_PER_ELEMENT 8.0
+#define LYTH_TRANSPOSE_TILED_COALESCENCE 1.0
+unsigned int lyth_transpose_tiled_elements(unsigned int rows, unsigned int cols);
+unsigned int lyth_transpose_tiled_grid(unsigned int rows, unsigned int cols);
+/* The kernel writes: b. */
+CUresult lyth_transpose_tiled_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_transpose_tiled_launch(CUfunction fn, unsigned int rows, unsigned int cols, CUdeviceptr a, CUdeviceptr b);
+CUresult lyth_transpose_tiled_launch_with(CUfunction fn, unsigned int grid, unsigned int rows, unsigned int cols, CUdeviceptr a, CUdeviceptr b);
+
+/* ---- reductions: examples/{sum,dot,max,min}.lyth. One partial per block, bit for bit the
+ * reference's two-stage order (eval.rs:326-345): thread t of block b folds elements
+ * b*256+t, +grid*256, ... in sequence, then the block's 256 slots go through the
+ * stride-halving tree (tree_reduce, eval.rs:537-546). Grid = ceil(n / (256*8)), capped
+ * (manifest.rs:186-192). The caller combines the partials. */
+#define LYTH_SUM_KERNEL "sum"
+#define LYTH_SUM_MACHINE "sm_100a"
+#define LYTH_SUM_BLOCK 256u
+#define LYTH_SUM_SHARED_BYTES 1024u
+#define LYTH_SUM_MAX_GRID 1048576u
+#define LYTH_SUM_DERIVED_INTENSITY 0.25
+#define LYTH_SUM_FLOPS_PER_ELEMENT 1.0
+#define LYTH_SUM_BYTES_PER_ELEMENT 4.0
+#define LYTH_SUM_COALESCENCE 1.0
+unsigned int lyth_sum_elements(unsigned int n);
+unsigned int lyth_sum_grid(unsigned int n);
+/* Elements `partial` must hold: one per block, NOT one per element. */
+unsigned int lyth_sum_partial_len(unsigned int n);
+/* The kernel writes: partial. */
+CUresult lyth_sum_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_sum_launch(CUfunction fn, unsigned int n, CUdeviceptr x, CUdeviceptr partial);
+CUresult lyth_sum_launch_with(CUfunction fn, unsigned int grid, unsigned int n, CUdeviceptr x, CUdeviceptr partial);
+
+#define LYTH_DOT_KERNEL "dot"
+#define LYTH_DOT_MACHINE "sm_100a"
+#define LYTH_DOT_BLOCK 256u
+#define LYTH_DOT_SHARED_BYTES 1024u
+#define LYTH_DOT_MAX_GRID 1048576u
+#define LYTH_DOT_DERIVED_INTENSITY 0.25
+#define LYTH_DOT_FLOPS_PER_ELEMENT 2.0
+#define LYTH_DOT_BYTES_PER_ELEMENT 8.0
+#define LYTH_DOT_COALESCENCE 1.0
+unsigned int lyth_dot_elements(unsigned int n);
+unsigned int lyth_dot_grid(unsigned int n);
+unsigned int lyth_dot_partial_len(unsigned int n);
+/* The kernel writes: partial. */
+CUresult lyth_dot_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_dot_launch(CUfunction fn, unsigned int n, CUdeviceptr x, CUdeviceptr y, CUdeviceptr partial);
+CUresult lyth_dot_launch_with(CUfunction fn, unsigned int grid, unsigned int n, CUdeviceptr x, CUdeviceptr y, CUdeviceptr partial);
+
+#define LYTH_MAX_OF_KERNEL "max_of"
+#define LYTH_MAX_OF_MACHINE "sm_100a"
+#define LYTH_MAX_OF_BLOCK 256u
+#define LYTH_MAX_OF_SHARED_BYTES 1024u
+#define LYTH_MAX_OF_MAX_GRID 1048576u
+#define LYTH_MAX_OF_DERIVED_INTENSITY 0.0
+#define LYTH_MAX_OF_FLOPS_PER_ELEMENT 0.0
+#define LYTH_MAX_OF_BYTES_PER_ELEMENT 4.0
+#define LYTH_MAX_OF_COALESCENCE 1.0
+unsigned int lyth_max_of_elements(unsigned int n);
+unsigned int lyth_max_of_grid(unsigned int n);
+unsigned int lyth_max_of_partial_len(unsigned int n);
+/* The kernel writes: partial. */
+CUresult lyth_max_of_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_max_of_launch(CUfunction fn, unsigned int n, CUdeviceptr x, CUdeviceptr partial);
+CUresult lyth_max_of_launch_with(CUfunction fn, unsigned int grid, unsigned int n, CUdeviceptr x, CUdeviceptr partial);
+
+#define LYTH_MIN_OF_KERNEL "min_of"
+#define LYTH_MIN_OF_MACHINE "sm_100a"
+#define LYTH_MIN_OF_BLOCK 256u
+#define LYTH_MIN_OF_SHARED_BYTES 1024u
+#define LYTH_MIN_OF_MAX_GRID 1048576u
+#define LYTH_MIN_OF_DERIVED_INTENSITY 0.0
+#define LYTH_MIN_OF_FLOPS_PER_ELEMENT 0.0
+#define LYTH_MIN_OF_BYTES_PER_ELEMENT 4.0
+#define LYTH_MIN_OF_COALESCENCE 1.0
+unsigned int lyth_min_of_elements(unsigned int n);
+unsigned int lyth_min_of_grid(unsigned int n);
+unsigned int lyth_min_of_partial_len(unsigned int n);
+/* The kernel writes: partial. */
+CUresult lyth_min_of_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_min_of_launch(CUfunction fn, unsigned int n, CUdeviceptr x, CUdeviceptr partial);
+CUresult lyth_min_of_launch_with(CUfunction fn, unsigned int grid, unsigned int n, CUdeviceptr x, CUdeviceptr partial);
+
+/* ---- matmul: examples/matmul.lyth, C[i, j] = sum_p A[i, p] * B[p, j]. The ADR-0016 entry
+ * keeps the reference's contract bit for bit: p ascending, mul.rn then add.rn, accumulator
+ * from 0.0 (contracted.rs:23-26, eval.rs:459-508). Traffic is an expression in k (the
+ * symbolic cost, bind_c.rs:150-185), here at the 128x128 tile this image stages. */
+#define LYTH_MATMUL_KERNEL "matmul"
+#define LYTH_MATMUL_MACHINE "sm_100a"
+#define LYTH_MATMUL_TILE 128u
+#define LYTH_MATMUL_BLOCK 256u
+#define LYTH_MATMUL_SHARED_BYTES 32768u
+#define LYTH_MATMUL_MAX_GRID 2147483647u
+#define LYTH_MATMUL_COALESCENCE 1.0
+static inline double lyth_matmul_derived_bytes_per_element(unsigned int k)
+{
+    return 0.0625 * (double)k + 4.0;
+}
+static inline double lyth_matmul_derived_flops_per_element(unsigned int k)
+{
+    return 2.0 * (double)k + 0.0;
+}
+static inline double lyth_matmul_derived_intensity(unsigned int k)
+{
+    return lyth_matmul_derived_flops_per_element(k) / lyth_matmul_derived_bytes_per_element(k);
+}
+unsigned int lyth_matmul_elements(unsigned int m, unsigned int n);
+unsigned int lyth_matmul_grid(unsigned int m, unsigned int n);
+/* The kernel writes: c. */
+CUresult lyth_matmul_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_matmul_launch(CUfunction fn, unsigned int m, unsigned int n, unsigned int k, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c);
+CUresult lyth_matmul_launch_with(CUfunction fn, unsigned int grid, unsigned int m, unsigned int n, unsigned int k, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c);
+
+/* ---- state-vector gates. The reference's C generator refuses split kernels
+ * (crates/lyth/src/main.rs:897-905); the Rust binding carries check_splits
+ * (bind_rust.rs:298-360). This ABI gives C the same: `_check_splits` returns LYTH_OK or
+ * LYTH_E_SPLIT, and `_launch` / `_launch_with` refuse (CUDA_ERROR_INVALID_VALUE) before
+ * anything runs. n is the amplitude count; the walk is n/2 pairs (depth 1) or n/4 quads
+ * (depth 2). Output buffers may alias the inputs (an in-place pass). */
+
+/* hadamard_q: examples/hadamard_q.lyth, q0 = s*(p0 + p1), q1 = s*(p0 - p1). */
+#define LYTH_HADAMARD_Q_KERNEL "hadamard_q"
+#define LYTH_HADAMARD_Q_MACHINE "sm_100a"
+#define LYTH_HADAMARD_Q_BLOCK 256u
+#define LYTH_HADAMARD_Q_SHARED_BYTES 0u
+#define LYTH_HADAMARD_Q_MAX_GRID 1048576u
+#define LYTH_HADAMARD_Q_DERIVED_INTENSITY 0.25
+#define LYTH_HADAMARD_Q_FLOPS_PER_ELEMENT 8.0
+#define LYTH_HADAMARD_Q_BYTES_PER_ELEMENT 32.0
+#define LYTH_HADAMARD_Q_COALESCENCE 1.0
+unsigned int lyth_hadamard_q_elements(unsigned int n);
+unsigned int lyth_hadamard_q_grid(unsigned int n);
+int lyth_hadamard_q_check_splits(unsigned int n, unsigned int w);
+/* The kernel writes: qr, qi. */
+CUresult lyth_hadamard_q_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_hadamard_q_launch(CUfunction fn, unsigned int n, unsigned int w, float s, CUdeviceptr re, CUdeviceptr im, CUdeviceptr qr, CUdeviceptr qi);
+CUresult lyth_hadamard_q_launch_with(CUfunction fn, unsigned int grid, unsigned int n, unsigned int w, float s, CUdeviceptr re, CUdeviceptr im, CUdeviceptr qr, CUdeviceptr qi);
+
+/* gate_q: examples/gate_q.lyth, any 1-qubit U = [[a, b], [c, d]] in four fixed fma chains. */
+#define LYTH_GATE_Q_KERNEL "gate_q"
+#define LYTH_GATE_Q_MACHINE "sm_100a"
+#define LYTH_GATE_Q_BLOCK 256u
+#define LYTH_GATE_Q_SHARED_BYTES 0u
+#define LYTH_GATE_Q_MAX_GRID 1048576u
+#define LYTH_GATE_Q_DERIVED_INTENSITY 0.875
+#define LYTH_GATE_Q_FLOPS_PER_ELEMENT 28.0
+#define LYTH_GATE_Q_BYTES_PER_ELEMENT 32.0
+#define LYTH_GATE_Q_COALESCENCE 1.0
+unsigned int lyth_gate_q_elements(unsigned int n);
+unsigned int lyth_gate_q_grid(unsigned int n);
+int lyth_gate_q_check_splits(unsigned int n, unsigned int w);
+/* The kernel writes: qr, qi. */
+CUresult lyth_gate_q_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_gate_q_launch(CUfunction fn, unsigned int n, unsigned int w, float ar, float ai, float br, float bi, float cr, float ci, float dr, float di, CUdeviceptr re, CUdeviceptr im, CUdeviceptr qr, CUdeviceptr qi);
+CUresult lyth_gate_q_launch_with(CUfunction fn, unsigned int grid, unsigned int n, unsigned int w, float ar, float ai, float br, float bi, float cr, float ci, float dr, float di, CUdeviceptr re, CUdeviceptr im, CUdeviceptr qr, CUdeviceptr qi);
+
+/* cu_q: examples/cu_q.lyth, controlled U on (c, t) with widths (wc, wt) as
+ * lyth-circuit widths_ct gives them (lib.rs:387-389); the control=0 half is copied.
+ * cu_q_grouped (examples/cu_q_grouped.lyth) is the same kernel: its only difference in the
+ * reference is the order of the stores, which this image chooses itself. */
+#define LYTH_CU_Q_KERNEL "cu_q"
+#define LYTH_CU_Q_MACHINE "sm_100a"
+#define LYTH_CU_Q_BLOCK 256u
+#define LYTH_CU_Q_SHARED_BYTES 0u
+#define LYTH_CU_Q_MAX_GRID 1048576u
+#define LYTH_CU_Q_DERIVED_INTENSITY 0.4375
+#define LYTH_CU_Q_FLOPS_PER_ELEMENT 28.0
+#define LYTH_CU_Q_BYTES_PER_ELEMENT 64.0
+#define LYTH_CU_Q_COALESCENCE 1.0
+unsigned int lyth_cu_q_elements(unsigned int n);
+unsigned int lyth_cu_q_grid(unsigned int n);
+int lyth_cu_q_check_splits(unsigned int n, unsigned int wc, unsigned int wt);
+/* The kernel writes: qr, qi. */
+CUresult lyth_cu_q_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_cu_q_launch(CUfunction fn, unsigned int n, unsigned int wc, unsigned int wt, float ar, float ai, float br, float bi, float cr, float ci, float dr, float di, CUdeviceptr re, CUdeviceptr im, CUdeviceptr qr, CUdeviceptr qi);
+CUresult lyth_cu_q_launch_with(CUfunction fn, unsigned int grid, unsigned int n, unsigned int wc, unsigned int wt, float ar, float ai, float br, float bi, float cr, float ci, float dr, float di, CUdeviceptr re, CUdeviceptr im, CUdeviceptr qr, CUdeviceptr qi);
+
+/* swap_q: examples/swap_q.lyth, |01> <-> |10>, |00> and |11> copied; no arithmetic. */
+#define LYTH_SWAP_Q_KERNEL "swap_q"
+#define LYTH_SWAP_Q_MACHINE "sm_100a"
+#define LYTH_SWAP_Q_BLOCK 256u
+#define LYTH_SWAP_Q_SHARED_BYTES 0u
+#define LYTH_SWAP_Q_MAX_GRID 1048576u
+#define LYTH_SWAP_Q_DERIVED_INTENSITY 0.0
+#define LYTH_SWAP_Q_FLOPS_PER_ELEMENT 0.0
+#define LYTH_SWAP_Q_BYTES_PER_ELEMENT 64.0
+#define LYTH_SWAP_Q_COALESCENCE 1.0
+unsigned int lyth_swap_q_elements(unsigned int n);
+unsigned int lyth_swap_q_grid(unsigned int n);
+int lyth_swap_q_check_splits(unsigned int n, unsigned int wc, unsigned int wt);
+/* The kernel writes: qr, qi. */
+CUresult lyth_swap_q_load(CUmodule *module, CUfunction *fn);
+CUresult lyth_swap_q_launch(CUfunction fn, unsigned int n, unsigned int wc, unsigned int wt, CUdeviceptr re, CUdeviceptr im, CUdeviceptr qr, CUdeviceptr qi);
+CUresult lyth_swap_q_launch_with(CUfunction fn, unsigned int grid, unsigned int n, unsigned int wc, unsigned int wt, CUdeviceptr re, CUdeviceptr im, CUdeviceptr qr, CUdeviceptr qi);
+
+/* ==================================================================================== */
+/* 2. B200 surface: 64-bit sizes, explicit streams.                                        */
+/* ==================================================================================== */
+
+/* Streams (replaces the launch of lyth run, crates/lyth/src/main.rs:1320-1499, for these
+ * bodies). x/y/z may be any alignment; 16-byte aligned buffers take the 128-bit path. */
+int lyth_b200_saxpy(uint64_t n, float a, const float *x, float *y, cudaStream_t stream);
+int lyth_b200_axpby(uint64_t n, float a, float b, const float *x, float *y, cudaStream_t stream);
+int lyth_b200_lerp(uint64_t n, float t, const float *x, const float *y, float *z, cudaStream_t stream);
+int lyth_b200_horner(uint64_t n, float c0, float c1, float c2, float c3, const float *x, float *y,
+                     cudaStream_t stream);
+
+/* Rank-2 walks of examples/{copy2d,transpose,transpose-tiled}.lyth. a is rows x cols row-major;
+ * b is rows x cols (copy2d) or cols x rows (transposes). */
+int lyth_b200_copy2d(uint32_t rows, uint32_t cols, const float *a, float *b, cudaStream_t stream);
+int lyth_b200_transpose_naive(uint32_t rows, uint32_t cols, const float *a, float *b, cudaStream_t stream);
+int lyth_b200_transpose_tiled(uint32_t rows, uint32_t cols, const float *a, float *b, cudaStream_t stream);
+
+/* Reductions. op: 0 = sum, 1 = max, 2 = min (ast.rs ReduceOp); y != NULL makes it dot (sum
+ * of x*y, mul.rn then add.rn). */
+#define LYTH_REDUCE_SUM 0
+#define LYTH_REDUCE_MAX 1
+#define LYTH_REDUCE_MIN 2
+/* The reference's default grid for a reduction over n: ceil(n / 2048), in [1, 2^20]. */
+uint32_t lyth_b200_reduce_grid(uint64_t n);
+/* One partial per block, bit-exact to the reference's order for this (grid, 256). */
+int lyth_b200_reduce_partials(int op, uint64_t n, const float *x, const float *y, uint32_t grid,
+                              float *partial, cudaStream_t stream);
+/* The whole reduction to one f32 in `out` (device memory): the same per-block partials
+ * (grid = lyth_b200_reduce_grid(n)), combined across each thread-block cluster through
+ * distributed shared memory, then across clusters. `workspace` is caller-owned device
+ * memory of lyth_b200_reduce_workspace_bytes(n) bytes (ADR-0016: LYTH never owns memory). */
+size_t lyth_b200_reduce_workspace_bytes(uint64_t n);
+int lyth_b200_reduce(int op, uint64_t n, const float *x, const float *y, float *out, void *workspace,
+                     size_t workspace_bytes, cudaStream_t stream);
+
+/* Contraction C = A * B, row-major, A m x k, B k x n, C m x n (examples/matmul.lyth).
+ * exact = 1: the reference's order bit for bit (p ascending, mul.rn then add.rn).
+ * exact = 0: FFMA register-tiled (p ascending, fused), within 1e-5 relative of the reference. */
+int lyth_b200_matmul_f32(uint32_t m, uint32_t n, uint32_t k, const float *a, const float *b, float *c,
+                         int exact, cudaStream_t stream);
+/* bf16 inputs (raw bfloat16 bits), f32 accumulate and output, on the tcgen05 tensor cores with
+ * TMEM accumulators. m, n multiples of 128 and k a multiple of 64 take the tensor-core path;
+ * other shapes return LYTH_E_UNSUPPORTED. No reference kernel: the reference never uses tensor
+ * cores. Compared with eval_contraction on the bf16-rounded inputs within 1e-2 relative. */
+int lyth_b200_matmul_bf16(uint32_t m, uint32_t n, uint32_t k, const uint16_t *a, const uint16_t *b,
+                          float *c, cudaStream_t stream);
+
+/* gate_proj GEMV (fixtures/kernel/gate_proj_int4.json, fixtures/poly/gate-proj-int4-nf4.json:
+ * cost contracts only; the reference has no kernel). y[r] = sum_k dequant(W)[r, k] * x[k].
+ * W: rows x k 4-bit, row r contiguous along k, byte (r*k + c)/2, low nibble = even c.
+ * fmt 0 = INT4 (two's-complement nibble, -8..7, w = q * scale, exact in f32);
+ * fmt 1 = NF4 (nibble indexes lyth_b200_nf4_codebook, w = code * scale, one rounding).
+ * scales: fp16 bits [rows][k / group]; x: fp16 bits [k]; y: fp16 bits [rows] (f32 accumulate,
+ * rounded once, RNE). k a multiple of 64; group a multiple of 32 dividing k. */
+#define LYTH_GEMV_INT4 0
+#define LYTH_GEMV_NF4 1
+int lyth_b200_gemv_q4(int fmt, uint32_t rows, uint32_t k, uint32_t group, const uint8_t *w,
+                      const uint16_t *scales, const uint16_t *x, uint16_t *y, cudaStream_t stream);
+/* The dequantised matrix (rows x k f32), through the same unpack the GEMV uses: bit-exact. */
+int lyth_b200_gemv_dequant(int fmt, uint32_t rows, uint32_t k, uint32_t group, const uint8_t *w,
+                           const uint16_t *scales, float *out, cudaStream_t stream);
+/* The 16 NF4 levels (QLoRA's normal-float construction, computed on the host at load). */
+void lyth_b200_nf4_codebook(float out[16]);
+
+/* State-vector gates on the caller's buffers (examples/{hadamard_q,gate_q,cu_q,swap_q}.lyth),
+ * 64-bit: n amplitudes, split re/im f32. m = ar ai br bi cr ci dr di (lyth-circuit f32s,
+ * lib.rs:49-56) as a host array. qr/qi may alias re/im. Power-of-two widths take the fast
+ * kernels; any other width that divides takes the general view_index path. */
+int lyth_b200_hadamard(uint64_t n, uint64_t w, float s, const float *re, const float *im, float *qr,
+                       float *qi, cudaStream_t stream);
+int lyth_b200_gate(uint64_t n, uint64_t w, const float *m, const float *re, const float *im, float *qr,
+                   float *qi, cudaStream_t stream);
+int lyth_b200_cu(uint64_t n, uint64_t wc, uint64_t wt, const float *m, const float *re, const float *im,
+                 float *qr, float *qi, cudaStream_t stream);
+int lyth_b200_swap(uint64_t n, uint64_t wc, uint64_t wt, const float *re, const float *im, float *qr,
+                   float *qi, cudaStream_t stream);
+
+/* ---- the state vector (lyth-circuit, crates/lyth-circuit/src/lib.rs:327-371, re-designed:
+ * in place, a qubit map that makes SWAP a relabel, and sharded over ranks on its high qubits
+ * with pairwise NCCL exchange for gates on those qubits). One handle per rank/GPU. ---------- */
+typedef struct lyth_sv lyth_sv;
+
+/* A gate as lyth-circuit's Gate enum (lib.rs:29-46): kind 0 = U on q0, 1 = CU control q0 /
+ * target q1, 2 = Swap(q0, q1). m = ar ai br bi cr ci dr di (unused for Swap). */
+#define LYTH_GATE_U 0
+#define LYTH_GATE_CU 1
+#define LYTH_GATE_SWAP 2
+typedef struct lyth_gate {
+    uint32_t kind;
+    uint32_t q0;
+    uint32_t q1;
+    float m[8];
+} lyth_gate;
+
+/* Bytes of an NCCL unique id (ncclUniqueId). */
+#define LYTH_SV_ID_BYTES 128
+/* Fill `id` on one rank (usually 0) and hand it to every rank's lyth_sv_create. */
+int lyth_sv_unique_id(unsigned char id[LYTH_SV_ID_BYTES]);
+/* A state of 2^qubits amplitudes over `nranks` ranks (a power of two); this rank's shard of
+ * 2^(qubits - log2 nranks) amplitudes lives on `device`. nranks = 1 needs no id (NULL). */
+int lyth_sv_create(lyth_sv **out, uint32_t qubits, int device, int rank, int nranks,
+                   const unsigned char *id);
+int lyth_sv_destroy(lyth_sv *sv);
+/* This rank's shard length, and the stream every operation of the handle is ordered on. */
+uint64_t lyth_sv_local_len(const lyth_sv *sv);
+cudaStream_t lyth_sv_stream(const lyth_sv *sv);
+/* |index> (lyth-circuit's initial |0...0> is index 0). */
+int lyth_sv_init_basis(lyth_sv *sv, uint64_t index);
+/* re, im ~ U[-1, 1) from SplitMix64 keyed by the global amplitude index (re: stream output 2i,
+ * im: 2i+1), then scaled by 1/sqrt(sum |a|^2) (the sum in f64, applied in f32). */
+int lyth_sv_init_random(lyth_sv *sv, uint64_t seed);
+/* Copy this rank's shard in/out, in logical qubit order (the qubit map is undone first by
+ * real permutation passes). Pointers may be host (pageable or pinned) or device memory. */
+int lyth_sv_set_local(lyth_sv *sv, const float *re, const float *im);
+int lyth_sv_get_local(lyth_sv *sv, float *re, float *im);
+/* Apply `count` gates in order. Returns when the work is queued on lyth_sv_stream. */
+int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count);
+int lyth_sv_sync(lyth_sv *sv);
+/* Counters since creation: data passes run, exchange steps run, bytes sent over NCCL. */
+int lyth_sv_stats(const lyth_sv *sv, uint64_t *passes, uint64_t *exchanges, uint64_t *bytes_sent);
+/* Kernel launches since creation (every pass, exchange chunk and permutation kernel). */
+uint64_t lyth_sv_launches(const lyth_sv *sv);
+/* Per-class device timing: when on, every data pass is bracketed by CUDA events on the stream it
+ * runs on. Classes: 0 = 1-qubit local pass, 1 = 2-qubit local pass, 2 = exchange gate (first
+ * chunk's send to last chunk's compute, on the compute stream). lyth_sv_timing synchronises,
+ * folds the recorded pairs into (count, total ms) per class, and keeps the totals. */
+#define LYTH_SV_T_U 0
+#define LYTH_SV_T_CU 1
+#define LYTH_SV_T_EXCHANGE 2
+int lyth_sv_set_timing(lyth_sv *sv, int on);
+int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms);
+int lyth_sv_reset_timing(lyth_sv *sv);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,208 @@
+// Reductions for sm_100a: examples/{sum,dot,max,min}.lyth.
+//
+// The partials are the reference's, bit for bit (eval.rs:326-345): block b, thread t folds
+// x[b*256 + t], x[b*256 + t + grid*256], ... in that order from the identity, then the 256
+// slots of the block go through the stride-halving tree (tree_reduce, eval.rs:537-546):
+// slots[t] = slots[t] (+) slots[t + s] for s = 128, 64, ..., 1. Here the three widest levels
+// run in shared memory and the last five are warp shuffles: __shfl_down_sync(v, s) hands lane
+// t exactly slots[t + s], so the tree, and every rounding in it, is unchanged.
+//
+// The whole reduction (lyth_b200_reduce) launches the same blocks in clusters of 8: after the
+// partials, each cluster's leader reads its seven neighbours' partials from their shared
+// memory (DSMEM) and folds the eight in block order; a last single-block pass folds the
+// cluster results in cluster order. The combine order is therefore fixed and documented, and
+// the host oracle reproduces it exactly.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace lyth {
+
+constexpr int kRedBlock = 256;
+constexpr int kRedPerThread = 8;  // manifest.rs:186-192: a reduction walks 8 elements per thread
+constexpr int kCluster = 8;
+
+template <int OP>
+LYTH_D float identity_of() {
+    return OP == 1 ? -__int_as_float(0x7f800000) : (OP == 2 ? __int_as_float(0x7f800000) : 0.0f);
+}
+
+// ReduceOp::combine (ast.rs:222-249): sum adds (add.rn); max/min take the positive / negative
+// zero when both operands are zeros, and otherwise the larger / smaller, ignoring one NaN.
+template <int OP>
+LYTH_D float combine(float a, float b) {
+    if (OP == 0) return __fadd_rn(a, b);
+    if (a == 0.0f && b == 0.0f) {
+        const bool aneg = signbit(a);
+        if (OP == 1) return aneg ? b : a;
+        return aneg ? a : b;
+    }
+    return OP == 1 ? fmaxf(a, b) : fminf(a, b);
+}
+
+// One block's partial, in the reference's order. `grid` is the grid of the reference's launch
+// (the stride is grid * 256); blocks at or past it contribute the identity.
+template <int OP, bool DOT>
+LYTH_D float block_partial(uint64_t n, const float *x, const float *y, uint64_t grid, float *slots) {
+    const unsigned t = threadIdx.x;
+    const uint64_t stride = grid * kRedBlock;
+    float acc = identity_of<OP>();
+    if (blockIdx.x < grid) {
+        uint64_t i = (uint64_t)blockIdx.x * kRedBlock + t;
+        // Issue up to eight independent loads, then fold them strictly in order.
+        while (i < n) {
+            float v[kRedPerThread];
+#pragma unroll
+            for (int u = 0; u < kRedPerThread; u++) {
+                const uint64_t j = i + (uint64_t)u * stride;
+                if (j < n) v[u] = DOT ? __fmul_rn(x[j], y[j]) : x[j];
+            }
+#pragma unroll
+            for (int u = 0; u < kRedPerThread; u++) {
+                const uint64_t j = i + (uint64_t)u * stride;
+                if (j < n) acc = combine<OP>(acc, v[u]);
+            }
+            i += (uint64_t)kRedPerThread * stride;
+        }
+    }
+    // The tree. Levels 128, 64, 32 through shared memory ...
+    slots[t] = acc;
+    __syncthreads();
+    if (t < 128) slots[t] = combine<OP>(slots[t], slots[t + 128]);
+    __syncthreads();
+    if (t < 64) slots[t] = combine<OP>(slots[t], slots[t + 64]);
+    __syncthreads();
+    float v = 0.0f;
+    if (t < 32) {
+        v = combine<OP>(slots[t], slots[t + 32]);
+        // ... and 16, 8, 4, 2, 1 in registers.
+#pragma unroll
+        for (int s = 16; s > 0; s >>= 1) v = combine<OP>(v, __shfl_down_sync(0xffffffffu, v, s));
+    }
+    return v;  // valid in thread 0
+}
+
+template <int OP, bool DOT, typename I>
+__global__ void __launch_bounds__(kRedBlock) reduce_partials_kernel(I n, const float *x, const float *y,
+                                                                    float *partial) {
+    __shared__ float slots[kRedBlock];
+    const float v = block_partial<OP, DOT>((uint64_t)n, x, y, gridDim.x, slots);
+    if (threadIdx.x == 0) partial[blockIdx.x] = v;
+}
+
+// The ADR-0016 kernels, in the reference's parameter order.
+template <typename I>
+__global__ void __launch_bounds__(kRedBlock) sum_kernel(I n, const float *x, float *partial) {
+    __shared__ float slots[kRedBlock];
+    const float v = block_partial<0, false>((uint64_t)n, x, nullptr, gridDim.x, slots);
+    if (threadIdx.x == 0) partial[blockIdx.x] = v;
+}
+template <typename I>
+__global__ void __launch_bounds__(kRedBlock) dot_kernel(I n, const float *x, const float *y, float *partial) {
+    __shared__ float slots[kRedBlock];
+    const float v = block_partial<0, true>((uint64_t)n, x, y, gridDim.x, slots);
+    if (threadIdx.x == 0) partial[blockIdx.x] = v;
+}
+template <typename I>
+__global__ void __launch_bounds__(kRedBlock) max_of_kernel(I n, const float *x, float *partial) {
+    __shared__ float slots[kRedBlock];
+    const float v = block_partial<1, false>((uint64_t)n, x, nullptr, gridDim.x, slots);
+    if (threadIdx.x == 0) partial[blockIdx.x] = v;
+}
+template <typename I>
+__global__ void __launch_bounds__(kRedBlock) min_of_kernel(I n, const float *x, float *partial) {
+    __shared__ float slots[kRedBlock];
+    const float v = block_partial<2, false>((uint64_t)n, x, nullptr, gridDim.x, slots);
+    if (threadIdx.x == 0) partial[blockIdx.x] = v;
+}
+
+template __global__ void sum_kernel<uint32_t>(uint32_t, const float *, float *);
+template __global__ void dot_kernel<uint32_t>(uint32_t, const float *, const float *, float *);
+template __global__ void max_of_kernel<uint32_t>(uint32_t, const float *, float *);
+template __global__ void min_of_kernel<uint32_t>(uint32_t, const float *, float *);
+
+// Clusters of 8 blocks: the partial of every block, then the leader folds the cluster's
+// eight partials (blocks 8q .. 8q+7, in order) reading its neighbours' shared memory.
+template <int OP, bool DOT>
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kRedBlock)
+    reduce_cluster_kernel(uint64_t n, const float *x, const float *y, uint64_t grid, float *cluster_out) {
+    __shared__ float slots[kRedBlock];
+    __shared__ float mine;
+    cg::cluster_group cluster = cg::this_cluster();
+    const float v = block_partial<OP, DOT>(n, x, y, grid, slots);
+    if (threadIdx.x == 0) mine = v;
+    cluster.sync();
+    if (cluster.block_rank() == 0 && threadIdx.x == 0) {
+        float acc = mine;
+        for (unsigned r = 1; r < kCluster; r++) {
+            const float *peer = cluster.map_shared_rank(&mine, r);
+            acc = combine<OP>(acc, *peer);
+        }
+        cluster_out[blockIdx.x / kCluster] = acc;
+    }
+    // No block may leave while the leader may still read its shared memory.
+    cluster.sync();
+}
+
+// Fold `count` values in index order, one thread: the last step is tiny (grid / 8 values).
+template <int OP>
+__global__ void fold_kernel(uint64_t count, const float *in, float *out) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        float acc = in[0];
+        for (uint64_t i = 1; i < count; i++) acc = combine<OP>(acc, in[i]);
+        *out = acc;
+    }
+}
+
+template <int OP, bool DOT>
+int reduce_full(uint64_t n, const float *x, const float *y, float *out, float *ws, cudaStream_t s) {
+    const uint64_t grid = lyth_b200_reduce_grid(n);
+    const uint64_t clusters = (grid + kCluster - 1) / kCluster;
+    reduce_cluster_kernel<OP, DOT><<<(unsigned)(clusters * kCluster), kRedBlock, 0, s>>>(n, x, y, grid, ws);
+    int st = last_launch_status();
+    if (st) return st;
+    fold_kernel<OP><<<1, 32, 0, s>>>(clusters, ws, out);
+    return last_launch_status();
+}
+
+}  // namespace lyth
+
+using namespace lyth;
+
+extern "C" uint32_t lyth_b200_reduce_grid(uint64_t n) {
+    uint64_t per = (uint64_t)kRedBlock * kRedPerThread;
+    uint64_t g = (n + per - 1) / per;
+    if (g == 0) g = 1;
+    if (g > (1u << 20)) g = 1u << 20;
+    return (uint32_t)g;
+}
+
+extern "C" int lyth_b200_reduce_partials(int op, uint64_t n, const float *x, const float *y, uint32_t grid,
+                                         float *partial, cudaStream_t s) {
+    if (!x || !partial || grid == 0) return LYTH_E_INVALID;
+    if (op == 0 && y) reduce_partials_kernel<0, true, uint64_t><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
+    else if (op == 0) reduce_partials_kernel<0, false, uint64_t><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
+    else if (op == 1 && !y) reduce_partials_kernel<1, false, uint64_t><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
+    else if (op == 2 && !y) reduce_partials_kernel<2, false, uint64_t><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
+    else return LYTH_E_UNSUPPORTED;
+    return last_launch_status();
+}
+
+extern "C" size_t lyth_b200_reduce_workspace_bytes(uint64_t n) {
+    const uint64_t grid = lyth_b200_reduce_grid(n);
+    return (size_t)((grid + kCluster - 1) / kCluster) * sizeof(float);
+}
+
+extern "C" int lyth_b200_reduce(int op, uint64_t n, const float *x, const float *y, float *out, void *workspace,
+                                size_t workspace_bytes, cudaStream_t s) {
+    if (!x || !out || !workspace) return LYTH_E_INVALID;
+    if (workspace_bytes < lyth_b200_reduce_workspace_bytes(n)) return LYTH_E_INVALID;
+    float *ws = static_cast<float *>(workspace);
+    if (op == 0 && y) return reduce_full<0, true>(n, x, y, out, ws, s);
+    if (op == 0) return reduce_full<0, false>(n, x, nullptr, out, ws, s);
+    if (op == 1 && !y) return reduce_full<1, false>(n, x, nullptr, out, ws, s);
+    if (op == 2 && !y) return reduce_full<2, false>(n, x, nullptr, out, ws, s);
+    return LYTH_E_UNSUPPORTED;
+}

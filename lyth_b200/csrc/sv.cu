@@ -1,0 +1,613 @@
+// The state vector (lyth-circuit, crates/lyth-circuit/src/lib.rs:327-371), re-designed for B200.
+//
+// The reference ping-pongs two full state buffers and launches one pass per gate on one GPU.
+// This engine:
+//  * updates the state in place (one copy of 2^q amplitudes: 33 qubits is 64 GiB, which leaves
+//    room on a 180 GB part), with the same fma chains as the out-of-place kernels, so every
+//    amplitude is bit-identical to the reference's;
+//  * keeps a logical -> physical qubit map, so a SWAP moves no data: it relabels two qubits.
+//    The map is undone by real permutation passes only when the state is read out, which is
+//    exact because a swap is a permutation;
+//  * skips the control=0 half of a CU (it is a copy in the reference: identity in place);
+//  * shards 2^q amplitudes over 2^g ranks on the g highest physical bits: rank r holds global
+//    indices [r * 2^L, (r+1) * 2^L), L = q - g. A gate on a local bit is a local pass. A CU
+//    whose control is a rank bit runs (as a local U) only on the ranks whose bit is 1. A gate
+//    whose target is a rank bit pairs rank r with r ^ (1 << b): each sends its shard to the
+//    other in chunks with NCCL (ncclSend / ncclRecv in a group, on a communication stream)
+//    into a double-buffered receive area, and computes its own row of the gate from (own,
+//    received) as each chunk lands -- receive-then-compute, no remote loads. The chunk's
+//    compute and the next chunk's transfer overlap.
+//
+// NCCL is opened with dlopen on first use by a multi-rank handle, so the library itself loads
+// (and serves every single-GPU entry point) without it.
+#include <dlfcn.h>
+#include <math.h>
+#include <nccl.h>
+#include <string.h>
+
+#include <vector>
+
+#include "gates.cuh"
+
+namespace lyth {
+
+// ------------------------------------------------------------------ NCCL, loaded on demand
+struct NcclApi {
+    bool tried = false, ok = false;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+};
+static NcclApi g_nccl;
+
+static bool load_nccl() {
+    if (g_nccl.tried) return g_nccl.ok;
+    g_nccl.tried = true;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return false;
+#define LYTH_SYM(field, name) g_nccl.field = reinterpret_cast<decltype(g_nccl.field)>(dlsym(h, name))
+    LYTH_SYM(GetUniqueId, "ncclGetUniqueId");
+    LYTH_SYM(CommInitRank, "ncclCommInitRank");
+    LYTH_SYM(CommDestroy, "ncclCommDestroy");
+    LYTH_SYM(CommAbort, "ncclCommAbort");
+    LYTH_SYM(GroupStart, "ncclGroupStart");
+    LYTH_SYM(GroupEnd, "ncclGroupEnd");
+    LYTH_SYM(Send, "ncclSend");
+    LYTH_SYM(Recv, "ncclRecv");
+    LYTH_SYM(AllReduce, "ncclAllReduce");
+#undef LYTH_SYM
+    g_nccl.ok = g_nccl.GetUniqueId && g_nccl.CommInitRank && g_nccl.CommDestroy && g_nccl.GroupStart &&
+                g_nccl.GroupEnd && g_nccl.Send && g_nccl.Recv && g_nccl.AllReduce;
+    return g_nccl.ok;
+}
+
+// ------------------------------------------------------------------ kernels of the engine
+__global__ void set_one_kernel(float *re, float *im, uint64_t i) {
+    re[i] = 1.0f;
+    im[i] = 0.0f;
+}
+
+// re = U(stream 2g), im = U(stream 2g + 1), g the global index; f64 partial of |a|^2 per block.
+__global__ void __launch_bounds__(256) init_random_kernel(uint64_t len, uint64_t base, uint64_t seed, float *re,
+                                                          float *im, double *partial) {
+    __shared__ double sh[256];
+    double acc = 0.0;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < len; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t g = base + i;
+        uint64_t z0 = seed + (2 * g + 1) * 0x9E3779B97F4A7C15ull;
+        uint64_t z1 = seed + (2 * g + 2) * 0x9E3779B97F4A7C15ull;
+        z0 = (z0 ^ (z0 >> 30)) * 0xBF58476D1CE4E5B9ull; z0 = (z0 ^ (z0 >> 27)) * 0x94D049BB133111EBull; z0 ^= z0 >> 31;
+        z1 = (z1 ^ (z1 >> 30)) * 0xBF58476D1CE4E5B9ull; z1 = (z1 ^ (z1 >> 27)) * 0x94D049BB133111EBull; z1 ^= z1 >> 31;
+        const float r = __fsub_rn(__fmul_rn(__fmul_rn((float)(z0 >> 40), 1.0f / 16777216.0f), 2.0f), 1.0f);
+        const float m = __fsub_rn(__fmul_rn(__fmul_rn((float)(z1 >> 40), 1.0f / 16777216.0f), 2.0f), 1.0f);
+        re[i] = r;
+        im[i] = m;
+        acc += (double)r * (double)r + (double)m * (double)m;
+    }
+    sh[threadIdx.x] = acc;
+    __syncthreads();
+    for (int s = 128; s > 0; s >>= 1) {
+        if (threadIdx.x < s) sh[threadIdx.x] += sh[threadIdx.x + s];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) partial[blockIdx.x] = sh[0];
+}
+
+__global__ void sum_partials_kernel(const double *partial, int count, double *out) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        double s = 0.0;
+        for (int i = 0; i < count; i++) s += partial[i];
+        *out = s;
+    }
+}
+
+__global__ void __launch_bounds__(256) scale_kernel(uint64_t len, const double *norm2, float *re, float *im) {
+    const float f = (float)(1.0 / sqrt(*norm2));
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < len; i += (uint64_t)gridDim.x * blockDim.x) {
+        re[i] = __fmul_rn(re[i], f);
+        im[i] = __fmul_rn(im[i], f);
+    }
+}
+
+// Pack / unpack the local indices whose bit `lb` equals `v` (a half of the shard), taking the
+// k-th such index for k in [k0, k0 + count).
+__global__ void __launch_bounds__(256) pack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
+                                                        const float *re, const float *im, float *ore, float *oim) {
+    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t i = insert_bit(k0 + k, lb, v);
+        ore[k] = re[i];
+        oim[k] = im[i];
+    }
+}
+__global__ void __launch_bounds__(256) unpack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
+                                                          float *re, float *im, const float *ire, const float *iim) {
+    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t i = insert_bit(k0 + k, lb, v);
+        re[i] = ire[k];
+        im[i] = iim[k];
+    }
+}
+
+}  // namespace lyth
+
+using namespace lyth;
+
+struct lyth_sv {
+    uint32_t qubits = 0, local_bits = 0, global_bits = 0;
+    int device = 0, rank = 0, nranks = 1;
+    uint64_t local_len = 0, chunk = 0;
+    float *re = nullptr, *im = nullptr;
+    float *rre[2] = {nullptr, nullptr}, *rim[2] = {nullptr, nullptr};
+    double *scratch = nullptr;  // norm partials
+    cudaStream_t stream = nullptr, comm_stream = nullptr;
+    cudaEvent_t ev_recv[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_start = nullptr;
+    ncclComm_t comm = nullptr;
+    std::vector<uint32_t> pos;  // logical qubit -> physical bit
+    std::vector<uint32_t> inv;  // physical bit -> logical qubit
+    uint64_t passes = 0, exchanges = 0, bytes_sent = 0, launches = 0;
+    // Per-class device timing (lyth_sv_set_timing): pending event pairs, folded totals.
+    bool timing = false;
+    struct Mark { int cls; cudaEvent_t a, b; };
+    std::vector<Mark> marks;
+    std::vector<cudaEvent_t> pool;
+    uint64_t t_count[3] = {0, 0, 0};
+    double t_ms[3] = {0, 0, 0};
+};
+
+namespace {
+
+constexpr uint64_t kChunk = 1ull << 24;  // exchange chunk: 16 Mi amplitudes (64 MiB per component)
+constexpr int kInitBlocks = 1184;
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+int nccl_status(ncclResult_t r) { return r == ncclSuccess ? LYTH_OK : LYTH_E_NCCL; }
+
+void reset_map(lyth_sv *sv) {
+    sv->pos.resize(sv->qubits);
+    sv->inv.resize(sv->qubits);
+    for (uint32_t q = 0; q < sv->qubits; q++) sv->pos[q] = sv->inv[q] = q;
+}
+
+cudaEvent_t take_event(lyth_sv *sv) {
+    if (!sv->pool.empty()) {
+        cudaEvent_t e = sv->pool.back();
+        sv->pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Opens a timed region of class `cls` on the compute stream (no-op when timing is off).
+int mark_begin(lyth_sv *sv, int cls) {
+    if (!sv->timing) return -1;
+    sv->marks.push_back({cls, take_event(sv), take_event(sv)});
+    cudaEventRecord(sv->marks.back().a, sv->stream);
+    return (int)sv->marks.size() - 1;
+}
+void mark_end(lyth_sv *sv, int idx) {
+    if (idx >= 0) cudaEventRecord(sv->marks[idx].b, sv->stream);
+}
+
+int fold_timing(lyth_sv *sv) {
+    if (sv->marks.empty()) return LYTH_OK;
+    int st = status_of(cudaStreamSynchronize(sv->stream));
+    if (st) return st;
+    for (auto &mk : sv->marks) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, mk.a, mk.b) == cudaSuccess) {
+            sv->t_count[mk.cls]++;
+            sv->t_ms[mk.cls] += ms;
+        }
+        sv->pool.push_back(mk.a);
+        sv->pool.push_back(mk.b);
+    }
+    sv->marks.clear();
+    return LYTH_OK;
+}
+
+// The rank bit b of this rank.
+inline int rank_bit(const lyth_sv *sv, uint32_t b) { return (sv->rank >> b) & 1; }
+
+// A gate whose target is rank bit b: chunked pairwise exchange, then this rank's row.
+int exchange_gate(lyth_sv *sv, uint32_t b, const U8 &m, int ctrl_bit) {
+    const int partner = sv->rank ^ (1 << b);
+    const int side = rank_bit(sv, b);
+    const int mk = mark_begin(sv, LYTH_SV_T_EXCHANGE);
+    int st = status_of(cudaEventRecord(sv->ev_start, sv->stream));
+    if (st) return st;
+    st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_start, 0));
+    if (st) return st;
+    const uint64_t nchunks = (sv->local_len + sv->chunk - 1) / sv->chunk;
+    for (uint64_t c = 0; c < nchunks; c++) {
+        const int buf = (int)(c & 1);
+        const uint64_t off = c * sv->chunk;
+        const uint64_t len = (sv->local_len - off) < sv->chunk ? (sv->local_len - off) : sv->chunk;
+        if (c >= 2) {
+            st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_done[buf], 0));
+            if (st) return st;
+        }
+        if ((st = nccl_status(g_nccl.GroupStart()))) return st;
+        g_nccl.Send(sv->re + off, len, ncclFloat32, partner, sv->comm, sv->comm_stream);
+        g_nccl.Send(sv->im + off, len, ncclFloat32, partner, sv->comm, sv->comm_stream);
+        g_nccl.Recv(sv->rre[buf], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
+        g_nccl.Recv(sv->rim[buf], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
+        if ((st = nccl_status(g_nccl.GroupEnd()))) return st;
+        if ((st = status_of(cudaEventRecord(sv->ev_recv[buf], sv->comm_stream)))) return st;
+        if ((st = status_of(cudaStreamWaitEvent(sv->stream, sv->ev_recv[buf], 0)))) return st;
+        if ((st = launch_exchange_u(len, off, side, ctrl_bit, m, sv->re + off, sv->im + off, sv->rre[buf],
+                                    sv->rim[buf], sv->stream)))
+            return st;
+        if ((st = status_of(cudaEventRecord(sv->ev_done[buf], sv->stream)))) return st;
+        sv->bytes_sent += 2 * len * sizeof(float);
+        sv->launches++;
+    }
+    mark_end(sv, mk);
+    sv->exchanges++;
+    sv->passes++;
+    return LYTH_OK;
+}
+
+// A local 1-qubit or 2-qubit pass, counted and (when on) timed.
+int local_u(lyth_sv *sv, uint32_t p, const U8 &m) {
+    const int mk = mark_begin(sv, LYTH_SV_T_U);
+    const int st = launch_u(sv->local_len, p, m, sv->re, sv->im, sv->re, sv->im, sv->stream);
+    mark_end(sv, mk);
+    sv->passes++;
+    sv->launches++;
+    return st;
+}
+int local_cu(lyth_sv *sv, uint32_t pc, uint32_t pt, const U8 &m) {
+    const int mk = mark_begin(sv, LYTH_SV_T_CU);
+    const int st = launch_cu(sv->local_len, pc, pt, m, sv->re, sv->im, sv->re, sv->im, sv->stream);
+    mark_end(sv, mk);
+    sv->passes++;
+    sv->launches++;
+    return st;
+}
+
+// Physical swap of local bit lb with rank bit gb: the half of the shard whose bit lb differs
+// from this rank's bit gb goes to the partner, landing at the same index with bit lb flipped;
+// the partner's matching half comes back.
+int physical_swap_local_global(lyth_sv *sv, uint32_t lb, uint32_t gb) {
+    const int partner = sv->rank ^ (1 << gb);
+    const uint64_t g = (uint64_t)rank_bit(sv, gb);
+    const uint64_t send_v = g ^ 1ull;   // local bit value of what leaves
+    const uint64_t recv_v = send_v;     // it is replaced in place by the partner's
+    const uint64_t half = sv->local_len >> 1;
+    int st = LYTH_OK;
+    for (uint64_t k0 = 0; k0 < half; k0 += sv->chunk) {
+        const uint64_t len = (half - k0) < sv->chunk ? (half - k0) : sv->chunk;
+        const unsigned grid = stream_grid(len, 256);
+        // pack into buffer 0, receive into buffer 1
+        pack_half_kernel<<<grid, 256, 0, sv->stream>>>(len, k0, lb, send_v, sv->re, sv->im, sv->rre[0], sv->rim[0]);
+        if ((st = last_launch_status())) return st;
+        if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
+        if ((st = nccl_status(g_nccl.GroupStart()))) return st;
+        g_nccl.Send(sv->rre[0], len, ncclFloat32, partner, sv->comm, sv->stream);
+        g_nccl.Send(sv->rim[0], len, ncclFloat32, partner, sv->comm, sv->stream);
+        g_nccl.Recv(sv->rre[1], len, ncclFloat32, partner, sv->comm, sv->stream);
+        g_nccl.Recv(sv->rim[1], len, ncclFloat32, partner, sv->comm, sv->stream);
+        if ((st = nccl_status(g_nccl.GroupEnd()))) return st;
+        unpack_half_kernel<<<grid, 256, 0, sv->stream>>>(len, k0, lb, recv_v, sv->re, sv->im, sv->rre[1], sv->rim[1]);
+        if ((st = last_launch_status())) return st;
+        sv->bytes_sent += 2 * len * sizeof(float);
+    }
+    sv->exchanges++;
+    return LYTH_OK;
+}
+
+// Physical swap of rank bits b1, b2: ranks whose two bits differ trade whole shards with the
+// rank that has them exchanged.
+int physical_swap_global_global(lyth_sv *sv, uint32_t b1, uint32_t b2) {
+    if (rank_bit(sv, b1) == rank_bit(sv, b2)) return LYTH_OK;
+    const int partner = sv->rank ^ (1 << b1) ^ (1 << b2);
+    int st = LYTH_OK;
+    for (uint64_t off = 0; off < sv->local_len; off += sv->chunk) {
+        const uint64_t len = (sv->local_len - off) < sv->chunk ? (sv->local_len - off) : sv->chunk;
+        if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
+        if ((st = nccl_status(g_nccl.GroupStart()))) return st;
+        g_nccl.Send(sv->re + off, len, ncclFloat32, partner, sv->comm, sv->stream);
+        g_nccl.Send(sv->im + off, len, ncclFloat32, partner, sv->comm, sv->stream);
+        g_nccl.Recv(sv->rre[0], len, ncclFloat32, partner, sv->comm, sv->stream);
+        g_nccl.Recv(sv->rim[0], len, ncclFloat32, partner, sv->comm, sv->stream);
+        if ((st = nccl_status(g_nccl.GroupEnd()))) return st;
+        if ((st = status_of(cudaMemcpyAsync(sv->re + off, sv->rre[0], len * 4, cudaMemcpyDeviceToDevice, sv->stream)))) return st;
+        if ((st = status_of(cudaMemcpyAsync(sv->im + off, sv->rim[0], len * 4, cudaMemcpyDeviceToDevice, sv->stream)))) return st;
+        sv->bytes_sent += 2 * len * sizeof(float);
+    }
+    sv->exchanges++;
+    return LYTH_OK;
+}
+
+// Swap physical bits p1 < p2 with real data motion, and update the map to match.
+int physical_swap(lyth_sv *sv, uint32_t p1, uint32_t p2) {
+    if (p1 == p2) return LYTH_OK;
+    if (p1 > p2) { uint32_t t = p1; p1 = p2; p2 = t; }
+    const uint32_t L = sv->local_bits;
+    int st;
+    if (p2 < L) {
+        st = launch_swap(sv->local_len, p1, p2, sv->re, sv->im, sv->re, sv->im, sv->stream);
+        sv->passes++;
+        sv->launches++;
+    } else if (p1 < L) {
+        st = physical_swap_local_global(sv, p1, p2 - L);
+    } else {
+        st = physical_swap_global_global(sv, p1 - L, p2 - L);
+    }
+    if (st) return st;
+    const uint32_t q1 = sv->inv[p1], q2 = sv->inv[p2];
+    sv->pos[q1] = p2; sv->pos[q2] = p1;
+    sv->inv[p1] = q2; sv->inv[p2] = q1;
+    return LYTH_OK;
+}
+
+// Undo the qubit map with real swaps, so physical bit q holds logical qubit q.
+int normalize(lyth_sv *sv) {
+    for (uint32_t q = 0; q < sv->qubits; q++) {
+        if (sv->pos[q] != q) {
+            int st = physical_swap(sv, q, sv->pos[q]);
+            if (st) return st;
+        }
+    }
+    return LYTH_OK;
+}
+
+int apply_one(lyth_sv *sv, const lyth_gate &g) {
+    const uint32_t L = sv->local_bits;
+    if (g.q0 >= sv->qubits || (g.kind != LYTH_GATE_U && (g.q1 >= sv->qubits || g.q1 == g.q0))) return LYTH_E_INVALID;
+    const U8 m = u8_of(g.m);
+    switch (g.kind) {
+        case LYTH_GATE_SWAP: {
+            const uint32_t pa = sv->pos[g.q0], pb = sv->pos[g.q1];
+            sv->pos[g.q0] = pb; sv->pos[g.q1] = pa;
+            sv->inv[pa] = g.q1; sv->inv[pb] = g.q0;
+            return LYTH_OK;
+        }
+        case LYTH_GATE_U: {
+            const uint32_t p = sv->pos[g.q0];
+            if (p < L) return local_u(sv, p, m);
+            return exchange_gate(sv, p - L, m, -1);
+        }
+        case LYTH_GATE_CU: {
+            const uint32_t pc = sv->pos[g.q0], pt = sv->pos[g.q1];
+            if (pc < L && pt < L) return local_cu(sv, pc, pt, m);
+            if (pc >= L && !rank_bit(sv, pc - L)) return LYTH_OK;  // control 0 on this whole shard
+            if (pt < L) return local_u(sv, pt, m);
+            return exchange_gate(sv, pt - L, m, pc < L ? (int)pc : -1);
+        }
+        default:
+            return LYTH_E_INVALID;
+    }
+}
+
+void free_all(lyth_sv *sv) {
+    if (sv->comm && g_nccl.CommDestroy) g_nccl.CommDestroy(sv->comm);
+    cudaFree(sv->re);
+    cudaFree(sv->im);
+    for (int b = 0; b < 2; b++) {
+        cudaFree(sv->rre[b]);
+        cudaFree(sv->rim[b]);
+        if (sv->ev_recv[b]) cudaEventDestroy(sv->ev_recv[b]);
+        if (sv->ev_done[b]) cudaEventDestroy(sv->ev_done[b]);
+    }
+    cudaFree(sv->scratch);
+    for (auto &mk : sv->marks) { cudaEventDestroy(mk.a); cudaEventDestroy(mk.b); }
+    for (auto e : sv->pool) cudaEventDestroy(e);
+    if (sv->ev_start) cudaEventDestroy(sv->ev_start);
+    if (sv->stream) cudaStreamDestroy(sv->stream);
+    if (sv->comm_stream) cudaStreamDestroy(sv->comm_stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int lyth_sv_unique_id(unsigned char id[LYTH_SV_ID_BYTES]) {
+    if (!id) return LYTH_E_INVALID;
+    if (!load_nccl()) return LYTH_E_NO_NCCL;
+    ncclUniqueId u;
+    int st = nccl_status(g_nccl.GetUniqueId(&u));
+    if (st) return st;
+    memcpy(id, u.internal, LYTH_SV_ID_BYTES);
+    return LYTH_OK;
+}
+
+int lyth_sv_create(lyth_sv **out, uint32_t qubits, int device, int rank, int nranks, const unsigned char *id) {
+    if (!out) return LYTH_E_INVALID;
+    *out = nullptr;
+    if (nranks < 1 || (nranks & (nranks - 1)) || rank < 0 || rank >= nranks) return LYTH_E_INVALID;
+    uint32_t g = 0;
+    while ((1 << g) < nranks) g++;
+    if (qubits < g + 2 || qubits > 40) return LYTH_E_INVALID;
+    if (nranks > 1 && !id) return LYTH_E_INVALID;
+    if (nranks > 1 && !load_nccl()) return LYTH_E_NO_NCCL;
+    DeviceGuard guard(device);
+    lyth_sv *sv = new lyth_sv();
+    sv->qubits = qubits;
+    sv->global_bits = g;
+    sv->local_bits = qubits - g;
+    sv->device = device;
+    sv->rank = rank;
+    sv->nranks = nranks;
+    sv->local_len = 1ull << sv->local_bits;
+    sv->chunk = sv->local_len < kChunk ? sv->local_len : kChunk;
+    reset_map(sv);
+    int st = LYTH_OK;
+    auto fail = [&](int code) {
+        free_all(sv);
+        delete sv;
+        return code;
+    };
+    if (cudaMalloc(&sv->re, sv->local_len * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&sv->im, sv->local_len * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&sv->scratch, (kInitBlocks + 2) * sizeof(double)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(LYTH_E_OOM);
+    }
+    if (nranks > 1) {
+        for (int b = 0; b < 2; b++) {
+            if (cudaMalloc(&sv->rre[b], sv->chunk * sizeof(float)) != cudaSuccess ||
+                cudaMalloc(&sv->rim[b], sv->chunk * sizeof(float)) != cudaSuccess) {
+                cudaGetLastError();
+                return fail(LYTH_E_OOM);
+            }
+        }
+    }
+    if ((st = status_of(cudaStreamCreateWithFlags(&sv->stream, cudaStreamNonBlocking)))) return fail(st);
+    if ((st = status_of(cudaStreamCreateWithFlags(&sv->comm_stream, cudaStreamNonBlocking)))) return fail(st);
+    for (int b = 0; b < 2; b++) {
+        if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_recv[b], cudaEventDisableTiming)))) return fail(st);
+        if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_done[b], cudaEventDisableTiming)))) return fail(st);
+    }
+    if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_start, cudaEventDisableTiming)))) return fail(st);
+    if (nranks > 1) {
+        ncclUniqueId u;
+        memcpy(u.internal, id, LYTH_SV_ID_BYTES);
+        if (g_nccl.CommInitRank(&sv->comm, nranks, u, rank) != ncclSuccess) {
+            sv->comm = nullptr;
+            return fail(LYTH_E_NCCL);
+        }
+    }
+    *out = sv;
+    return LYTH_OK;
+}
+
+int lyth_sv_destroy(lyth_sv *sv) {
+    if (!sv) return LYTH_OK;
+    DeviceGuard guard(sv->device);
+    if (sv->stream) cudaStreamSynchronize(sv->stream);
+    if (sv->comm_stream) cudaStreamSynchronize(sv->comm_stream);
+    free_all(sv);
+    delete sv;
+    return LYTH_OK;
+}
+
+uint64_t lyth_sv_local_len(const lyth_sv *sv) { return sv ? sv->local_len : 0; }
+cudaStream_t lyth_sv_stream(const lyth_sv *sv) { return sv ? sv->stream : nullptr; }
+
+int lyth_sv_init_basis(lyth_sv *sv, uint64_t index) {
+    if (!sv) return LYTH_E_INVALID;
+    if (index >> sv->qubits) return LYTH_E_INVALID;
+    DeviceGuard guard(sv->device);
+    reset_map(sv);
+    int st;
+    if ((st = status_of(cudaMemsetAsync(sv->re, 0, sv->local_len * 4, sv->stream)))) return st;
+    if ((st = status_of(cudaMemsetAsync(sv->im, 0, sv->local_len * 4, sv->stream)))) return st;
+    if ((index >> sv->local_bits) == (uint64_t)sv->rank) {
+        set_one_kernel<<<1, 1, 0, sv->stream>>>(sv->re, sv->im, index & (sv->local_len - 1));
+        return last_launch_status();
+    }
+    return LYTH_OK;
+}
+
+int lyth_sv_init_random(lyth_sv *sv, uint64_t seed) {
+    if (!sv) return LYTH_E_INVALID;
+    DeviceGuard guard(sv->device);
+    reset_map(sv);
+    const uint64_t base = (uint64_t)sv->rank * sv->local_len;
+    init_random_kernel<<<kInitBlocks, 256, 0, sv->stream>>>(sv->local_len, base, seed, sv->re, sv->im, sv->scratch);
+    int st = last_launch_status();
+    if (st) return st;
+    double *norm2 = sv->scratch + kInitBlocks;
+    sum_partials_kernel<<<1, 32, 0, sv->stream>>>(sv->scratch, kInitBlocks, norm2);
+    if ((st = last_launch_status())) return st;
+    if (sv->nranks > 1) {
+        if ((st = nccl_status(g_nccl.AllReduce(norm2, norm2, 1, ncclFloat64, ncclSum, sv->comm, sv->stream)))) return st;
+    }
+    scale_kernel<<<stream_grid(sv->local_len, 256), 256, 0, sv->stream>>>(sv->local_len, norm2, sv->re, sv->im);
+    return last_launch_status();
+}
+
+int lyth_sv_set_local(lyth_sv *sv, const float *re, const float *im) {
+    if (!sv || !re || !im) return LYTH_E_INVALID;
+    DeviceGuard guard(sv->device);
+    reset_map(sv);
+    int st;
+    if ((st = status_of(cudaMemcpyAsync(sv->re, re, sv->local_len * 4, cudaMemcpyDefault, sv->stream)))) return st;
+    if ((st = status_of(cudaMemcpyAsync(sv->im, im, sv->local_len * 4, cudaMemcpyDefault, sv->stream)))) return st;
+    return status_of(cudaStreamSynchronize(sv->stream));
+}
+
+int lyth_sv_get_local(lyth_sv *sv, float *re, float *im) {
+    if (!sv || !re || !im) return LYTH_E_INVALID;
+    DeviceGuard guard(sv->device);
+    int st = normalize(sv);
+    if (st) return st;
+    if ((st = status_of(cudaMemcpyAsync(re, sv->re, sv->local_len * 4, cudaMemcpyDefault, sv->stream)))) return st;
+    if ((st = status_of(cudaMemcpyAsync(im, sv->im, sv->local_len * 4, cudaMemcpyDefault, sv->stream)))) return st;
+    return status_of(cudaStreamSynchronize(sv->stream));
+}
+
+int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count) {
+    if (!sv || (count && !gates)) return LYTH_E_INVALID;
+    DeviceGuard guard(sv->device);
+    for (uint64_t i = 0; i < count; i++) {
+        int st = apply_one(sv, gates[i]);
+        if (st) return st;
+    }
+    return LYTH_OK;
+}
+
+int lyth_sv_sync(lyth_sv *sv) {
+    if (!sv) return LYTH_E_INVALID;
+    DeviceGuard guard(sv->device);
+    int st = status_of(cudaStreamSynchronize(sv->comm_stream));
+    if (st) return st;
+    return status_of(cudaStreamSynchronize(sv->stream));
+}
+
+uint64_t lyth_sv_launches(const lyth_sv *sv) { return sv ? sv->launches : 0; }
+
+int lyth_sv_set_timing(lyth_sv *sv, int on) {
+    if (!sv) return LYTH_E_INVALID;
+    sv->timing = on != 0;
+    return LYTH_OK;
+}
+
+int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms) {
+    if (!sv || cls < 0 || cls > 2) return LYTH_E_INVALID;
+    DeviceGuard guard(sv->device);
+    int st = fold_timing(sv);
+    if (st) return st;
+    if (count) *count = sv->t_count[cls];
+    if (ms) *ms = sv->t_ms[cls];
+    return LYTH_OK;
+}
+
+int lyth_sv_reset_timing(lyth_sv *sv) {
+    if (!sv) return LYTH_E_INVALID;
+    DeviceGuard guard(sv->device);
+    int st = fold_timing(sv);
+    for (int c = 0; c < 3; c++) { sv->t_count[c] = 0; sv->t_ms[c] = 0.0; }
+    return st;
+}
+
+int lyth_sv_stats(const lyth_sv *sv, uint64_t *passes, uint64_t *exchanges, uint64_t *bytes_sent) {
+    if (!sv) return LYTH_E_INVALID;
+    if (passes) *passes = sv->passes;
+    if (exchanges) *exchanges = sv->exchanges;
+    if (bytes_sent) *bytes_sent = sv->bytes_sent;
+    return LYTH_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,128 @@
+"""The sharded state vector (lyth_sv_* in include/lyth_b200.h), from Python.
+
+Mirrors lyth-circuit's ``execute`` (crates/lyth-circuit/src/lib.rs:327-371) one rank at a time:
+a handle owns this rank's shard of 2^qubits complex64 amplitudes (split re/im), applies a gate
+list in order on its own stream, and reads the shard back in logical qubit order.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import GATE_CU, GATE_SWAP, GATE_U, Gate, check, lib
+from .circuit import CU, Swap, U, f32s
+
+
+def unique_id() -> bytes:
+    """An NCCL unique id for a multi-rank state vector (call on one rank, share with all)."""
+    buf = C.create_string_buffer(128)
+    check(lib.lyth_sv_unique_id(buf), "lyth_sv_unique_id")
+    return buf.raw
+
+
+def gates_array(gates) -> "C.Array[Gate]":
+    """lyth-circuit Gate values -> a ``lyth_gate`` array (matrices rounded to f32 once, f32s)."""
+    arr = (Gate * max(len(gates), 1))()
+    for i, g in enumerate(gates):
+        if isinstance(g, U):
+            arr[i].kind, arr[i].q0, arr[i].q1 = GATE_U, g.q, 0
+            arr[i].m[:] = f32s(g.m)
+        elif isinstance(g, CU):
+            arr[i].kind, arr[i].q0, arr[i].q1 = GATE_CU, g.c, g.t
+            arr[i].m[:] = f32s(g.m)
+        elif isinstance(g, Swap):
+            arr[i].kind, arr[i].q0, arr[i].q1 = GATE_SWAP, g.a, g.b
+        else:
+            raise TypeError(f"not a gate: {g!r}")
+    return arr
+
+
+class StateVector:
+    """One rank's shard. ``nranks`` must be a power of two; ``nccl_id`` is required when > 1."""
+
+    def __init__(self, qubits: int, device: int = 0, rank: int = 0, nranks: int = 1, nccl_id: bytes | None = None):
+        h = C.c_void_p()
+        check(lib.lyth_sv_create(C.byref(h), qubits, device, rank, nranks, nccl_id), "lyth_sv_create")
+        self._h = h
+        self.qubits, self.device, self.rank, self.nranks = qubits, device, rank, nranks
+        self.local_len = int(lib.lyth_sv_local_len(h))
+
+    def close(self) -> None:
+        if self._h:
+            check(lib.lyth_sv_destroy(self._h), "lyth_sv_destroy")
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        """The cudaStream_t every operation of this handle is ordered on."""
+        return int(lib.lyth_sv_stream(self._h) or 0)
+
+    def init_basis(self, index: int = 0) -> None:
+        check(lib.lyth_sv_init_basis(self._h, index), "init_basis")
+
+    def init_random(self, seed: int) -> None:
+        check(lib.lyth_sv_init_random(self._h, seed), "init_random")
+
+    def set_local(self, re, im) -> None:
+        """re/im: this rank's shard, as torch tensors (CPU or CUDA) or raw pointers."""
+        check(lib.lyth_sv_set_local(self._h, _addr(re), _addr(im)), "set_local")
+
+    def get_local(self, re, im) -> None:
+        check(lib.lyth_sv_get_local(self._h, _addr(re), _addr(im)), "get_local")
+
+    def apply(self, gates) -> None:
+        arr = gates if isinstance(gates, C.Array) else gates_array(gates)
+        count = len(gates)
+        check(lib.lyth_sv_apply(self._h, arr, count), "apply")
+
+    def sync(self) -> None:
+        check(lib.lyth_sv_sync(self._h), "sync")
+
+    def stats(self) -> dict:
+        p, e, b = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        check(lib.lyth_sv_stats(self._h, C.byref(p), C.byref(e), C.byref(b)), "stats")
+        return {"passes": p.value, "exchanges": e.value, "bytes_sent": b.value,
+                "launches": int(lib.lyth_sv_launches(self._h))}
+
+    def set_timing(self, on: bool) -> None:
+        check(lib.lyth_sv_set_timing(self._h, int(on)), "set_timing")
+
+    def timing(self) -> dict:
+        """{class: (count, total ms)} for 'u' (1-qubit passes), 'cu' (2-qubit), 'exchange'."""
+        out = {}
+        for cls, name in enumerate(("u", "cu", "exchange")):
+            n, ms = C.c_uint64(), C.c_double()
+            check(lib.lyth_sv_timing(self._h, cls, C.byref(n), C.byref(ms)), "timing")
+            out[name] = (n.value, ms.value)
+        return out
+
+    def reset_timing(self) -> None:
+        check(lib.lyth_sv_reset_timing(self._h), "reset_timing")
+
+
+def _addr(t) -> int:
+    if isinstance(t, int):
+        return t
+    try:
+        import numpy as np
+
+        if isinstance(t, np.ndarray):
+            if t.dtype != np.float32 or not t.flags["C_CONTIGUOUS"]:
+                raise TypeError("expected a contiguous float32 array")
+            return t.ctypes.data
+    except ImportError:
+        pass
+    if not t.is_contiguous():
+        raise ValueError("buffer must be contiguous")
+    return t.data_ptr()

@@ -1,0 +1,95 @@
+"""The state-vector engine (one GPU): whole circuits from seeded states, bit for bit against
+the evaluator applying the same gates unfused (lyth-circuit's execute / run_fused_host)."""
+import numpy as np
+import pytest
+
+import lyth_b200 as lb
+from lyth_b200 import circuit as cc
+from oracle import oracle as orc
+from tests.conftest import bits
+
+pytestmark = pytest.mark.gpu
+
+
+def as_tuples(gates):
+    out = []
+    for g in gates:
+        if isinstance(g, cc.U):
+            out.append((0, g.q, 0, cc.f32s(g.m)))
+        elif isinstance(g, cc.CU):
+            out.append((1, g.c, g.t, cc.f32s(g.m)))
+        else:
+            out.append((2, g.a, g.b, [0.0] * 8))
+    return out
+
+
+def run_engine(q, gates, re0, im0):
+    with lb.StateVector(q, device=0) as sv:
+        sv.set_local(re0, im0)
+        sv.apply(gates)
+        sv.sync()
+        gr, gi = np.empty_like(re0), np.empty_like(im0)
+        sv.get_local(gr, gi)
+        return gr, gi, sv.stats()
+
+
+def suite():
+    rng = cc.Rng(20_260_930)
+    return [
+        ("GHZ(12)", 12, cc.ghz(12)),
+        ("QFT(10)", 10, cc.qft(10, rng)),
+        ("random(10, depth 20)", 10, cc.random(10, 20, rng)),
+        ("random(20, depth 10)", 20, cc.random(20, 10, cc.Rng(20_260_931))),
+        ("layered(16, 4)", 16, cc.layered(16, 4, cc.Rng(cc.BENCH_SEED))),
+        ("layered(22, 2)", 22, cc.layered(22, 2, cc.Rng(cc.BENCH_SEED))),
+    ]
+
+
+@pytest.mark.parametrize("case", range(6))
+def test_circuits_bit_exact(cuda, case):
+    name, q, gates = suite()[case]
+    re0, im0 = orc.random_state(100 + case, q)
+    wr, wi = orc.run_gates(as_tuples(gates), re0, im0)
+    gr, gi, st = run_engine(q, gates, re0, im0)
+    assert np.array_equal(bits(gr), bits(wr)), name
+    assert np.array_equal(bits(gi), bits(wi)), name
+    swaps = sum(isinstance(g, cc.Swap) for g in gates)
+    assert st["passes"] >= len(gates) - swaps - 0  # swaps are relabels, the rest one pass each
+
+
+def test_from_basis_zero_like_lyth_circuit(cuda):
+    q = 12
+    gates = cc.ghz(q)
+    with lb.StateVector(q, device=0) as sv:
+        sv.init_basis(0)
+        sv.apply(gates)
+        gr, gi = np.empty(1 << q, np.float32), np.empty(1 << q, np.float32)
+        sv.get_local(gr, gi)
+    re0 = np.zeros(1 << q, np.float32)
+    re0[0] = 1.0
+    wr, wi = orc.run_gates(as_tuples(gates), re0, np.zeros_like(re0))
+    assert np.array_equal(bits(gr), bits(wr)) and np.array_equal(bits(gi), bits(wi))
+    assert gr[0] == gr[-1] == np.float32(cc.S)
+
+
+def test_init_random_matches_the_definition(cuda):
+    q = 18
+    with lb.StateVector(q, device=0) as sv:
+        sv.init_random(77)
+        gr, gi = np.empty(1 << q, np.float32), np.empty(1 << q, np.float32)
+        sv.get_local(gr, gi)
+    wr, wi = orc.random_state(77, q)
+    assert np.array_equal(bits(gr), bits(wr)) and np.array_equal(bits(gi), bits(wi))
+    norm = float(np.sum(gr.astype(np.float64) ** 2 + gi.astype(np.float64) ** 2))
+    assert abs(norm - 1.0) < 1e-5
+
+
+def test_unitarity_physics_check(cuda):
+    # The check bit-exactness cannot see (unitary_gate.rs): U then U-dagger returns the state.
+    q = 14
+    m = cc.zyz(0.4, -1.1, 2.0)
+    mdag = ((m[0][0], -m[0][1]), (m[2][0], -m[2][1]), (m[1][0], -m[1][1]), (m[3][0], -m[3][1]))
+    gates = [cc.U(3, m), cc.CU(5, 9, m), cc.CU(5, 9, mdag), cc.U(3, mdag)]
+    re0, im0 = orc.random_state(5, q)
+    gr, gi, _ = run_engine(q, gates, re0, im0)
+    assert np.max(np.abs(gr - re0)) < 1e-6 and np.max(np.abs(gi - im0)) < 1e-6

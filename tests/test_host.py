@@ -1,0 +1,139 @@
+"""Host-side tests without a GPU: the C-ABI library loads and exports every symbol the header
+declares, the launch arithmetic of the ADR-0016 surface (manifest.rs figures), refusals that
+happen before any device work, and the circuit host logic (fuse, generators)."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+import lyth_b200 as lb
+from lyth_b200 import circuit as cc
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "lyth_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = set(re.findall(r"\b(lyth_\w+)\s*\(", text))
+    inline = set(re.findall(r"static inline [\w\s\*]+?\b(lyth_\w+)\s*\(", text))
+    return sorted(names - inline)
+
+
+def test_library_exports_every_declared_symbol():
+    names = declared_functions()
+    assert len(names) > 100
+    missing = [n for n in names if not hasattr(lb.lib, n)]
+    assert not missing, f"declared in include/lyth_b200.h but not exported: {missing}"
+
+
+def test_every_adr16_kernel_has_the_full_family():
+    kernels = ["saxpy", "axpby", "lerp", "horner", "copy2d", "transpose", "transpose_tiled", "sum", "dot",
+               "max_of", "min_of", "matmul", "hadamard_q", "gate_q", "cu_q", "swap_q"]
+    for k in kernels:
+        for suffix in ["elements", "grid", "load", "launch", "launch_with"]:
+            assert hasattr(lb.lib, f"lyth_{k}_{suffix}"), f"lyth_{k}_{suffix}"
+
+
+def test_manifest_launch_figures():
+    # manifest.rs:617-857: one element per thread -> 262144 blocks at 2^26; a reduction walks 8
+    # per thread -> 32768; a tile gets one block.
+    assert lb.lib.lyth_saxpy_grid(1 << 26) == 262144
+    assert lb.lib.lyth_sum_grid(1 << 26) == 32768
+    assert lb.lib.lyth_sum_partial_len(1 << 26) == 32768
+    assert lb.lib.lyth_saxpy_grid(0) == 0
+    assert lb.lib.lyth_saxpy_grid(1 << 31) == 1 << 20  # capped at MAX_GRID
+    assert lb.lib.lyth_transpose_tiled_grid(4096, 4096) == 64 * 64
+    assert lb.lib.lyth_transpose_tiled_grid(4097, 33) == 65 * 1
+    assert lb.lib.lyth_copy2d_elements(1 << 16, 1 << 16) == 0  # overflows a 32-bit index
+    assert lb.lib.lyth_gate_q_grid(1 << 22) == (1 << 21) // 256
+    assert lb.lib.lyth_cu_q_grid(1 << 22) == (1 << 20) // 256
+    assert lb.reduce_grid(1 << 26) == 32768 and lb.reduce_grid(1) == 1
+
+
+def test_split_checks_refuse_before_any_device_work():
+    assert lb.lib.lyth_gate_q_check_splits(12, 0) == lb.E_SPLIT
+    assert lb.lib.lyth_gate_q_check_splits(12, 4) == lb.E_SPLIT
+    assert lb.lib.lyth_gate_q_check_splits(96, 3) == lb.OK
+    assert lb.lib.lyth_cu_q_check_splits(64, 4, 2) == lb.OK
+    assert lb.lib.lyth_cu_q_check_splits(64, 16, 32) == lb.E_SPLIT
+    m = (C.c_float * 8)()
+    assert lb.lib.lyth_b200_gate(12, 4, m, 1, 1, 1, 1, None) == lb.E_SPLIT
+    assert lb.lib.lyth_b200_cu(64, 16, 32, m, 1, 1, 1, 1, None) == lb.E_SPLIT
+    with pytest.raises(lb.LythError) as e:
+        lb.check(lb.E_SPLIT, "gate_q")
+    assert "2*width" in str(e.value)
+
+
+def test_error_strings_cover_every_code():
+    for code in range(-7, 1):
+        assert lb.lib.lyth_b200_error_string(code)
+    assert b"unknown" in lb.lib.lyth_b200_error_string(-99)
+
+
+def test_gemv_shape_refusals_are_host_side():
+    assert lb.lib.lyth_b200_gemv_q4(0, 8, 100, 64, 16, 16, 16, 16, None) == lb.E_UNSUPPORTED
+    assert lb.lib.lyth_b200_gemv_q4(0, 8, 4096, 48, 16, 16, 16, 16, None) == lb.E_UNSUPPORTED
+    assert lb.lib.lyth_b200_gemv_q4(7, 8, 4096, 64, 16, 16, 16, 16, None) == lb.E_UNSUPPORTED
+
+
+def test_nf4_codebook_matches_the_oracle():
+    from oracle import oracle as orc
+
+    assert lb.nf4_codebook() == orc.nf4_codebook().tolist()
+
+
+# ------------------------------------------------------------------ lyth-circuit host logic
+def suite():
+    rng = cc.Rng(20_260_930)
+    return [
+        ("GHZ(12)", 12, cc.ghz(12)),
+        ("QFT(10)", 10, cc.qft(10, rng)),
+        ("random(10, depth 20)", 10, cc.random(10, 20, rng)),
+        ("random(20, depth 10)", 20, cc.random(20, 10, cc.Rng(20_260_931))),
+    ]
+
+
+def test_fuser_keeps_every_gate_in_order_and_respects_k():
+    for name, _, gates in suite():
+        for k in range(1, 6):
+            groups = cc.fuse(gates, k)
+            flat = [g for grp in groups for g in grp.gates]
+            assert flat == gates, name
+            for grp in groups:
+                need = max(len(g.qubits()) for g in grp.gates)
+                assert len(grp.qubits) <= max(k, need)
+                assert all(a > b for a, b in zip(grp.qubits, grp.qubits[1:]))
+
+
+def test_layered_circuit_gate_counts():
+    for q, per in [(30, 74), (33, 81)]:
+        g = cc.layered(q, 20, cc.Rng(cc.BENCH_SEED))
+        assert len(g) == 20 * per
+        assert sum(isinstance(x, cc.Swap) for x in g) == 20 * (q // 2)
+
+
+def test_f32s_rounds_once():
+    m = cc.f32s(cc.H)
+    assert m[0] == float(__import__("numpy").float32(1 / 2 ** 0.5))
+    assert m[6] == -m[0] and m[1] == 0.0
+
+
+def test_gate_array_packs_kind_and_qubits():
+    from lyth_b200.statevector import gates_array
+
+    arr = gates_array([cc.U(3, cc.H), cc.CU(1, 2, cc.X), cc.Swap(0, 5)])
+    assert (arr[0].kind, arr[0].q0) == (lb.GATE_U, 3)
+    assert (arr[1].kind, arr[1].q0, arr[1].q1) == (lb.GATE_CU, 1, 2)
+    assert (arr[2].kind, arr[2].q0, arr[2].q1) == (lb.GATE_SWAP, 0, 5)
+    assert list(arr[1].m) == cc.f32s(cc.X)
+
+
+def test_sv_create_refuses_bad_arguments_without_a_device():
+    h = C.c_void_p()
+    assert lb.lib.lyth_sv_create(C.byref(h), 10, 0, 0, 3, None) == lb.E_INVALID  # not a power of 2
+    assert lb.lib.lyth_sv_create(C.byref(h), 10, 0, 2, 2, None) == lb.E_INVALID  # rank out of range
+    assert lb.lib.lyth_sv_create(C.byref(h), 10, 0, 0, 2, None) == lb.E_INVALID  # no id
+    assert lb.lib.lyth_sv_create(C.byref(h), 2, 0, 0, 4, b"x" * 128) == lb.E_INVALID  # too few qubits
