@@ -64,6 +64,9 @@ def args_():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-qubits", type=int, default=25)
+    ap.add_argument("--case", default=None, help="run one kernel case (small config) and exit")
+    ap.add_argument("--case-reps", type=int, default=3)
+    ap.add_argument("--list-cases", action="store_true")
     return ap.parse_args()
 
 
@@ -254,102 +257,159 @@ def reference_arm(a, dist: Dist) -> None:
 
 
 # --------------------------------------------------------------------------- per-kernel table
-def per_kernel(pk: dict) -> dict:
-    """HBM GB/s of each kernel class at its BASELINE config, CUDA events on the current stream,
-    L2 flushed (a 256 MiB write) before every timed launch, median of the reps."""
-    import numpy as np
+def kernel_cases(dev, small: bool = False):
+    """Named cases, each (setup -> (callable, algorithmic bytes or flops, kind)). The BASELINE
+    configs; `small` shrinks the large ones for an ncu capture (inputs still larger than L2)."""
     import torch
 
     import lyth_b200 as lb
 
-    dev = torch.device("cuda")
-    hbm = pk["hbm_gbs"]
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    out = {}
-
-    def timeit(fn, reps=10, warm=3):
-        for _ in range(warm):
-            fn()
-        ts = []
-        for _ in range(reps):
-            flush.fill_(1.0)
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            fn()
-            e.record()
-            e.synchronize()
-            ts.append(s.elapsed_time(e))
-        return statistics.median(ts)
-
-    def row(name, byts, ms, extra=None):
-        gbs = byts / (ms * 1e-3) / 1e9
-        r = {"GB_s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4), "ms": round(ms, 5), "bytes": int(byts)}
-        if extra:
-            r.update(extra)
-        out[name] = r
-
     g = torch.Generator(device=dev)
     g.manual_seed(1)
-    # saxpy sweep 2^20 .. 2^30 (12 B/elem)
+    cases = {}
+
+    def stream_case(name, p, body, nbytes_per):
+        def setup():
+            n = 1 << p
+            x = torch.rand(n, device=dev, generator=g)
+            y = torch.rand(n, device=dev, generator=g)
+            z = torch.empty_like(x)
+            return (lambda: body(x, y, z)), nbytes_per * n, "bytes"
+        cases[name] = setup
+
     for p in (20, 22, 24, 26, 28, 30):
-        n = 1 << p
-        x = torch.rand(n, device=dev, generator=g)
-        y = torch.rand(n, device=dev, generator=g)
-        row(f"saxpy_2^{p}", 12.0 * n, timeit(lambda: lb.saxpy(2.5, x, y)))
-        del x, y
-    n = 1 << 28
-    x = torch.rand(n, device=dev, generator=g)
-    y = torch.rand(n, device=dev, generator=g)
-    z = torch.empty_like(x)
-    row("axpby_2^28", 12.0 * n, timeit(lambda: lb.axpby(1.5, 0.5, x, y)))
-    row("lerp_2^28", 12.0 * n, timeit(lambda: lb.lerp(0.3, x, y, z)))
-    row("horner_2^28", 8.0 * n, timeit(lambda: lb.horner(0.1, 0.2, 0.3, 0.4, x, z)))
-    row("sum_2^28", 4.0 * n, timeit(lambda: lb.reduce_partials(lb.SUM, x)))
-    row("max_2^28", 4.0 * n, timeit(lambda: lb.reduce_partials(lb.MAX, x)))
-    row("dot_2^28", 8.0 * n, timeit(lambda: lb.reduce_partials(lb.SUM, x, y)))
-    del x, y, z
-    # transposes 4096^2 (8 B/elem payload)
-    a = torch.rand(4096, 4096, device=dev, generator=g)
-    b = torch.empty(4096, 4096, device=dev)
-    nn = 4096 * 4096
-    row("transpose_tiled_4096", 8.0 * nn, timeit(lambda: lb.transpose_tiled(a, b)))
-    row("copy2d_4096", 8.0 * nn, timeit(lambda: lb.copy2d(a, b)))
-    row("transpose_naive_4096", 8.0 * nn, timeit(lambda: lb.transpose_naive(a, b)))
-    del a, b
-    # gate_proj GEMV, 4096 -> 14336, group 64
-    rows, k, grp = 14336, 4096, 64
-    w = torch.randint(0, 256, (rows, k // 2), dtype=torch.uint8, device=dev, generator=g)
-    sc = (torch.rand(rows * (k // grp), device=dev, generator=g) * 0.02).half()
-    xv = torch.randn(k, device=dev, generator=g).half()
-    yv = torch.empty(rows, dtype=torch.float16, device=dev)
-    gbytes = rows * k / 2 + rows * (k // grp) * 2 + k * 2 + rows * 2
-    row("gemv_int4_4096x14336", gbytes, timeit(lambda: lb.gemv_q4(lb.GEMV_INT4, w, sc, xv, yv, grp), reps=20))
-    row("gemv_nf4_4096x14336", gbytes, timeit(lambda: lb.gemv_q4(lb.GEMV_NF4, w, sc, xv, yv, grp), reps=20))
-    del w, sc, xv, yv
-    # f32 contraction 4096^3 (FP32 pipe: TFLOP/s against the nominal FFMA rate at the max clock)
-    m = 4096
-    A = torch.randn(m, m, device=dev, generator=g) / 64.0
-    B = torch.randn(m, m, device=dev, generator=g) / 64.0
-    Cm = torch.empty(m, m, device=dev)
+        if not small or p == 26:
+            stream_case(f"saxpy_2^{p}", p, lambda x, y, z: lb.saxpy(2.5, x, y), 12.0)
+    P = 26 if small else 28
+    stream_case(f"axpby_2^{P}", P, lambda x, y, z: lb.axpby(1.5, 0.5, x, y), 12.0)
+    stream_case(f"lerp_2^{P}", P, lambda x, y, z: lb.lerp(0.3, x, y, z), 12.0)
+    stream_case(f"horner_2^{P}", P, lambda x, y, z: lb.horner(0.1, 0.2, 0.3, 0.4, x, z), 8.0)
+    stream_case(f"sum_2^{P}", P, lambda x, y, z: lb.reduce_partials(lb.SUM, x), 4.0)
+    stream_case(f"max_2^{P}", P, lambda x, y, z: lb.reduce_partials(lb.MAX, x), 4.0)
+    stream_case(f"dot_2^{P}", P, lambda x, y, z: lb.reduce_partials(lb.SUM, x, y), 8.0)
+
+    def transpose_case(name, fn):
+        def setup():
+            a = torch.rand(4096, 4096, device=dev, generator=g)
+            b = torch.empty(4096, 4096, device=dev)
+            return (lambda: fn(a, b)), 8.0 * 4096 * 4096, "bytes"
+        cases[name] = setup
+
+    transpose_case("transpose_tiled_4096", lb.transpose_tiled)
+    transpose_case("copy2d_4096", lb.copy2d)
+    transpose_case("transpose_naive_4096", lb.transpose_naive)
+
+    def gemv_case(name, fmt):
+        def setup():
+            rows, k, grp = 14336, 4096, 64
+            w = torch.randint(0, 256, (rows, k // 2), dtype=torch.uint8, device=dev, generator=g)
+            sc = (torch.rand(rows * (k // grp), device=dev, generator=g) * 0.02).half()
+            xv = torch.randn(k, device=dev, generator=g).half()
+            yv = torch.empty(rows, dtype=torch.float16, device=dev)
+            nbytes = rows * k / 2 + rows * (k // grp) * 2 + k * 2 + rows * 2
+            return (lambda: lb.gemv_q4(fmt, w, sc, xv, yv, grp)), nbytes, "bytes"
+        cases[name] = setup
+
+    gemv_case("gemv_int4_4096x14336", lb.GEMV_INT4)
+    gemv_case("gemv_nf4_4096x14336", lb.GEMV_NF4)
+
+    def mm_case(name, fn, m):
+        def setup():
+            A = torch.randn(m, m, device=dev, generator=g) / 64.0
+            B = torch.randn(m, m, device=dev, generator=g) / 64.0
+            C = torch.empty(m, m, device=dev)
+            return (lambda: fn(A, B, C)), 2.0 * m ** 3, "flops"
+        cases[name] = setup
+
+    M = 2048 if small else 4096
+    mm_case(f"matmul_f32_ffma_{M}", lambda A, B, C: lb.matmul_f32(A, B, C, exact=False), M)
+    mm_case(f"matmul_f32_exact_{M}", lambda A, B, C: lb.matmul_f32(A, B, C, exact=True), M)
+    mm_case(f"matmul_bf16_{M}", lambda A, B, C: lb.matmul_bf16(A.bfloat16(), B.bfloat16(), C), M)
+
+    def gate_case(name, q, fn):
+        def setup():
+            n = 1 << q
+            re = torch.rand(n, device=dev, generator=g)
+            im = torch.rand(n, device=dev, generator=g)
+            return (lambda: fn(n, re, im)), 16.0 * n if "cu" not in name else 8.0 * n, "bytes"
+        cases[name] = setup
+
+    from lyth_b200 import circuit as cc
+
+    Q = 28 if small else 30
+    H8 = cc.f32s(cc.H)
+    gate_case(f"gate_q_q10_2^{Q}", Q, lambda n, re, im: lb.gate(1 << 10, H8, re, im))
+    gate_case(f"gate_q_q0_2^{Q}", Q, lambda n, re, im: lb.gate(1, H8, re, im))
+    wc, wt = cc.widths_ct(12, 13)
+    gate_case(f"cu_q_inplace_12_13_2^{Q}", Q, lambda n, re, im: lb.cu(wc, wt, cc.f32s(cc.phase(0.3)), re, im))
+    return cases
+
+
+def per_kernel(pk: dict, only: str | None = None, small: bool = False, reps: int = 10) -> dict:
+    """HBM GB/s (or TFLOP/s) of each kernel class at its BASELINE config: CUDA events on the
+    current stream, L2 flushed before every timed launch by READING a 256 MiB buffer (a read
+    leaves clean lines, so no write-back lands inside the timed window), median of the reps."""
+    import torch
+
+    dev = torch.device("cuda")
+    hbm = pk["hbm_gbs"]
+    flush = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    sink = torch.empty(1, device=dev)
     ffma_peak = 148 * 128 * 2 * pk.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
-    for exact in (False, True):
-        ms = timeit(lambda: lb.matmul_f32(A, B, Cm, exact=exact), reps=5, warm=2)
-        tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
-        out["matmul_f32_4096" + ("_exact" if exact else "_ffma")] = {
-            "TFLOP_s": round(tf, 2), "frac_fp32_nominal": round(tf / ffma_peak, 4), "ms": round(ms, 4),
-            "fp32_nominal_tflops": round(ffma_peak, 1)}
-    try:
-        Ab, Bb = A.bfloat16(), B.bfloat16()
-        ms = timeit(lambda: lb.matmul_bf16(Ab, Bb, Cm), reps=10, warm=3)
-        tf = 2.0 * m ** 3 / (ms * 1e-3) / 1e12
-        out["matmul_bf16_4096"] = {"TFLOP_s": round(tf, 1), "frac_bf16_measured": round(tf / pk["bf16_tflops"], 4),
-                                   "ms": round(ms, 4)}
-    except Exception as e:  # the tensor-core path refuses shapes it does not take
-        out["matmul_bf16_4096"] = {"unavailable": str(e)[:120]}
-    del A, B, Cm, flush
-    torch.cuda.empty_cache()
-    del np
+    out = {}
+    for name, setup in kernel_cases(dev, small).items():
+        if only and name != only:
+            continue
+        try:
+            fn, amount, kind = setup()
+        except Exception as e:  # a case whose entry point refuses (e.g. an unsupported shape)
+            out[name] = {"unavailable": str(e)[:160]}
+            continue
+        try:
+            for _ in range(3):
+                fn()
+            ts = []
+            for _ in range(reps):
+                torch.sum(flush, dim=0, keepdim=True, out=sink)
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                fn()
+                e.record()
+                e.synchronize()
+                ts.append(s.elapsed_time(e))
+        except Exception as e:
+            out[name] = {"unavailable": str(e)[:160]}
+            continue
+        ms = statistics.median(ts)
+        if kind == "bytes":
+            gbs = amount / (ms * 1e-3) / 1e9
+            out[name] = {"GB_s": round(gbs, 1), "frac_hbm": round(gbs / hbm, 4), "ms": round(ms, 5),
+                         "bytes": int(amount)}
+        else:
+            tf = amount / (ms * 1e-3) / 1e12
+            r = {"TFLOP_s": round(tf, 2), "ms": round(ms, 4)}
+            if "bf16" in name:
+                r["frac_bf16_measured"] = round(tf / pk["bf16_tflops"], 4)
+            else:
+                r["frac_fp32_nominal"] = round(tf / ffma_peak, 4)
+                r["fp32_nominal_tflops"] = round(ffma_peak, 1)
+            out[name] = r
+        del fn
+        torch.cuda.empty_cache()
     return out
+
+
+def run_case(name: str, reps: int) -> None:
+    """--case NAME: one kernel case on its small config, `reps` launches (for an ncu capture)."""
+    import torch
+
+    torch.cuda.set_device(0)
+    cases = kernel_cases(torch.device("cuda"), small=True)
+    fn, amount, kind = cases[name]()
+    for _ in range(reps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"case": name, "reps": reps, kind: amount}))
 
 
 # --------------------------------------------------------------------------- our arm
@@ -491,6 +551,14 @@ def ours(a, dist: Dist) -> None:
 
 def main():
     a = args_()
+    if a.list_cases:
+        import torch
+
+        print("\n".join(kernel_cases(torch.device("cpu"), small=True)))
+        return
+    if a.case:
+        run_case(a.case, a.case_reps)
+        return
     dist = Dist()
     if a.impl == "reference":
         reference_arm(a, dist)

@@ -415,11 +415,15 @@ int lyth_b200_reduce(int op, uint64_t n, const float *x, const float *y, float *
 int lyth_b200_matmul_f32(uint32_t m, uint32_t n, uint32_t k, const float *a, const float *b, float *c,
                          int exact, cudaStream_t stream);
 /* bf16 inputs (raw bfloat16 bits), f32 accumulate and output, on the tcgen05 tensor cores with
- * TMEM accumulators. m, n multiples of 128 and k a multiple of 64 take the tensor-core path;
- * other shapes return LYTH_E_UNSUPPORTED. No reference kernel: the reference never uses tensor
- * cores. Compared with eval_contraction on the bf16-rounded inputs within 1e-2 relative. */
+ * TMEM accumulators. m a multiple of 128, n of 256 and k of 64 (16-byte aligned buffers) take the
+ * tensor-core path; other shapes return LYTH_E_UNSUPPORTED. No reference kernel: the reference
+ * never uses tensor cores. Compared with eval_contraction on the bf16-rounded inputs within 1e-2
+ * relative. */
 int lyth_b200_matmul_bf16(uint32_t m, uint32_t n, uint32_t k, const uint16_t *a, const uint16_t *b,
                           float *c, cudaStream_t stream);
+/* LYTH_E_TIMEOUT when a bounded device-side wait of any kernel in this library ran out since the
+ * last call (the flag is then cleared), else LYTH_OK. Synchronises with the current device. */
+int lyth_b200_device_error(void);
 
 /* gate_proj GEMV (fixtures/kernel/gate_proj_int4.json, fixtures/poly/gate-proj-int4-nf4.json:
  * cost contracts only; the reference has no kernel). y[r] = sum_k dequant(W)[r, k] * x[k].
@@ -503,6 +507,11 @@ uint64_t lyth_sv_launches(const lyth_sv *sv);
 #define LYTH_SV_T_U 0
 #define LYTH_SV_T_CU 1
 #define LYTH_SV_T_EXCHANGE 2
+#define LYTH_SV_T_FUSED 3
+/* Fusion (lyth-circuit fuse, lib.rs:72-100; docs/ADR-0030): consecutive local gates touching at
+ * most `max_qubits` (1..5) bits run as one pass with the same chains in circuit order, bit-exact
+ * with the unfused passes. 1 = one pass per gate. The default is 5. */
+int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits);
 int lyth_sv_set_timing(lyth_sv *sv, int on);
 int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms);
 int lyth_sv_reset_timing(lyth_sv *sv);

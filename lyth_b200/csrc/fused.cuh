@@ -1,0 +1,29 @@
+// A fused group of state-vector gates (see k_fused.cu).
+#pragma once
+
+#include "gates.cuh"
+
+namespace lyth {
+
+constexpr int kFuseMaxQubits = 5;
+constexpr int kFuseMaxGates = 48;
+
+// A gate inside a group: target level t, control level c (-1 for a plain U), levels index the
+// group's bits; the matrix as lyth-circuit's f32s gives it.
+struct FusedGate {
+    int8_t t, c;
+    int16_t pad;
+    float m[8];
+};
+
+struct FusedGroup {
+    int32_t k;              // number of bits (levels)
+    uint32_t bits[kFuseMaxQubits];    // level l <-> amplitude bit bits[l]
+    uint32_t sorted[kFuseMaxQubits];  // the same bits ascending (for the zero insertion)
+    uint32_t ngates;
+    FusedGate gates[kFuseMaxGates];
+};
+
+int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaStream_t s);
+
+}  // namespace lyth

@@ -27,7 +27,7 @@
 
 #include <vector>
 
-#include "gates.cuh"
+#include "fused.cuh"
 
 namespace lyth {
 
@@ -158,8 +158,11 @@ struct lyth_sv {
     struct Mark { int cls; cudaEvent_t a, b; };
     std::vector<Mark> marks;
     std::vector<cudaEvent_t> pool;
-    uint64_t t_count[3] = {0, 0, 0};
-    double t_ms[3] = {0, 0, 0};
+    uint64_t t_count[4] = {0, 0, 0, 0};
+    double t_ms[4] = {0, 0, 0, 0};
+    // Fusion (lyth_sv_set_fusion): the open group of consecutive local gates, on physical bits.
+    int fuse_k = kFuseMaxQubits;
+    FusedGroup open{};
 };
 
 namespace {
@@ -285,6 +288,63 @@ int local_cu(lyth_sv *sv, uint32_t pc, uint32_t pt, const U8 &m) {
     return st;
 }
 
+// ---- fusion: lyth-circuit's greedy in-order rule (lib.rs:72-100) on physical local bits. A
+// gate joins the open group while the union of bits stays within fuse_k (and the group has
+// room); otherwise the group is run and the gate opens the next. A group of one gate runs the
+// specialised single-gate pass (the in-place CU then skips its control=0 half).
+int level_of(FusedGroup &g, uint32_t bit) {
+    for (int l = 0; l < g.k; l++)
+        if (g.bits[l] == bit) return l;
+    return -1;
+}
+
+int flush_group(lyth_sv *sv) {
+    FusedGroup &g = sv->open;
+    if (g.ngates == 0) return LYTH_OK;
+    int st;
+    if (g.ngates == 1) {
+        const FusedGate &fg = g.gates[0];
+        const U8 m{fg.m[0], fg.m[1], fg.m[2], fg.m[3], fg.m[4], fg.m[5], fg.m[6], fg.m[7]};
+        st = fg.c < 0 ? local_u(sv, g.bits[fg.t], m) : local_cu(sv, g.bits[fg.c], g.bits[fg.t], m);
+    } else {
+        for (int l = 0; l < g.k; l++) g.sorted[l] = g.bits[l];
+        for (int i = 1; i < g.k; i++)
+            for (int j = i; j > 0 && g.sorted[j - 1] > g.sorted[j]; j--) {
+                const uint32_t t = g.sorted[j];
+                g.sorted[j] = g.sorted[j - 1];
+                g.sorted[j - 1] = t;
+            }
+        const int mk = mark_begin(sv, LYTH_SV_T_FUSED);
+        st = launch_fused(sv->local_len, g, sv->re, sv->im, sv->stream);
+        mark_end(sv, mk);
+        sv->passes++;
+        sv->launches++;
+    }
+    g.k = 0;
+    g.ngates = 0;
+    return st;
+}
+
+// Queue a local gate: c < 0 for a U on bit t, else a CU (control c, target t).
+int add_local(lyth_sv *sv, int c, uint32_t t, const U8 &m) {
+    if (sv->fuse_k <= 1) return c < 0 ? local_u(sv, t, m) : local_cu(sv, (uint32_t)c, t, m);
+    FusedGroup &g = sv->open;
+    int extra = (level_of(g, t) < 0) + (c >= 0 && level_of(g, (uint32_t)c) < 0);
+    if (g.ngates > 0 && (g.k + extra > sv->fuse_k || g.ngates == (uint32_t)kFuseMaxGates)) {
+        int st = flush_group(sv);
+        if (st) return st;
+    }
+    if (level_of(g, t) < 0) g.bits[g.k++] = t;
+    if (c >= 0 && level_of(g, (uint32_t)c) < 0) g.bits[g.k++] = (uint32_t)c;
+    FusedGate &fg = g.gates[g.ngates++];
+    fg.t = (int8_t)level_of(g, t);
+    fg.c = (int8_t)(c >= 0 ? level_of(g, (uint32_t)c) : -1);
+    fg.pad = 0;
+    fg.m[0] = m.ar; fg.m[1] = m.ai; fg.m[2] = m.br; fg.m[3] = m.bi;
+    fg.m[4] = m.cr; fg.m[5] = m.ci; fg.m[6] = m.dr; fg.m[7] = m.di;
+    return LYTH_OK;
+}
+
 // Physical swap of local bit lb with rank bit gb: the half of the shard whose bit lb differs
 // from this rank's bit gb goes to the partner, landing at the same index with bit lb flipped;
 // the partner's matching half comes back.
@@ -385,14 +445,18 @@ int apply_one(lyth_sv *sv, const lyth_gate &g) {
         }
         case LYTH_GATE_U: {
             const uint32_t p = sv->pos[g.q0];
-            if (p < L) return local_u(sv, p, m);
+            if (p < L) return add_local(sv, -1, p, m);
+            int st = flush_group(sv);
+            if (st) return st;
             return exchange_gate(sv, p - L, m, -1);
         }
         case LYTH_GATE_CU: {
             const uint32_t pc = sv->pos[g.q0], pt = sv->pos[g.q1];
-            if (pc < L && pt < L) return local_cu(sv, pc, pt, m);
+            if (pc < L && pt < L) return add_local(sv, (int)pc, pt, m);
             if (pc >= L && !rank_bit(sv, pc - L)) return LYTH_OK;  // control 0 on this whole shard
-            if (pt < L) return local_u(sv, pt, m);
+            if (pt < L) return add_local(sv, -1, pt, m);
+            int st = flush_group(sv);
+            if (st) return st;
             return exchange_gate(sv, pt - L, m, pc < L ? (int)pc : -1);
         }
         default:
@@ -563,8 +627,19 @@ int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count) {
     DeviceGuard guard(sv->device);
     for (uint64_t i = 0; i < count; i++) {
         int st = apply_one(sv, gates[i]);
-        if (st) return st;
+        if (st) {
+            sv->open.k = 0;
+            sv->open.ngates = 0;
+            return st;
+        }
     }
+    return flush_group(sv);
+}
+
+int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits) {
+    if (!sv) return LYTH_E_INVALID;
+    if (max_qubits < 1 || max_qubits > kFuseMaxQubits) return LYTH_E_UNSUPPORTED;
+    sv->fuse_k = max_qubits;
     return LYTH_OK;
 }
 
@@ -585,7 +660,7 @@ int lyth_sv_set_timing(lyth_sv *sv, int on) {
 }
 
 int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms) {
-    if (!sv || cls < 0 || cls > 2) return LYTH_E_INVALID;
+    if (!sv || cls < 0 || cls > 3) return LYTH_E_INVALID;
     DeviceGuard guard(sv->device);
     int st = fold_timing(sv);
     if (st) return st;
@@ -598,7 +673,7 @@ int lyth_sv_reset_timing(lyth_sv *sv) {
     if (!sv) return LYTH_E_INVALID;
     DeviceGuard guard(sv->device);
     int st = fold_timing(sv);
-    for (int c = 0; c < 3; c++) { sv->t_count[c] = 0; sv->t_ms[c] = 0.0; }
+    for (int c = 0; c < 4; c++) { sv->t_count[c] = 0; sv->t_ms[c] = 0.0; }
     return st;
 }
 

@@ -98,10 +98,15 @@ class StateVector:
     def set_timing(self, on: bool) -> None:
         check(lib.lyth_sv_set_timing(self._h, int(on)), "set_timing")
 
+    def set_fusion(self, max_qubits: int) -> None:
+        """Fuse consecutive local gates touching at most max_qubits (1..5) bits; 1 = unfused."""
+        check(lib.lyth_sv_set_fusion(self._h, max_qubits), "set_fusion")
+
     def timing(self) -> dict:
-        """{class: (count, total ms)} for 'u' (1-qubit passes), 'cu' (2-qubit), 'exchange'."""
+        """{class: (count, total ms)}: 'u' (1-qubit passes), 'cu' (2-qubit), 'exchange',
+        'fused' (fused multi-gate passes)."""
         out = {}
-        for cls, name in enumerate(("u", "cu", "exchange")):
+        for cls, name in enumerate(("u", "cu", "exchange", "fused")):
             n, ms = C.c_uint64(), C.c_double()
             check(lib.lyth_sv_timing(self._h, cls, C.byref(n), C.byref(ms)), "timing")
             out[name] = (n.value, ms.value)

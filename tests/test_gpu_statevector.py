@@ -23,8 +23,9 @@ def as_tuples(gates):
     return out
 
 
-def run_engine(q, gates, re0, im0):
+def run_engine(q, gates, re0, im0, fuse=5):
     with lb.StateVector(q, device=0) as sv:
+        sv.set_fusion(fuse)
         sv.set_local(re0, im0)
         sv.apply(gates)
         sv.sync()
@@ -54,7 +55,22 @@ def test_circuits_bit_exact(cuda, case):
     assert np.array_equal(bits(gr), bits(wr)), name
     assert np.array_equal(bits(gi), bits(wi)), name
     swaps = sum(isinstance(g, cc.Swap) for g in gates)
-    assert st["passes"] >= len(gates) - swaps - 0  # swaps are relabels, the rest one pass each
+    assert st["passes"] <= len(gates) - swaps  # swaps are relabels; fused groups take one pass
+
+
+@pytest.mark.parametrize("case", [1, 2, 4])
+def test_fused_equals_unfused_at_every_k(cuda, case):
+    # ADR-0030 Q1: a fused circuit is the unfused circuit, bit for bit, for k = 1..5.
+    name, q, gates = suite()[case]
+    re0, im0 = orc.random_state(200 + case, q)
+    ur, ui, ust = run_engine(q, gates, re0, im0, fuse=1)
+    passes = []
+    for k in range(2, 6):
+        fr, fi, fst = run_engine(q, gates, re0, im0, fuse=k)
+        assert np.array_equal(bits(fr), bits(ur)), (name, k)
+        assert np.array_equal(bits(fi), bits(ui)), (name, k)
+        passes.append(fst["passes"])
+    assert passes == sorted(passes, reverse=True) and passes[-1] < ust["passes"], passes
 
 
 def test_from_basis_zero_like_lyth_circuit(cuda):
