@@ -400,10 +400,25 @@ def per_kernel(pk: dict, only: str | None = None, small: bool = False, reps: int
 
 
 def run_case(name: str, reps: int) -> None:
-    """--case NAME: one kernel case on its small config, `reps` launches (for an ncu capture)."""
+    """--case NAME: one kernel case on its small config, `reps` launches (for an ncu capture).
+    `sv_layer_2^Q` runs `reps` layers of the benchmark circuit on a Q-qubit state (the engine's
+    fused passes, as in the headline)."""
     import torch
 
     torch.cuda.set_device(0)
+    if name.startswith("sv_layer_2^"):
+        import lyth_b200 as lb
+        from lyth_b200 import circuit as cc
+
+        q = int(name.split("^")[1])
+        gates = cc.layered(q, reps, cc.Rng(cc.BENCH_SEED))
+        with lb.StateVector(q, device=0) as sv:
+            sv.init_random(cc.BENCH_SEED)
+            sv.apply(gates)
+            sv.sync()
+            st = sv.stats()
+        print(json.dumps({"case": name, "layers": reps, "passes": st["passes"], "bytes_per_pass": 16 << q}))
+        return
     cases = kernel_cases(torch.device("cuda"), small=True)
     fn, amount, kind = cases[name]()
     for _ in range(reps):
@@ -460,25 +475,36 @@ def ours(a, dist: Dist) -> None:
     gates_timed = a.steps * per
     value = gates_timed / (ms * 1e-3)
 
-    # roofline of the dominant kernel: the in-place 1-qubit pass, 16 B per local amplitude.
-    u_n, u_ms = tim["u"]
-    cu_n, cu_ms = tim["cu"]
-    ex_n, ex_ms = tim["exchange"]
-    u_bytes = 16.0 * sv.local_len
-    u_avg = u_ms / u_n if u_n else float("nan")
-    achieved = u_bytes / (u_avg * 1e-3) / 1e9 if u_n else None
+    # roofline of the dominant kernel: the in-place fused pass (every amplitude read and written
+    # once: 16 B per local amplitude per launch); the single-gate passes are reported beside it.
+    def cls_row(n_ms, bytes_per_launch):
+        n, tot = n_ms
+        if not n:
+            return None
+        avg = tot / n
+        return {"launches": n, "avg_ms": round(avg, 4), "GB_s": round(bytes_per_launch / (avg * 1e-3) / 1e9, 1)}
+
+    pass_bytes = 16.0 * sv.local_len
+    dominant = "fused" if tim["fused"][0] else "u"
+    d_n, d_ms = tim[dominant]
+    d_avg = d_ms / d_n if d_n else float("nan")
+    achieved = pass_bytes / (d_avg * 1e-3) / 1e9 if d_n else None
     peak = pk["hbm_gbs"]
     roofline = {"bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4) if achieved else None, "traffic": None,
-                "peak_source": pk_kind, "kernel": "gate_q_kernel (in-place 1-qubit pass)",
-                "algorithmic_bytes_per_launch": int(u_bytes), "avg_launch_ms": round(u_avg, 4),
-                "launches_timed": u_n,
-                "cu_pass": {"launches": cu_n, "avg_ms": round(cu_ms / cu_n, 4) if cu_n else None,
-                            "GB_s": round(8.0 * sv.local_len / (cu_ms / cu_n * 1e-3) / 1e9, 1) if cu_n else None},
-                "exchange": {"gates": ex_n, "avg_ms": round(ex_ms / ex_n, 4) if ex_n else None}}
-    traffic_ratio = os.environ.get("LYTH_GATE_TRAFFIC_RATIO")
+                "peak_source": pk_kind,
+                "kernel": "fused_pass_kernel (in place, <= 5 qubits per pass)" if dominant == "fused"
+                else "gate_q_kernel (in-place 1-qubit pass)",
+                "algorithmic_bytes_per_launch": int(pass_bytes), "avg_launch_ms": round(d_avg, 4),
+                "launches_timed": d_n,
+                "share_of_timed_region": round(d_ms / ms, 4) if ms else None,
+                "single_u_pass": cls_row(tim["u"], pass_bytes),
+                "single_cu_pass": cls_row(tim["cu"], 8.0 * sv.local_len),
+                "exchange": {"gates": tim["exchange"][0],
+                             "avg_ms": round(tim["exchange"][1] / tim["exchange"][0], 4) if tim["exchange"][0] else None}}
+    traffic_ratio = os.environ.get("LYTH_PASS_TRAFFIC_RATIO")
     if traffic_ratio:
-        roofline["traffic"] = int(float(traffic_ratio) * u_bytes)
+        roofline["traffic"] = int(float(traffic_ratio) * pass_bytes)
 
     # e2e: upload the shard from pinned host memory, apply one layer, read the shard back.
     e2e = None

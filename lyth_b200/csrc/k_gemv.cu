@@ -7,13 +7,21 @@
 // row r of W is contiguous along k, byte (r*k + c) / 2, low nibble = even c; INT4 nibbles are
 // two's complement (-8..7); NF4 nibbles index the 16-level normal-float codebook of QLoRA.
 //
-// Kernel: one warp per output row. A lane loads 16 bytes (32 weights) per step, 512 bytes a
-// warp, so a 4096-wide row is four coalesced 128-bit loads per lane, all issued before any is
-// used. x is staged once per block in shared memory, widened to f32 and permuted so that lane
-// l's 32 values at step s sit in 32 different words of 32 different banks. A lane's 32
-// weights lie in one scale group (the group is a multiple of 32), so the scale multiplies the
-// lane's partial once per step instead of once per weight. The warp's partials combine with
-// shuffles; the row result is rounded once to fp16 (RNE).
+// Kernel: one warp per output row at a time. A lane owns 32-weight chunks (16 bytes of W):
+// chunk = lane + 32 * s, so each step of a warp is one coalesced 512-byte load, and every step
+// of a row is issued before any is used. x is staged once per block in shared memory, widened
+// to f32, one 32-value chunk per row of 36 floats (the pad makes a lane's 128-bit reads
+// conflict-free: 8 lanes of a phase hit 8 different 4-bank groups). A chunk lies inside one
+// scale group (the group is a multiple of 32), so the scale multiplies a chunk's partial once.
+//
+// The arithmetic is the instruction budget: 58.7 M weights in ~5 us leaves ~3 instructions per
+// weight on 148 SMs. INT4: the word is xor'ed with 0x88888888 (nibble v = q + 8, 0..15), split
+// into its even and odd nibbles as bytes, and one PRMT per weight builds the float whose bits
+// are 0x3F00_0000 | v << 16, i.e. 0.5 + v/256; one FFMA accumulates it against x. Per chunk,
+// sum q x = 256 * (sum f x - (17/32) * sum x), with sum x over the chunk precomputed once per
+// block (x is shared by every row); the cancellation costs ~5 of f32's 24 bits, far inside the
+// 1e-3 output tolerance. NF4: the same byte split, a PRMT to an index, and a 16-entry shared
+// table. The warp's chunk partials combine with shuffles; the row is rounded once to fp16.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -23,39 +31,98 @@ namespace lyth {
 
 __constant__ float c_nf4[16];
 
-// INT4: (nibble ^ 8) is q + 8 in 0..15; OR-ing it into the mantissa of 2^23 gives the float
-// 8388608 + q + 8 exactly, and one subtraction leaves q. One LOP3 and one FADD per weight.
-LYTH_D float int4_of(uint32_t word, int j) {
-    const uint32_t bits = ((word >> (4 * j)) & 0xfu) ^ 0x4b000008u;
-    return __fsub_rn(__uint_as_float(bits), 8388616.0f);
-}
-
-template <int FMT>
-LYTH_D float weight_of(uint32_t word, int j, const float *lut) {
-    if (FMT == 0) return int4_of(word, j);
-    return lut[(word >> (4 * j)) & 0xfu];
-}
-
 LYTH_D float half_bits_to_float(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+LYTH_D uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// One 16-byte chunk (32 weights) against its 32 staged x values. INT4 returns sum f x with
+// f = 0.5 + (q + 8)/256 (the caller corrects); NF4 returns sum code[v] x.
+template <int FMT>
+LYTH_D float chunk_dot(uint4 v, const float *xr, const float *lut) {
+    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+    float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        uint32_t w = words[q];
+        if (FMT == 0) w ^= 0x88888888u;            // v = q + 8 in every nibble
+        const uint32_t lo = w & 0x0F0F0F0Fu;        // nibbles 0, 2, 4, 6 as bytes
+        const uint32_t hi = (w >> 4) & 0x0F0F0F0Fu; // nibbles 1, 3, 5, 7 as bytes
+        const float4 xa = *reinterpret_cast<const float4 *>(xr + 8 * q);
+        const float4 xb = *reinterpret_cast<const float4 *>(xr + 8 * q + 4);
+        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            float f0, f1;
+            if (FMT == 0) {
+                // bytes [0, 0, v, 0x3F] -> bits 0x3F00_0000 | v << 16 -> 0.5 + v / 256
+                f0 = __uint_as_float(prmt(lo, 0x3F000000u, 0x7044u | (uint32_t)(b << 8)));
+                f1 = __uint_as_float(prmt(hi, 0x3F000000u, 0x7044u | (uint32_t)(b << 8)));
+            } else {
+                f0 = lut[prmt(lo, 0u, 0x4440u | (uint32_t)b)];
+                f1 = lut[prmt(hi, 0u, 0x4440u | (uint32_t)b)];
+            }
+            acc0 = __fmaf_rn(f0, xv[2 * b], acc0);
+            acc1 = __fmaf_rn(f1, xv[2 * b + 1], acc1);
+        }
+    }
+    return __fadd_rn(acc0, acc1);
+}
+
+constexpr int kGemvRowStride = 36;  // floats per staged 32-value chunk (pad 4: conflict-free LDS.128)
 
 template <int FMT>
 __global__ void __launch_bounds__(256) gemv_q4_kernel(uint32_t rows, uint32_t k, uint32_t group, const uint8_t *w,
                                                       const uint16_t *scales, const uint16_t *x, uint16_t *y) {
-    extern __shared__ float smem[];
-    float *xs = smem;        // k floats, permuted: [step][j][lane]
-    float *lut = smem + k;   // 16 floats
+    extern __shared__ __align__(16) float smem[];
+    const uint32_t chunks = k >> 5;
+    float *xs = smem;                                 // chunks x 36
+    float *xsum = smem + chunks * kGemvRowStride;     // chunks
+    float *lut = xsum + chunks;                       // 16
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t steps = k / 1024;  // 1024 weights per warp-step (32 lanes x 32)
-    // Stage x: element c = 32*(lane + 32*s) + j goes to xs[(s*32 + j)*32 + lane].
-    for (uint32_t c = threadIdx.x; c < k; c += blockDim.x) {
-        const uint32_t chunk = c >> 5, j = c & 31;
-        const uint32_t s = chunk >> 5, l = chunk & 31;
-        xs[(s * 32 + j) * 32 + l] = half_bits_to_float(x[c]);
+    // Stage x: each thread moves 8 fp16 values (one 16-byte load) per step, all loads issued
+    // before any conversion; four consecutive threads cover one 32-value chunk, and their four
+    // 8-value sums combine with two shuffles into that chunk's sum (INT4's correction term).
+    {
+        const uint4 *x16 = reinterpret_cast<const uint4 *>(x);
+        const uint32_t nvec = k >> 3;  // 16-byte groups of x
+        for (uint32_t v0 = 0; v0 < nvec; v0 += 4 * blockDim.x) {
+            uint4 raw[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t v = v0 + u * blockDim.x + threadIdx.x;
+                if (v < nvec) raw[u] = x16[v];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t v = v0 + u * blockDim.x + threadIdx.x;
+                float part = 0.0f;
+                if (v < nvec) {
+                    const uint32_t hw[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+                    float *dst = xs + (v >> 2) * kGemvRowStride + (v & 3) * 8;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&hw[e]));
+                        dst[2 * e] = f.x;
+                        dst[2 * e + 1] = f.y;
+                        part = __fadd_rn(part, __fadd_rn(f.x, f.y));
+                    }
+                }
+                // Whole warps take part in the shuffles; v < nvec is uniform per 4-lane group.
+                part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 1));
+                part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 2));
+                if (FMT == 0 && v < nvec && (v & 3) == 0) xsum[v >> 2] = part;
+            }
+        }
     }
     if (FMT == 1 && threadIdx.x < 16) lut[threadIdx.x] = c_nf4[threadIdx.x];
     __syncthreads();
 
     const uint32_t groups = k / group;
+    const uint32_t steps = chunks >> 5;  // 32 chunks (one per lane) per warp-step
     for (uint32_t r = blockIdx.x * 8 + warp; r < rows; r += gridDim.x * 8) {
         const uint4 *wrow = reinterpret_cast<const uint4 *>(w + (uint64_t)r * (k >> 1));
         const uint16_t *srow = scales + (uint64_t)r * groups;
@@ -76,16 +143,9 @@ __global__ void __launch_bounds__(256) gemv_q4_kernel(uint32_t rows, uint32_t k,
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 if (s0 + u < steps) {
-                    const float *xv = xs + (uint64_t)(s0 + u) * 1024 + lane;
-                    const uint32_t words[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-                    float part = 0.0f;
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-#pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            part = __fmaf_rn(weight_of<FMT>(words[q], j, lut), xv[(q * 8 + j) * 32], part);
-                        }
-                    }
+                    const uint32_t chunk = lane + 32 * (s0 + u);
+                    float part = chunk_dot<FMT>(v[u], xs + chunk * kGemvRowStride, lut);
+                    if (FMT == 0) part = __fmul_rn(256.0f, __fmaf_rn(-0.53125f, xsum[chunk], part));
                     acc = __fmaf_rn(sc[u], part, acc);
                 }
             }
@@ -197,9 +257,13 @@ extern "C" int lyth_b200_gemv_q4(int fmt, uint32_t rows, uint32_t k, uint32_t gr
     if (rows == 0) return LYTH_OK;
     if (k == 0 || k % 1024 != 0 || group == 0 || group % 32 != 0 || k % group != 0) return LYTH_E_UNSUPPORTED;
     if ((((uintptr_t)w) & 15u) != 0) return LYTH_E_UNSUPPORTED;
-    const size_t smem = (size_t)k * sizeof(float) + 16 * sizeof(float);
+    const size_t smem = ((size_t)(k >> 5) * (kGemvRowStride + 1) + 16) * sizeof(float);
     if (smem > 200 * 1024) return LYTH_E_UNSUPPORTED;
-    const unsigned grid = (rows + 7) / 8;
+    // Persistent: at most 4 blocks per SM (the register budget), each walking rows, so x is
+    // staged once per block rather than once per 8 rows.
+    unsigned grid = (rows + 7) / 8;
+    const unsigned cap = (unsigned)device_sms() * 4u;
+    if (grid > cap) grid = cap;
     if (fmt == LYTH_GEMV_INT4) {
         if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_q4_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         gemv_q4_kernel<0><<<grid, 256, smem, s>>>(rows, k, group, w, scales, x, y);

@@ -32,6 +32,7 @@ constexpr int MM_STAGE_BYTES = MM_A_BYTES + MM_B_BYTES;     // 48 KiB
 constexpr int MM_TMEM_COLS = 2 * MM_BN;                     // two f32 accumulators
 constexpr int MM_THREADS = 192;
 constexpr uint32_t MM_WAIT_LIMIT = 1u << 24;                 // try_wait polls before giving up
+constexpr uint64_t MM_WAIT_NS = 2000000000ull;               // or 2 s of wall time, whichever first
 constexpr size_t MM_SMEM = 1024 + (size_t)MM_STAGES * MM_STAGE_BYTES + 256;
 
 __device__ int g_device_error;
@@ -47,8 +48,17 @@ LYTH_D uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_sha
 LYTH_D void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
-// Wait for the phase of parity `parity` to complete; false (and the error flag) after the limit.
+LYTH_D uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for the phase of parity `parity` to complete. Bounded twice: by a poll count and by
+// wall time (MM_WAIT_NS of the global timer), since one try_wait may itself suspend for an
+// implementation-defined interval. On the limit: set the error flag and return false.
 LYTH_D bool mbar_wait(uint32_t bar, uint32_t parity) {
+    uint64_t t0 = 0;
     for (uint32_t i = 0; i < MM_WAIT_LIMIT; ++i) {
         uint32_t ok;
         asm volatile(
@@ -59,6 +69,11 @@ LYTH_D bool mbar_wait(uint32_t bar, uint32_t parity) {
             : "r"(bar), "r"(parity)
             : "memory");
         if (ok) return true;
+        if ((i & 255u) == 0) {
+            const uint64_t t = global_ns();
+            if (i == 0) t0 = t;
+            else if (t - t0 > MM_WAIT_NS) break;
+        }
     }
     atomicExch(&g_device_error, 1);
     return false;

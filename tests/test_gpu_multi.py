@@ -1,0 +1,81 @@
+"""The sharded state vector on 2 (or more) GPUs: each rank's shard, after whole circuits whose
+gates hit the rank bits (exchange), a rank-bit control (rank-local) and SWAPs across the
+boundary (relabels undone by real exchanges at read-out), is bit-identical to the host
+evaluator's unsharded result. One process per GPU, spawned by the test; NVLS off."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _ngpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _worker(rank, nranks, q, case, nid, out_dir):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import lyth_b200 as lb
+    from tests.test_gpu_statevector import as_tuples, suite
+
+    torch.cuda.set_device(rank)
+    from oracle import oracle as orc
+
+    name, q, gates = case_gates(case, q)
+    re0, im0 = orc.random_state(300 + case, q)
+    L = (1 << q) // nranks
+    lo, hi = rank * L, (rank + 1) * L
+    with lb.StateVector(q, device=rank, rank=rank, nranks=nranks, nccl_id=nid) as sv:
+        sv.set_local(np.ascontiguousarray(re0[lo:hi]), np.ascontiguousarray(im0[lo:hi]))
+        sv.apply(gates)
+        sv.sync()
+        gr, gi = np.empty(L, np.float32), np.empty(L, np.float32)
+        sv.get_local(gr, gi)
+        st = sv.stats()
+    wr, wi = orc.run_gates(as_tuples(gates), re0, im0)
+    ok = np.array_equal(gr.view(np.uint32), wr[lo:hi].view(np.uint32)) and \
+        np.array_equal(gi.view(np.uint32), wi[lo:hi].view(np.uint32))
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{int(ok)} {st['exchanges']} {st['bytes_sent']}\n")
+    del suite
+
+
+def case_gates(case, q):
+    from lyth_b200 import circuit as cc
+
+    if case == 0:
+        return "layered", q, cc.layered(q, 3, cc.Rng(cc.BENCH_SEED))
+    if case == 1:
+        return "random", q, cc.random(q, 6, cc.Rng(20_260_931))
+    # gates aimed at the top (rank) bits: U on them, CU with rank-bit control / target, swaps
+    t = q - 1
+    g = [cc.U(t, cc.H), cc.CU(t, 0, cc.X), cc.CU(1, t, cc.zyz(0.3, 0.2, 0.1)), cc.Swap(0, t),
+         cc.U(t, cc.zyz(1.0, 2.0, 3.0)), cc.CU(t, t - 1, cc.phase(0.7)), cc.Swap(t - 1, 2), cc.U(0, cc.H)]
+    return "rank-bit gates", q, g
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_two_ranks_bit_exact(case, tmp_path):
+    import lyth_b200 as lb
+
+    nranks, q = 2, 18
+    nid = lb.unique_id()
+    ctx = torch.multiprocessing.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, nranks, q, case, nid, str(tmp_path))) for r in range(nranks)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for r, p in enumerate(procs):
+        assert p.exitcode == 0, f"rank {r} exit {p.exitcode}"
+        ok, ex, sent = open(tmp_path / f"r{r}.txt").read().split()
+        assert ok == "1", f"rank {r}: shard differs from the evaluator"
+        assert int(ex) > 0, "the circuit must exercise the exchange"

@@ -51,6 +51,19 @@ def test_signed_zeros_and_nan_in_max_min(cuda):
         assert np.array_equal(bits(got), bits(want)), op
 
 
+@pytest.mark.parametrize("pair", [(-0.0, 0.0), (0.0, -0.0), (-0.0, -0.0), (0.0, 0.0), (float("nan"), -0.0),
+                                  (-0.0, float("nan")), (-1.5, float("nan"))])
+def test_combine_both_operand_orders(cuda, pair):
+    # ast.rs:594-621: max(-0, +0) = +0 and min(-0, +0) = -0 whichever comes first; NaN loses.
+    # With two elements in one block, slot 0 = x[0], slot 1 = x[1], and the tree's last level
+    # combines them in that order.
+    x = np.array(pair, np.float32)
+    for op in (lb.MAX, lb.MIN):
+        got = lb.reduce_partials(op, dev(x, cuda), grid=1).cpu().numpy()
+        want = orc.reduce(op, x, grid=1)
+        assert np.array_equal(bits(got), bits(want)), (op, pair, got, want)
+
+
 def _cluster_fold(op, partials):
     # lyth_b200_reduce's order: partials in groups of 8 (clusters), folded left to right within
     # each group, then the group results left to right. Blocks past the grid add the identity.
