@@ -71,20 +71,32 @@ LYTH_D void dispatch_cu(int c, int t, const U8 &m, float (&xr)[1 << K], float (&
     }
 }
 
+// Blocks per SM the register budget should allow: the 2^K amplitudes of a tuple live in
+// registers (2^(K+1) floats), and a second resident block doubles the loads in flight.
 template <int K>
-__global__ void __launch_bounds__(256) fused_pass_kernel(uint64_t len, const __grid_constant__ FusedGroup G,
-                                                         float *re, float *im) {
+constexpr int fused_min_blocks() {
+    return K >= 5 ? 1 : (K == 4 ? 2 : 4);
+}
+
+template <int K>
+__global__ void __launch_bounds__(256, fused_min_blocks<K>())
+    fused_pass_kernel(uint64_t len, const __grid_constant__ FusedGroup G, float *re, float *im) {
     constexpr int S = 1 << K;
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t nthreads = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t rest = len >> K;
-    uint64_t stride[K];
-#pragma unroll
-    for (int l = 0; l < K; l++) stride[l] = 1ull << G.bits[l];
     for (uint64_t r = tid; r < rest; r += nthreads) {
         uint64_t base = r;
 #pragma unroll
         for (int l = 0; l < K; l++) base = insert_bit(base, G.sorted[l], 0);
+        // The per-level strides are re-read from the parameter space each iteration (an
+        // empty asm keeps the compiler from hoisting 2^K 64-bit offsets into registers).
+        uint64_t stride[K];
+#pragma unroll
+        for (int l = 0; l < K; l++) {
+            stride[l] = 1ull << G.bits[l];
+            asm volatile("" : "+l"(stride[l]));
+        }
         float xr[S], xi[S];
 #pragma unroll
         for (int j = 0; j < S; j++) {
