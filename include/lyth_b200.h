@@ -408,6 +408,18 @@ int lyth_b200_reduce_partials(int op, uint64_t n, const float *x, const float *y
 size_t lyth_b200_reduce_workspace_bytes(uint64_t n);
 int lyth_b200_reduce(int op, uint64_t n, const float *x, const float *y, float *out, void *workspace,
                      size_t workspace_bytes, cudaStream_t stream);
+/* The same whole reduction for callers that cannot provide device memory -- a host whose device
+ * memory all belongs to its own arena, a runtime that embeds these kernels and does not let them
+ * allocate, a loop that cannot take the synchronisation of cudaMalloc. It has no counterpart in
+ * the reference. It allocates nothing: the cluster results go to a fixed 64 KiB array in the
+ * library's own device memory, which every GPU that loads the library keeps until the process
+ * exits, so n is limited to LYTH_REDUCE_NOALLOC_MAX_N elements (larger n: LYTH_E_UNSUPPORTED,
+ * nothing runs). The first call on a device looks the array's address up; make it before any
+ * stream capture. All calls share the array: each writes every slot it reads, so no clearing is
+ * needed, but calls that overlap on the GPU race. Result: bit for bit lyth_b200_reduce's. */
+#define LYTH_REDUCE_NOALLOC_MAX_N 268435456ull
+int lyth_b200_reduce_noalloc(int op, uint64_t n, const float *x, const float *y, float *out,
+                             cudaStream_t stream);
 
 /* Contraction C = A * B, row-major, A m x k, B k x n, C m x n (examples/matmul.lyth).
  * exact = 1: the reference's order bit for bit (p ascending, mul.rn then add.rn).

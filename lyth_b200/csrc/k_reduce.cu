@@ -203,3 +203,67 @@ extern "C" int lyth_b200_reduce(int op, uint64_t n, const float *x, const float 
     if (op == 2 && !y) return reduce_full<2, false>(n, x, nullptr, out, ws, s);
     return LYTH_E_UNSUPPORTED;
 }
+
+// ---------------------------------------------------------------------------------------------
+// The whole reduction without any allocation by anyone: lyth_b200_reduce_noalloc.
+//
+// Some callers cannot hand this library a device workspace: a host that has given all device
+// memory to its own arena and forbids further allocation, a runtime that embeds LYTH kernels as
+// plug-ins and does not let them allocate, or a latency-bound loop that cannot afford the device
+// synchronisation cudaMalloc brings. For them the cluster results of the reduction go to a
+// fixed array in the library's own device memory instead of a caller workspace. The kernels and
+// the combine order are those of lyth_b200_reduce, so the result is the same, bit for bit.
+//
+// The array holds 16384 cluster results (64 KiB), enough for n up to LYTH_REDUCE_NOALLOC_MAX_N =
+// 2^28 elements (16384 clusters x 8 blocks x 2048 elements); every GPU that loads the library
+// keeps it until the process exits. The first call on a device looks the array's address up
+// (cudaGetSymbolAddress); make that first call before any stream capture. Each call writes every slot it
+// later reads, so nothing has to start at zero, but all calls share the array: two calls that
+// overlap on the GPU (different streams, or devices sharing nothing but this process) race.
+namespace lyth {
+
+constexpr uint32_t kNoAllocClusters = 16384;
+static __device__ __align__(256) float g_noalloc_clusters[kNoAllocClusters];
+
+// The array's device address, looked up once per device with that device current (a host-side
+// use of the symbol's name is not a device address).
+static float *noalloc_scratch(int *status) {
+    static float *ptr_of[64] = {nullptr};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *status = status_of(e);
+        return nullptr;
+    }
+    if (dev < 0 || dev >= 64) {
+        *status = LYTH_E_UNSUPPORTED;
+        return nullptr;
+    }
+    if (!ptr_of[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_clusters);
+        if (e != cudaSuccess) {
+            *status = status_of(e);
+            return nullptr;
+        }
+        ptr_of[dev] = static_cast<float *>(p);
+    }
+    *status = LYTH_OK;
+    return ptr_of[dev];
+}
+
+}  // namespace lyth
+
+extern "C" int lyth_b200_reduce_noalloc(int op, uint64_t n, const float *x, const float *y, float *out,
+                                        cudaStream_t s) {
+    if (!x || !out) return LYTH_E_INVALID;
+    if (n > LYTH_REDUCE_NOALLOC_MAX_N) return LYTH_E_UNSUPPORTED;  // more clusters than the array holds
+    if (!((op == 0) || ((op == 1 || op == 2) && !y))) return LYTH_E_UNSUPPORTED;
+    int st = LYTH_OK;
+    float *ws = noalloc_scratch(&st);
+    if (!ws) return st;
+    if (op == 0 && y) return reduce_full<0, true>(n, x, y, out, ws, s);
+    if (op == 0) return reduce_full<0, false>(n, x, nullptr, out, ws, s);
+    if (op == 1) return reduce_full<1, false>(n, x, nullptr, out, ws, s);
+    return reduce_full<2, false>(n, x, nullptr, out, ws, s);
+}
