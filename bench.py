@@ -64,6 +64,7 @@ def args_():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-qubits", type=int, default=25)
+    ap.add_argument("--fuse", type=int, default=None, help="max qubits per fused pass (1..5; default: the engine's)")
     ap.add_argument("--case", default=None, help="run one kernel case (small config) and exit")
     ap.add_argument("--case-reps", type=int, default=3)
     ap.add_argument("--list-cases", action="store_true")
@@ -441,6 +442,8 @@ def ours(a, dist: Dist) -> None:
     nid = lb.unique_id() if (dist.world > 1 and dist.rank == 0) else None
     nid = dist.bcast_bytes(nid)
     sv = lb.StateVector(q, device=dist.local, rank=dist.rank, nranks=dist.world, nccl_id=nid)
+    if a.fuse:
+        sv.set_fusion(a.fuse)
     total_layers = a.warmup + a.steps
     gates = cc.layered(q, total_layers, cc.Rng(cc.BENCH_SEED))
     per = len(gates) // total_layers
