@@ -524,6 +524,11 @@ uint64_t lyth_sv_launches(const lyth_sv *sv);
  * most `max_qubits` (1..5) bits run as one pass with the same chains in circuit order, bit-exact
  * with the unfused passes. 1 = one pass per gate. The default is 5. */
 int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits);
+/* A gate on a qubit that currently lives on a rank bit: on = 1 (default) first swaps it with the
+ * local qubit used furthest ahead in the gate list (half the shard crosses NVLink each way) and
+ * then runs the gate as a local (fusable) pass; on = 0 exchanges the whole shard with the partner
+ * rank and computes this rank's row of the gate. Both are bit-exact. */
+int lyth_sv_set_remap(lyth_sv *sv, int on);
 int lyth_sv_set_timing(lyth_sv *sv, int on);
 int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms);
 int lyth_sv_reset_timing(lyth_sv *sv);

@@ -104,6 +104,7 @@ _sig("lyth_sv_set_timing", _i32, [_vp, _i32])
 _sig("lyth_sv_timing", _i32, [_vp, _i32, C.POINTER(_u64), C.POINTER(C.c_double)])
 _sig("lyth_sv_reset_timing", _i32, [_vp])
 _sig("lyth_sv_set_fusion", _i32, [_vp, _i32])
+_sig("lyth_sv_set_remap", _i32, [_vp, _i32])
 _sig("lyth_b200_device_error", _i32, [])
 
 

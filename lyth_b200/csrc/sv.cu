@@ -118,10 +118,21 @@ __global__ void __launch_bounds__(256) scale_kernel(uint64_t len, const double *
 }
 
 // Pack / unpack the local indices whose bit `lb` equals `v` (a half of the shard), taking the
-// k-th such index for k in [k0, k0 + count).
+// k-th such index for k in [k0, k0 + count). With lb >= 2 (and count, k0 multiples of 4) four
+// consecutive k are four consecutive indices, so both sides move as 128-bit vectors.
 __global__ void __launch_bounds__(256) pack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
                                                         const float *re, const float *im, float *ore, float *oim) {
-    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t nth = (uint64_t)gridDim.x * blockDim.x;
+    if (lb >= 2 && (count & 3) == 0 && (k0 & 3) == 0) {
+        for (uint64_t g = tid; g < (count >> 2); g += nth) {
+            const uint64_t i = insert_bit(k0 + 4 * g, lb, v);
+            st4(ore + 4 * g, ld_stream4(re + i));
+            st4(oim + 4 * g, ld_stream4(im + i));
+        }
+        return;
+    }
+    for (uint64_t k = tid; k < count; k += nth) {
         const uint64_t i = insert_bit(k0 + k, lb, v);
         ore[k] = re[i];
         oim[k] = im[i];
@@ -129,7 +140,17 @@ __global__ void __launch_bounds__(256) pack_half_kernel(uint64_t count, uint64_t
 }
 __global__ void __launch_bounds__(256) unpack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
                                                           float *re, float *im, const float *ire, const float *iim) {
-    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t nth = (uint64_t)gridDim.x * blockDim.x;
+    if (lb >= 2 && (count & 3) == 0 && (k0 & 3) == 0) {
+        for (uint64_t g = tid; g < (count >> 2); g += nth) {
+            const uint64_t i = insert_bit(k0 + 4 * g, lb, v);
+            st4(re + i, ld_stream4(ire + 4 * g));
+            st4(im + i, ld_stream4(iim + 4 * g));
+        }
+        return;
+    }
+    for (uint64_t k = tid; k < count; k += nth) {
         const uint64_t i = insert_bit(k0 + k, lb, v);
         re[i] = ire[k];
         im[i] = iim[k];
@@ -145,10 +166,12 @@ struct lyth_sv {
     int device = 0, rank = 0, nranks = 1;
     uint64_t local_len = 0, chunk = 0;
     float *re = nullptr, *im = nullptr;
-    float *rre[2] = {nullptr, nullptr}, *rim[2] = {nullptr, nullptr};
+    float *rre[2] = {nullptr, nullptr}, *rim[2] = {nullptr, nullptr};  // receive chunks
+    float *sre[2] = {nullptr, nullptr}, *sim[2] = {nullptr, nullptr};  // packed send chunks
     double *scratch = nullptr;  // norm partials
     cudaStream_t stream = nullptr, comm_stream = nullptr;
     cudaEvent_t ev_recv[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_start = nullptr;
+    cudaEvent_t ev_packed[2] = {nullptr, nullptr};
     ncclComm_t comm = nullptr;
     std::vector<uint32_t> pos;  // logical qubit -> physical bit
     std::vector<uint32_t> inv;  // physical bit -> logical qubit
@@ -163,6 +186,10 @@ struct lyth_sv {
     // Fusion (lyth_sv_set_fusion): the open group of consecutive local gates, on physical bits.
     int fuse_k = kFuseMaxQubits;
     FusedGroup open{};
+    // Rank-bit gates: 1 = swap the qubit into a local bit first (default), 0 = pairwise
+    // exchange of the whole shard and compute this rank's row.
+    int remap = 1;
+    uint64_t swaps_in = 0;
 };
 
 namespace {
@@ -346,31 +373,53 @@ int add_local(lyth_sv *sv, int c, uint32_t t, const U8 &m) {
 }
 
 // Physical swap of local bit lb with rank bit gb: the half of the shard whose bit lb differs
-// from this rank's bit gb goes to the partner, landing at the same index with bit lb flipped;
-// the partner's matching half comes back.
+// from this rank's bit gb goes to the partner and lands at the same index (same other bits), and
+// the partner's matching half comes back into the positions it vacated. Chunked and pipelined
+// over two streams: pack(c) -> send/recv(c) -> unpack(c), with pack(c+1) running while chunk c
+// is on the wire and the receive buffers double-buffered.
 int physical_swap_local_global(lyth_sv *sv, uint32_t lb, uint32_t gb) {
     const int partner = sv->rank ^ (1 << gb);
-    const uint64_t g = (uint64_t)rank_bit(sv, gb);
-    const uint64_t send_v = g ^ 1ull;   // local bit value of what leaves
-    const uint64_t recv_v = send_v;     // it is replaced in place by the partner's
+    const uint64_t v = (uint64_t)rank_bit(sv, gb) ^ 1ull;  // local bit value of what leaves and arrives
     const uint64_t half = sv->local_len >> 1;
-    int st = LYTH_OK;
-    for (uint64_t k0 = 0; k0 < half; k0 += sv->chunk) {
-        const uint64_t len = (half - k0) < sv->chunk ? (half - k0) : sv->chunk;
-        const unsigned grid = stream_grid(len, 256);
-        // pack into buffer 0, receive into buffer 1
-        pack_half_kernel<<<grid, 256, 0, sv->stream>>>(len, k0, lb, send_v, sv->re, sv->im, sv->rre[0], sv->rim[0]);
-        if ((st = last_launch_status())) return st;
-        if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
+    const uint64_t nchunks = (half + sv->chunk - 1) / sv->chunk;
+    int st = status_of(cudaEventRecord(sv->ev_start, sv->stream));
+    if (st) return st;
+    if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_start, 0)))) return st;
+    auto len_of = [&](uint64_t c) { return (half - c * sv->chunk) < sv->chunk ? (half - c * sv->chunk) : sv->chunk; };
+    auto pack = [&](uint64_t c) -> int {
+        const int b = (int)(c & 1);
+        const uint64_t len = len_of(c);
+        pack_half_kernel<<<stream_grid(len / 4 + 1, 256), 256, 0, sv->stream>>>(len, c * sv->chunk, lb, v, sv->re,
+                                                                              sv->im, sv->sre[b], sv->sim[b]);
+        sv->launches++;
+        int r = last_launch_status();
+        if (r) return r;
+        return status_of(cudaEventRecord(sv->ev_packed[b], sv->stream));
+    };
+    if ((st = pack(0))) return st;
+    for (uint64_t c = 0; c < nchunks; c++) {
+        const int b = (int)(c & 1);
+        const uint64_t len = len_of(c);
+        // wire: after pack(c); into receive buffer b once unpack(c - 2) has drained it
+        if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_packed[b], 0)))) return st;
+        if (c >= 2 && (st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_done[b], 0)))) return st;
         if ((st = nccl_status(g_nccl.GroupStart()))) return st;
-        g_nccl.Send(sv->rre[0], len, ncclFloat32, partner, sv->comm, sv->stream);
-        g_nccl.Send(sv->rim[0], len, ncclFloat32, partner, sv->comm, sv->stream);
-        g_nccl.Recv(sv->rre[1], len, ncclFloat32, partner, sv->comm, sv->stream);
-        g_nccl.Recv(sv->rim[1], len, ncclFloat32, partner, sv->comm, sv->stream);
+        g_nccl.Send(sv->sre[b], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
+        g_nccl.Send(sv->sim[b], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
+        g_nccl.Recv(sv->rre[b], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
+        g_nccl.Recv(sv->rim[b], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
         if ((st = nccl_status(g_nccl.GroupEnd()))) return st;
-        unpack_half_kernel<<<grid, 256, 0, sv->stream>>>(len, k0, lb, recv_v, sv->re, sv->im, sv->rre[1], sv->rim[1]);
-        if ((st = last_launch_status())) return st;
+        if ((st = status_of(cudaEventRecord(sv->ev_recv[b], sv->comm_stream)))) return st;
         sv->bytes_sent += 2 * len * sizeof(float);
+        // compute stream: pack the next chunk while this one is on the wire; its send buffer
+        // (b ^ 1) was last read by transfer c - 1, which unpack(c - 1) already waited for.
+        if (c + 1 < nchunks && (st = pack(c + 1))) return st;
+        if ((st = status_of(cudaStreamWaitEvent(sv->stream, sv->ev_recv[b], 0)))) return st;
+        unpack_half_kernel<<<stream_grid(len / 4 + 1, 256), 256, 0, sv->stream>>>(len, c * sv->chunk, lb, v, sv->re,
+                                                                                sv->im, sv->rre[b], sv->rim[b]);
+        sv->launches++;
+        if ((st = last_launch_status())) return st;
+        if ((st = status_of(cudaEventRecord(sv->ev_done[b], sv->stream)))) return st;
     }
     sv->exchanges++;
     return LYTH_OK;
@@ -432,7 +481,42 @@ int normalize(lyth_sv *sv) {
     return LYTH_OK;
 }
 
-int apply_one(lyth_sv *sv, const lyth_gate &g) {
+// Bring the qubit on rank bit (gp - L) into a local bit: the victim is the local bit whose
+// logical qubit is next used furthest ahead in gates[i..count) (never used: best), ties to the
+// highest bit. The choice depends only on the map and the gate list, so every rank makes it.
+int swap_in(lyth_sv *sv, uint32_t gp, const lyth_gate *gates, uint64_t count, uint64_t i) {
+    int st = flush_group(sv);
+    if (st) return st;
+    const uint32_t L = sv->local_bits;
+    std::vector<uint64_t> next(sv->qubits, UINT64_MAX);
+    uint32_t seen = 0;
+    for (uint64_t j = i; j < count && seen < sv->qubits; j++) {
+        const lyth_gate &h = gates[j];
+        const uint32_t qs[2] = {h.q0, h.q1};
+        const int nq = h.kind == LYTH_GATE_U ? 1 : 2;
+        for (int e = 0; e < nq; e++)
+            if (qs[e] < sv->qubits && next[qs[e]] == UINT64_MAX) {
+                next[qs[e]] = j;
+                seen++;
+            }
+    }
+    uint32_t victim = L - 1;
+    uint64_t best = 0;
+    bool any = false;
+    for (int b = (int)L - 1; b >= 0; b--) {
+        const uint64_t nu = next[sv->inv[b]];
+        if (!any || nu > best) {
+            best = nu;
+            victim = (uint32_t)b;
+            any = true;
+        }
+    }
+    sv->swaps_in++;
+    return physical_swap(sv, victim, gp);
+}
+
+int apply_one(lyth_sv *sv, const lyth_gate *gates, uint64_t count, uint64_t i) {
+    const lyth_gate &g = gates[i];
     const uint32_t L = sv->local_bits;
     if (g.q0 >= sv->qubits || (g.kind != LYTH_GATE_U && (g.q1 >= sv->qubits || g.q1 == g.q0))) return LYTH_E_INVALID;
     const U8 m = u8_of(g.m);
@@ -444,13 +528,22 @@ int apply_one(lyth_sv *sv, const lyth_gate &g) {
             return LYTH_OK;
         }
         case LYTH_GATE_U: {
-            const uint32_t p = sv->pos[g.q0];
+            uint32_t p = sv->pos[g.q0];
+            if (p >= L && sv->remap) {
+                int st = swap_in(sv, p, gates, count, i);
+                if (st) return st;
+                p = sv->pos[g.q0];
+            }
             if (p < L) return add_local(sv, -1, p, m);
             int st = flush_group(sv);
             if (st) return st;
             return exchange_gate(sv, p - L, m, -1);
         }
         case LYTH_GATE_CU: {
+            if (sv->pos[g.q1] >= L && sv->remap) {
+                int st = swap_in(sv, sv->pos[g.q1], gates, count, i);
+                if (st) return st;
+            }
             const uint32_t pc = sv->pos[g.q0], pt = sv->pos[g.q1];
             if (pc < L && pt < L) return add_local(sv, (int)pc, pt, m);
             if (pc >= L && !rank_bit(sv, pc - L)) return LYTH_OK;  // control 0 on this whole shard
@@ -471,6 +564,9 @@ void free_all(lyth_sv *sv) {
     for (int b = 0; b < 2; b++) {
         cudaFree(sv->rre[b]);
         cudaFree(sv->rim[b]);
+        cudaFree(sv->sre[b]);
+        cudaFree(sv->sim[b]);
+        if (sv->ev_packed[b]) cudaEventDestroy(sv->ev_packed[b]);
         if (sv->ev_recv[b]) cudaEventDestroy(sv->ev_recv[b]);
         if (sv->ev_done[b]) cudaEventDestroy(sv->ev_done[b]);
     }
@@ -531,7 +627,9 @@ int lyth_sv_create(lyth_sv **out, uint32_t qubits, int device, int rank, int nra
     if (nranks > 1) {
         for (int b = 0; b < 2; b++) {
             if (cudaMalloc(&sv->rre[b], sv->chunk * sizeof(float)) != cudaSuccess ||
-                cudaMalloc(&sv->rim[b], sv->chunk * sizeof(float)) != cudaSuccess) {
+                cudaMalloc(&sv->rim[b], sv->chunk * sizeof(float)) != cudaSuccess ||
+                cudaMalloc(&sv->sre[b], sv->chunk * sizeof(float)) != cudaSuccess ||
+                cudaMalloc(&sv->sim[b], sv->chunk * sizeof(float)) != cudaSuccess) {
                 cudaGetLastError();
                 return fail(LYTH_E_OOM);
             }
@@ -542,6 +640,7 @@ int lyth_sv_create(lyth_sv **out, uint32_t qubits, int device, int rank, int nra
     for (int b = 0; b < 2; b++) {
         if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_recv[b], cudaEventDisableTiming)))) return fail(st);
         if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_done[b], cudaEventDisableTiming)))) return fail(st);
+        if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_packed[b], cudaEventDisableTiming)))) return fail(st);
     }
     if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_start, cudaEventDisableTiming)))) return fail(st);
     if (nranks > 1) {
@@ -626,7 +725,7 @@ int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count) {
     if (!sv || (count && !gates)) return LYTH_E_INVALID;
     DeviceGuard guard(sv->device);
     for (uint64_t i = 0; i < count; i++) {
-        int st = apply_one(sv, gates[i]);
+        int st = apply_one(sv, gates, count, i);
         if (st) {
             sv->open.k = 0;
             sv->open.ngates = 0;
@@ -634,6 +733,12 @@ int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count) {
         }
     }
     return flush_group(sv);
+}
+
+int lyth_sv_set_remap(lyth_sv *sv, int on) {
+    if (!sv) return LYTH_E_INVALID;
+    sv->remap = on != 0;
+    return LYTH_OK;
 }
 
 int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits) {

@@ -102,6 +102,11 @@ class StateVector:
         """Fuse consecutive local gates touching at most max_qubits (1..5) bits; 1 = unfused."""
         check(lib.lyth_sv_set_fusion(self._h, max_qubits), "set_fusion")
 
+    def set_remap(self, on: bool) -> None:
+        """Rank-bit gates: swap the qubit into a local bit first (True, default) or exchange the
+        whole shard and compute this rank's row (False)."""
+        check(lib.lyth_sv_set_remap(self._h, int(on)), "set_remap")
+
     def timing(self) -> dict:
         """{class: (count, total ms)}: 'u' (1-qubit passes), 'cu' (2-qubit), 'exchange',
         'fused' (fused multi-gate passes)."""

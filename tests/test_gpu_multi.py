@@ -17,7 +17,7 @@ def _ngpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _worker(rank, nranks, q, case, nid, out_dir):
+def _worker(rank, nranks, q, case, nid, out_dir, remap=True):
     import sys
 
     sys.path.insert(0, ROOT)
@@ -33,6 +33,7 @@ def _worker(rank, nranks, q, case, nid, out_dir):
     L = (1 << q) // nranks
     lo, hi = rank * L, (rank + 1) * L
     with lb.StateVector(q, device=rank, rank=rank, nranks=nranks, nccl_id=nid) as sv:
+        sv.set_remap(remap)
         sv.set_local(np.ascontiguousarray(re0[lo:hi]), np.ascontiguousarray(im0[lo:hi]))
         sv.apply(gates)
         sv.sync()
@@ -62,14 +63,16 @@ def case_gates(case, q):
 
 
 @pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("remap", [True, False])
 @pytest.mark.parametrize("case", [0, 1, 2])
-def test_two_ranks_bit_exact(case, tmp_path):
+def test_two_ranks_bit_exact(case, remap, tmp_path):
     import lyth_b200 as lb
 
     nranks, q = 2, 18
     nid = lb.unique_id()
     ctx = torch.multiprocessing.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, nranks, q, case, nid, str(tmp_path))) for r in range(nranks)]
+    procs = [ctx.Process(target=_worker, args=(r, nranks, q, case, nid, str(tmp_path), remap))
+             for r in range(nranks)]
     for p in procs:
         p.start()
     for p in procs:
