@@ -448,9 +448,13 @@ def ours(a, dist: Dist) -> None:
     gates = cc.layered(q, total_layers, cc.Rng(cc.BENCH_SEED))
     per = len(gates) // total_layers
     layers = [gates_array(gates[i * per:(i + 1) * per]) for i in range(total_layers)]
+    # The warm-up layers and the timed layers each go to the engine as one gate list, as a user
+    # applies a circuit: the engine then sees the layers ahead when it picks which local qubit to
+    # trade for a rank-bit one. Per-step time is the timed region over the K layers.
+    warm_arr = gates_array(gates[:a.warmup * per])
+    timed_arr = gates_array(gates[a.warmup * per:])
     sv.init_random(cc.BENCH_SEED)
-    for i in range(a.warmup):
-        lb.check(lb.lib.lyth_sv_apply(sv._h, layers[i], per), "apply")
+    lb.check(lb.lib.lyth_sv_apply(sv._h, warm_arr, a.warmup * per), "apply")
     sv.sync()
     stream = torch.cuda.ExternalStream(sv.stream)
     clocks = Clocks(gpu_id_for(dist.local))
@@ -462,8 +466,7 @@ def ours(a, dist: Dist) -> None:
     clocks.start()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
-    for i in range(a.warmup, total_layers):
-        lb.check(lb.lib.lyth_sv_apply(sv._h, layers[i], per), "apply")
+    lb.check(lb.lib.lyth_sv_apply(sv._h, timed_arr, a.steps * per), "apply")
     t_end.record(stream)
     sv.sync()
     torch.cuda.synchronize()

@@ -521,8 +521,8 @@ uint64_t lyth_sv_launches(const lyth_sv *sv);
 #define LYTH_SV_T_EXCHANGE 2
 #define LYTH_SV_T_FUSED 3
 /* Fusion (lyth-circuit fuse, lib.rs:72-100; docs/ADR-0030): consecutive local gates touching at
- * most `max_qubits` (1..5) bits run as one pass with the same chains in circuit order, bit-exact
- * with the unfused passes. 1 = one pass per gate. The default is 5. */
+ * most `max_qubits` (1..6) bits run as one pass with the same chains in circuit order, bit-exact
+ * with the unfused passes. 1 = one pass per gate. The default is 6. */
 int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits);
 /* A gate on a qubit that currently lives on a rank bit: on = 1 (default) first swaps it with the
  * local qubit used furthest ahead in the gate list (half the shard crosses NVLink each way) and

@@ -5,7 +5,7 @@
 
 namespace lyth {
 
-constexpr int kFuseMaxQubits = 5;
+constexpr int kFuseMaxQubits = 6;
 constexpr int kFuseMaxGates = 48;
 
 // A gate inside a group: target level t, control level c (-1 for a plain U), levels index the

@@ -23,7 +23,7 @@ def as_tuples(gates):
     return out
 
 
-def run_engine(q, gates, re0, im0, fuse=5):
+def run_engine(q, gates, re0, im0, fuse=6):
     with lb.StateVector(q, device=0) as sv:
         sv.set_fusion(fuse)
         sv.set_local(re0, im0)
@@ -65,7 +65,7 @@ def test_fused_equals_unfused_at_every_k(cuda, case):
     re0, im0 = orc.random_state(200 + case, q)
     ur, ui, ust = run_engine(q, gates, re0, im0, fuse=1)
     passes = []
-    for k in range(2, 6):
+    for k in range(2, 7):
         fr, fi, fst = run_engine(q, gates, re0, im0, fuse=k)
         assert np.array_equal(bits(fr), bits(ur)), (name, k)
         assert np.array_equal(bits(fi), bits(ui)), (name, k)
