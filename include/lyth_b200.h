@@ -533,6 +533,39 @@ int lyth_sv_set_timing(lyth_sv *sv, int on);
 int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms);
 int lyth_sv_reset_timing(lyth_sv *sv);
 
+/* ---- plan recording (no counterpart in the reference; the host-side check of the sharded
+ * engine). A plan handle runs the same planner as lyth_sv_create's handle -- fusion, qubit map,
+ * swap-in victims, exchanges -- but holds no device memory, makes no CUDA or NCCL call, and
+ * appends each step it would run to a list instead. lyth_sv_apply, lyth_sv_set_fusion,
+ * lyth_sv_set_remap and lyth_sv_stats work on it; set_local / init_* only reset the qubit map;
+ * lyth_sv_get_local records the permutation steps that undo the map and copies nothing (re and
+ * im may be NULL). Replaying the steps on every rank's shard gives the engine's result. */
+#define LYTH_SV_FUSE_MAX_QUBITS 6
+#define LYTH_SV_FUSE_MAX_GATES 48
+#define LYTH_SV_OP_U 0           /* U on local bit a */
+#define LYTH_SV_OP_CU 1          /* CU, control local bit a, target local bit b */
+#define LYTH_SV_OP_FUSED 2       /* gates[0..ngates) in order on levels of bits[0..k) */
+#define LYTH_SV_OP_EXCHANGE 3    /* gate on rank bit a with the partner rank ^ (1 << a); control
+                                    local bit c (or -1); this rank keeps its row */
+#define LYTH_SV_OP_SWAP_LOCAL 4  /* swap local bits a, b */
+#define LYTH_SV_OP_SWAP_LR 5     /* swap local bit a with rank bit b (half the shard each way) */
+#define LYTH_SV_OP_SWAP_RR 6     /* swap rank bits a, b (whole shards, where the bits differ) */
+typedef struct lyth_sv_op {
+    int32_t kind;
+    int32_t a, b, c;
+    float m[8];                                /* U, CU, EXCHANGE */
+    int32_t k;                                 /* FUSED: levels */
+    uint32_t bits[LYTH_SV_FUSE_MAX_QUBITS];    /* FUSED: level -> local bit */
+    uint32_t ngates;                           /* FUSED */
+    int8_t gt[LYTH_SV_FUSE_MAX_GATES];         /* FUSED: target level of gate i */
+    int8_t gc[LYTH_SV_FUSE_MAX_GATES];         /* FUSED: control level of gate i, or -1 */
+    float gm[LYTH_SV_FUSE_MAX_GATES][8];       /* FUSED: matrix of gate i */
+} lyth_sv_op;
+int lyth_sv_plan_create(lyth_sv **out, uint32_t qubits, int rank, int nranks);
+uint64_t lyth_sv_plan_count(const lyth_sv *sv);
+int lyth_sv_plan_op(const lyth_sv *sv, uint64_t index, lyth_sv_op *out);
+int lyth_sv_plan_clear(lyth_sv *sv);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,18 @@ class Gate(C.Structure):
     _fields_ = [("kind", _u32), ("q0", _u32), ("q1", _u32), ("m", _f32 * 8)]
 
 
+SV_OP_U, SV_OP_CU, SV_OP_FUSED, SV_OP_EXCHANGE = 0, 1, 2, 3
+SV_OP_SWAP_LOCAL, SV_OP_SWAP_LR, SV_OP_SWAP_RR = 4, 5, 6
+
+
+class SvOp(C.Structure):
+    """``lyth_sv_op``: one step a plan handle recorded (include/lyth_b200.h)."""
+
+    _fields_ = [("kind", C.c_int32), ("a", C.c_int32), ("b", C.c_int32), ("c", C.c_int32),
+                ("m", _f32 * 8), ("k", C.c_int32), ("bits", _u32 * 6), ("ngates", _u32),
+                ("gt", C.c_int8 * 48), ("gc", C.c_int8 * 48), ("gm", (_f32 * 8) * 48)]
+
+
 def _sig(name, res, args):
     fn = getattr(lib, name)
     fn.restype = res
@@ -105,6 +117,10 @@ _sig("lyth_sv_timing", _i32, [_vp, _i32, C.POINTER(_u64), C.POINTER(C.c_double)]
 _sig("lyth_sv_reset_timing", _i32, [_vp])
 _sig("lyth_sv_set_fusion", _i32, [_vp, _i32])
 _sig("lyth_sv_set_remap", _i32, [_vp, _i32])
+_sig("lyth_sv_plan_create", _i32, [C.POINTER(_vp), _u32, _i32, _i32])
+_sig("lyth_sv_plan_count", _u64, [_vp])
+_sig("lyth_sv_plan_op", _i32, [_vp, _u64, C.POINTER(SvOp)])
+_sig("lyth_sv_plan_clear", _i32, [_vp])
 _sig("lyth_b200_device_error", _i32, [])
 
 
@@ -317,4 +333,4 @@ def swap(wc: int, wt: int, re, im, qr=None, qi=None, stream=None) -> None:
                              _ptr(qi, _f32t()), _stream(stream)), "swap_q")
 
 
-from .statevector import StateVector, unique_id  # noqa: E402,F401
+from .statevector import Plan, StateVector, unique_id  # noqa: E402,F401

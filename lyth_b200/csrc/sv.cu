@@ -190,7 +190,12 @@ struct lyth_sv {
     // exchange of the whole shard and compute this rank's row.
     int remap = 1;
     uint64_t swaps_in = 0;
+    // Plan handle (lyth_sv_plan_create): no device state; each step is appended here instead.
+    bool plan = false;
+    std::vector<lyth_sv_op> ops;
 };
+static_assert(kFuseMaxQubits == LYTH_SV_FUSE_MAX_QUBITS && kFuseMaxGates == LYTH_SV_FUSE_MAX_GATES,
+              "plan op layout");
 
 namespace {
 
@@ -206,6 +211,11 @@ struct DeviceGuard {
     explicit DeviceGuard(int dev) {
         if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
         cudaSetDevice(dev);
+    }
+    explicit DeviceGuard(const lyth_sv *sv) {
+        if (sv->plan) return;  // a plan handle makes no CUDA call
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        cudaSetDevice(sv->device);
     }
     ~DeviceGuard() {
         if (prev >= 0) cudaSetDevice(prev);
@@ -233,7 +243,7 @@ cudaEvent_t take_event(lyth_sv *sv) {
 
 // Opens a timed region of class `cls` on the compute stream (no-op when timing is off).
 int mark_begin(lyth_sv *sv, int cls) {
-    if (!sv->timing) return -1;
+    if (!sv->timing || sv->plan) return -1;
     sv->marks.push_back({cls, take_event(sv), take_event(sv)});
     cudaEventRecord(sv->marks.back().a, sv->stream);
     return (int)sv->marks.size() - 1;
@@ -259,11 +269,33 @@ int fold_timing(lyth_sv *sv) {
     return LYTH_OK;
 }
 
+lyth_sv_op &record(lyth_sv *sv, int kind, int a, int b, int c) {
+    sv->ops.emplace_back();
+    lyth_sv_op &op = sv->ops.back();
+    memset(&op, 0, sizeof op);
+    op.kind = kind;
+    op.a = a;
+    op.b = b;
+    op.c = c;
+    return op;
+}
+void set_m(lyth_sv_op &op, const U8 &m) {
+    const float v[8] = {m.ar, m.ai, m.br, m.bi, m.cr, m.ci, m.dr, m.di};
+    memcpy(op.m, v, sizeof v);
+}
+
 // The rank bit b of this rank.
 inline int rank_bit(const lyth_sv *sv, uint32_t b) { return (sv->rank >> b) & 1; }
 
 // A gate whose target is rank bit b: chunked pairwise exchange, then this rank's row.
 int exchange_gate(lyth_sv *sv, uint32_t b, const U8 &m, int ctrl_bit) {
+    if (sv->plan) {
+        set_m(record(sv, LYTH_SV_OP_EXCHANGE, (int)b, 0, ctrl_bit), m);
+        sv->bytes_sent += 2 * sv->local_len * sizeof(float);
+        sv->exchanges++;
+        sv->passes++;
+        return LYTH_OK;
+    }
     const int partner = sv->rank ^ (1 << b);
     const int side = rank_bit(sv, b);
     const int mk = mark_begin(sv, LYTH_SV_T_EXCHANGE);
@@ -303,6 +335,11 @@ int exchange_gate(lyth_sv *sv, uint32_t b, const U8 &m, int ctrl_bit) {
 
 // A local 1-qubit or 2-qubit pass, counted and (when on) timed.
 int local_u(lyth_sv *sv, uint32_t p, const U8 &m) {
+    if (sv->plan) {
+        set_m(record(sv, LYTH_SV_OP_U, (int)p, 0, 0), m);
+        sv->passes++;
+        return LYTH_OK;
+    }
     const int mk = mark_begin(sv, LYTH_SV_T_U);
     const int st = launch_u(sv->local_len, p, m, sv->re, sv->im, sv->re, sv->im, sv->stream);
     mark_end(sv, mk);
@@ -311,6 +348,11 @@ int local_u(lyth_sv *sv, uint32_t p, const U8 &m) {
     return st;
 }
 int local_cu(lyth_sv *sv, uint32_t pc, uint32_t pt, const U8 &m) {
+    if (sv->plan) {
+        set_m(record(sv, LYTH_SV_OP_CU, (int)pc, (int)pt, 0), m);
+        sv->passes++;
+        return LYTH_OK;
+    }
     const int mk = mark_begin(sv, LYTH_SV_T_CU);
     const int st = launch_cu(sv->local_len, pc, pt, m, sv->re, sv->im, sv->re, sv->im, sv->stream);
     mark_end(sv, mk);
@@ -345,11 +387,24 @@ int flush_group(lyth_sv *sv) {
                 g.sorted[j] = g.sorted[j - 1];
                 g.sorted[j - 1] = t;
             }
-        const int mk = mark_begin(sv, LYTH_SV_T_FUSED);
-        st = launch_fused(sv->local_len, g, sv->re, sv->im, sv->stream);
-        mark_end(sv, mk);
+        if (sv->plan) {
+            lyth_sv_op &op = record(sv, LYTH_SV_OP_FUSED, 0, 0, 0);
+            op.k = g.k;
+            for (int l = 0; l < g.k; l++) op.bits[l] = g.bits[l];
+            op.ngates = g.ngates;
+            for (uint32_t i = 0; i < g.ngates; i++) {
+                op.gt[i] = g.gates[i].t;
+                op.gc[i] = g.gates[i].c;
+                memcpy(op.gm[i], g.gates[i].m, sizeof op.gm[i]);
+            }
+            st = LYTH_OK;
+        } else {
+            const int mk = mark_begin(sv, LYTH_SV_T_FUSED);
+            st = launch_fused(sv->local_len, g, sv->re, sv->im, sv->stream);
+            mark_end(sv, mk);
+            sv->launches++;
+        }
         sv->passes++;
-        sv->launches++;
     }
     g.k = 0;
     g.ngates = 0;
@@ -382,9 +437,15 @@ int add_local(lyth_sv *sv, int c, uint32_t t, const U8 &m) {
 // over two streams: pack(c) -> send/recv(c) -> unpack(c), with pack(c+1) running while chunk c
 // is on the wire and the receive buffers double-buffered.
 int physical_swap_local_global(lyth_sv *sv, uint32_t lb, uint32_t gb) {
+    const uint64_t half = sv->local_len >> 1;
+    if (sv->plan) {
+        record(sv, LYTH_SV_OP_SWAP_LR, (int)lb, (int)gb, 0);
+        sv->bytes_sent += 2 * half * sizeof(float);
+        sv->exchanges++;
+        return LYTH_OK;
+    }
     const int partner = sv->rank ^ (1 << gb);
     const uint64_t v = (uint64_t)rank_bit(sv, gb) ^ 1ull;  // local bit value of what leaves and arrives
-    const uint64_t half = sv->local_len >> 1;
     const uint64_t nchunks = (half + sv->chunk - 1) / sv->chunk;
     int st = status_of(cudaEventRecord(sv->ev_start, sv->stream));
     if (st) return st;
@@ -432,6 +493,14 @@ int physical_swap_local_global(lyth_sv *sv, uint32_t lb, uint32_t gb) {
 // Physical swap of rank bits b1, b2: ranks whose two bits differ trade whole shards with the
 // rank that has them exchanged.
 int physical_swap_global_global(lyth_sv *sv, uint32_t b1, uint32_t b2) {
+    if (sv->plan) {
+        record(sv, LYTH_SV_OP_SWAP_RR, (int)b1, (int)b2, 0);
+        if (rank_bit(sv, b1) != rank_bit(sv, b2)) {
+            sv->bytes_sent += 2 * sv->local_len * sizeof(float);
+            sv->exchanges++;
+        }
+        return LYTH_OK;
+    }
     if (rank_bit(sv, b1) == rank_bit(sv, b2)) return LYTH_OK;
     const int partner = sv->rank ^ (1 << b1) ^ (1 << b2);
     int st = LYTH_OK;
@@ -458,7 +527,11 @@ int physical_swap(lyth_sv *sv, uint32_t p1, uint32_t p2) {
     if (p1 > p2) { uint32_t t = p1; p1 = p2; p2 = t; }
     const uint32_t L = sv->local_bits;
     int st;
-    if (p2 < L) {
+    if (p2 < L && sv->plan) {
+        record(sv, LYTH_SV_OP_SWAP_LOCAL, (int)p1, (int)p2, 0);
+        sv->passes++;
+        st = LYTH_OK;
+    } else if (p2 < L) {
         st = launch_swap(sv->local_len, p1, p2, sv->re, sv->im, sv->re, sv->im, sv->stream);
         sv->passes++;
         sv->launches++;
@@ -661,7 +734,11 @@ int lyth_sv_create(lyth_sv **out, uint32_t qubits, int device, int rank, int nra
 
 int lyth_sv_destroy(lyth_sv *sv) {
     if (!sv) return LYTH_OK;
-    DeviceGuard guard(sv->device);
+    if (sv->plan) {
+        delete sv;
+        return LYTH_OK;
+    }
+    DeviceGuard guard(sv);
     if (sv->stream) cudaStreamSynchronize(sv->stream);
     if (sv->comm_stream) cudaStreamSynchronize(sv->comm_stream);
     free_all(sv);
@@ -675,8 +752,9 @@ cudaStream_t lyth_sv_stream(const lyth_sv *sv) { return sv ? sv->stream : nullpt
 int lyth_sv_init_basis(lyth_sv *sv, uint64_t index) {
     if (!sv) return LYTH_E_INVALID;
     if (index >> sv->qubits) return LYTH_E_INVALID;
-    DeviceGuard guard(sv->device);
+    DeviceGuard guard(sv);
     reset_map(sv);
+    if (sv->plan) return LYTH_OK;
     int st;
     if ((st = status_of(cudaMemsetAsync(sv->re, 0, sv->local_len * 4, sv->stream)))) return st;
     if ((st = status_of(cudaMemsetAsync(sv->im, 0, sv->local_len * 4, sv->stream)))) return st;
@@ -689,8 +767,9 @@ int lyth_sv_init_basis(lyth_sv *sv, uint64_t index) {
 
 int lyth_sv_init_random(lyth_sv *sv, uint64_t seed) {
     if (!sv) return LYTH_E_INVALID;
-    DeviceGuard guard(sv->device);
+    DeviceGuard guard(sv);
     reset_map(sv);
+    if (sv->plan) return LYTH_OK;
     const uint64_t base = (uint64_t)sv->rank * sv->local_len;
     init_random_kernel<<<kInitBlocks, 256, 0, sv->stream>>>(sv->local_len, base, seed, sv->re, sv->im, sv->scratch);
     int st = last_launch_status();
@@ -706,8 +785,13 @@ int lyth_sv_init_random(lyth_sv *sv, uint64_t seed) {
 }
 
 int lyth_sv_set_local(lyth_sv *sv, const float *re, const float *im) {
-    if (!sv || !re || !im) return LYTH_E_INVALID;
-    DeviceGuard guard(sv->device);
+    if (!sv) return LYTH_E_INVALID;
+    if (sv->plan) {
+        reset_map(sv);
+        return LYTH_OK;
+    }
+    if (!re || !im) return LYTH_E_INVALID;
+    DeviceGuard guard(sv);
     reset_map(sv);
     int st;
     if ((st = status_of(cudaMemcpyAsync(sv->re, re, sv->local_len * 4, cudaMemcpyDefault, sv->stream)))) return st;
@@ -716,8 +800,10 @@ int lyth_sv_set_local(lyth_sv *sv, const float *re, const float *im) {
 }
 
 int lyth_sv_get_local(lyth_sv *sv, float *re, float *im) {
-    if (!sv || !re || !im) return LYTH_E_INVALID;
-    DeviceGuard guard(sv->device);
+    if (!sv) return LYTH_E_INVALID;
+    if (sv->plan) return normalize(sv);
+    if (!re || !im) return LYTH_E_INVALID;
+    DeviceGuard guard(sv);
     int st = normalize(sv);
     if (st) return st;
     if ((st = status_of(cudaMemcpyAsync(re, sv->re, sv->local_len * 4, cudaMemcpyDefault, sv->stream)))) return st;
@@ -727,7 +813,7 @@ int lyth_sv_get_local(lyth_sv *sv, float *re, float *im) {
 
 int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count) {
     if (!sv || (count && !gates)) return LYTH_E_INVALID;
-    DeviceGuard guard(sv->device);
+    DeviceGuard guard(sv);
     for (uint64_t i = 0; i < count; i++) {
         int st = apply_one(sv, gates, count, i);
         if (st) {
@@ -754,7 +840,8 @@ int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits) {
 
 int lyth_sv_sync(lyth_sv *sv) {
     if (!sv) return LYTH_E_INVALID;
-    DeviceGuard guard(sv->device);
+    if (sv->plan) return LYTH_OK;
+    DeviceGuard guard(sv);
     int st = status_of(cudaStreamSynchronize(sv->comm_stream));
     if (st) return st;
     return status_of(cudaStreamSynchronize(sv->stream));
@@ -770,7 +857,7 @@ int lyth_sv_set_timing(lyth_sv *sv, int on) {
 
 int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms) {
     if (!sv || cls < 0 || cls > 3) return LYTH_E_INVALID;
-    DeviceGuard guard(sv->device);
+    DeviceGuard guard(sv);
     int st = fold_timing(sv);
     if (st) return st;
     if (count) *count = sv->t_count[cls];
@@ -780,7 +867,7 @@ int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms) {
 
 int lyth_sv_reset_timing(lyth_sv *sv) {
     if (!sv) return LYTH_E_INVALID;
-    DeviceGuard guard(sv->device);
+    DeviceGuard guard(sv);
     int st = fold_timing(sv);
     for (int c = 0; c < 4; c++) { sv->t_count[c] = 0; sv->t_ms[c] = 0.0; }
     return st;
@@ -791,6 +878,42 @@ int lyth_sv_stats(const lyth_sv *sv, uint64_t *passes, uint64_t *exchanges, uint
     if (passes) *passes = sv->passes;
     if (exchanges) *exchanges = sv->exchanges;
     if (bytes_sent) *bytes_sent = sv->bytes_sent;
+    return LYTH_OK;
+}
+
+int lyth_sv_plan_create(lyth_sv **out, uint32_t qubits, int rank, int nranks) {
+    if (!out) return LYTH_E_INVALID;
+    *out = nullptr;
+    if (nranks < 1 || (nranks & (nranks - 1)) || rank < 0 || rank >= nranks) return LYTH_E_INVALID;
+    uint32_t g = 0;
+    while ((1 << g) < nranks) g++;
+    if (qubits < g + 2 || qubits > 40) return LYTH_E_INVALID;
+    lyth_sv *sv = new lyth_sv();
+    sv->plan = true;
+    sv->qubits = qubits;
+    sv->global_bits = g;
+    sv->local_bits = qubits - g;
+    sv->device = -1;
+    sv->rank = rank;
+    sv->nranks = nranks;
+    sv->local_len = 1ull << sv->local_bits;
+    sv->chunk = sv->local_len < kChunk ? sv->local_len : kChunk;
+    reset_map(sv);
+    *out = sv;
+    return LYTH_OK;
+}
+
+uint64_t lyth_sv_plan_count(const lyth_sv *sv) { return sv ? (uint64_t)sv->ops.size() : 0; }
+
+int lyth_sv_plan_op(const lyth_sv *sv, uint64_t index, lyth_sv_op *out) {
+    if (!sv || !out || !sv->plan || index >= sv->ops.size()) return LYTH_E_INVALID;
+    *out = sv->ops[index];
+    return LYTH_OK;
+}
+
+int lyth_sv_plan_clear(lyth_sv *sv) {
+    if (!sv || !sv->plan) return LYTH_E_INVALID;
+    sv->ops.clear();
     return LYTH_OK;
 }
 

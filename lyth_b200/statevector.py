@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes as C
 
-from . import GATE_CU, GATE_SWAP, GATE_U, Gate, check, lib
+from . import GATE_CU, GATE_SWAP, GATE_U, Gate, SvOp, check, lib
 from .circuit import CU, Swap, U, f32s
 
 
@@ -99,7 +99,7 @@ class StateVector:
         check(lib.lyth_sv_set_timing(self._h, int(on)), "set_timing")
 
     def set_fusion(self, max_qubits: int) -> None:
-        """Fuse consecutive local gates touching at most max_qubits (1..5) bits; 1 = unfused."""
+        """Fuse consecutive local gates touching at most max_qubits (1..6) bits; 1 = unfused."""
         check(lib.lyth_sv_set_fusion(self._h, max_qubits), "set_fusion")
 
     def set_remap(self, on: bool) -> None:
@@ -119,6 +119,81 @@ class StateVector:
 
     def reset_timing(self) -> None:
         check(lib.lyth_sv_reset_timing(self._h), "reset_timing")
+
+
+_OP_NAMES = ("u", "cu", "fused", "exchange", "swap_local", "swap_lr", "swap_rr")
+
+
+class Plan:
+    """A plan handle (lyth_sv_plan_create): the engine's planner for ``rank`` of ``nranks``, with
+    no device memory. ``apply`` and ``finish`` (the read-out's permutation steps) append the
+    steps the engine would run; ``ops`` returns them as dicts:
+
+    * ``u``: U on local bit ``a``, matrix ``m``; ``cu``: control ``a``, target ``b``;
+    * ``fused``: ``gates`` = [(target bit, control bit or -1, m), ...] in order;
+    * ``exchange``: the gate ``m`` on rank bit ``a`` (control local bit ``c`` or -1), with the
+      partner rank ^ (1 << a); this rank keeps its row;
+    * ``swap_local`` (bits a, b), ``swap_lr`` (local bit a, rank bit b), ``swap_rr`` (rank bits).
+    """
+
+    def __init__(self, qubits: int, rank: int = 0, nranks: int = 1):
+        h = C.c_void_p()
+        check(lib.lyth_sv_plan_create(C.byref(h), qubits, rank, nranks), "lyth_sv_plan_create")
+        self._h = h
+        self.qubits, self.rank, self.nranks = qubits, rank, nranks
+        self.local_len = int(lib.lyth_sv_local_len(h))
+
+    def close(self) -> None:
+        if self._h:
+            check(lib.lyth_sv_destroy(self._h), "lyth_sv_destroy")
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_fusion(self, max_qubits: int) -> None:
+        check(lib.lyth_sv_set_fusion(self._h, max_qubits), "set_fusion")
+
+    def set_remap(self, on: bool) -> None:
+        check(lib.lyth_sv_set_remap(self._h, int(on)), "set_remap")
+
+    def apply(self, gates) -> None:
+        arr = gates if isinstance(gates, C.Array) else gates_array(gates)
+        check(lib.lyth_sv_apply(self._h, arr, len(gates)), "apply")
+
+    def finish(self) -> None:
+        """Record the steps that undo the qubit map (what lyth_sv_get_local runs first)."""
+        check(lib.lyth_sv_get_local(self._h, None, None), "get_local")
+
+    def clear(self) -> None:
+        check(lib.lyth_sv_plan_clear(self._h), "plan_clear")
+
+    def stats(self) -> dict:
+        p, e, b = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        check(lib.lyth_sv_stats(self._h, C.byref(p), C.byref(e), C.byref(b)), "stats")
+        return {"passes": p.value, "exchanges": e.value, "bytes_sent": b.value}
+
+    def ops(self) -> list[dict]:
+        out = []
+        op = SvOp()
+        for i in range(int(lib.lyth_sv_plan_count(self._h))):
+            check(lib.lyth_sv_plan_op(self._h, i, C.byref(op)), "plan_op")
+            d = {"kind": _OP_NAMES[op.kind], "a": op.a, "b": op.b, "c": op.c, "m": tuple(op.m)}
+            if op.kind == 2:
+                bits = list(op.bits[: op.k])
+                d["gates"] = [(bits[op.gt[j]], bits[op.gc[j]] if op.gc[j] >= 0 else -1, tuple(op.gm[j]))
+                              for j in range(op.ngates)]
+            out.append(d)
+        return out
 
 
 def _addr(t) -> int:

@@ -1,0 +1,207 @@
+"""The multi-rank state vector's planner on CPU ranks (gloo): every rank records, through a plan
+handle (lyth_sv_plan_create), the exact steps its engine would run -- fused passes, swap-ins of
+rank-bit qubits, pairwise exchanges, the read-out's permutation steps -- and replays them on its
+own shard with the host evaluator's gates, trading shards with its partner over gloo where a
+step crosses ranks. Every rank's final shard must equal the unsharded evaluator's, bit for bit,
+and every pair of ranks must take the steps between them in the same order.
+
+This covers the sharding logic (the qubit map, victim choice, rank-bit controls, rank-rank
+swaps) without a GPU; the GPU tests check the kernels that run each step."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+COMM = ("exchange", "swap_lr", "swap_rr")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def circuits(q):
+    from lyth_b200 import circuit as cc
+
+    t = q - 1
+    aimed = [cc.U(t, cc.H), cc.CU(t, 0, cc.X), cc.CU(1, t, cc.zyz(0.3, 0.2, 0.1)), cc.Swap(0, t),
+             cc.U(t, cc.zyz(1.0, 2.0, 3.0)), cc.CU(t, t - 1, cc.phase(0.7)), cc.Swap(t - 1, 2),
+             cc.CU(t - 1, t, cc.zyz(-0.4, 0.9, 1.3)), cc.Swap(t, t - 1), cc.U(0, cc.H)]
+    return [
+        ("layered", cc.layered(q, 3, cc.Rng(cc.BENCH_SEED))),
+        ("random", cc.random(q, 12, cc.Rng(20_260_931))),
+        ("qft", cc.qft(q, cc.Rng(20_260_932))),
+        ("ghz", cc.ghz(q)),
+        ("rank-bit gates", aimed),
+    ]
+
+
+def _trade(mine, partner):
+    """Send this rank's (re, im) to `partner` and return the partner's."""
+    import torch.distributed as dist
+
+    out = torch.from_numpy(np.concatenate(mine))
+    back = torch.empty_like(out)
+    reqs = [dist.isend(out, partner), dist.irecv(back, partner)]
+    for r in reqs:
+        r.wait()
+    n = mine[0].size
+    b = back.numpy()
+    return np.ascontiguousarray(b[:n]), np.ascontiguousarray(b[n:])
+
+
+def _paired(rank, bit, re, im, partner_state, fn):
+    """Run `fn` on the 2L-amplitude sub-state (this shard, the partner's) ordered by rank bit
+    `bit`, and keep this rank's half."""
+    pr, pi = partner_state
+    low = not ((rank >> bit) & 1)
+    cr = np.concatenate([re, pr] if low else [pr, re])
+    ci = np.concatenate([im, pi] if low else [pi, im])
+    cr, ci = fn(cr, ci)
+    n = re.size
+    sl = slice(0, n) if low else slice(n, 2 * n)
+    return np.ascontiguousarray(cr[sl]), np.ascontiguousarray(ci[sl])
+
+
+def partner_of(op, rank):
+    """The rank a communication step trades with (this rank itself: no data moves)."""
+    if op["kind"] == "exchange":
+        return rank ^ (1 << op["a"])
+    if op["kind"] == "swap_lr":
+        return rank ^ (1 << op["b"])
+    if ((rank >> op["a"]) & 1) != ((rank >> op["b"]) & 1):
+        return rank ^ (1 << op["a"]) ^ (1 << op["b"])
+    return rank
+
+
+def pairs_agree(seqs):
+    """Each pair of ranks takes the steps between them in the same order. (Ranks whose
+    rank-bit control is 0 skip a controlled exchange together with their partner, so whole
+    sequences may differ between pairs.)"""
+    for r, seq in enumerate(seqs):
+        for p in range(len(seqs)):
+            if p != r and [e[:3] for e in seq if e[3] == p] != [e[:3] for e in seqs[p] if e[3] == r]:
+                return False
+    return True
+
+
+def replay(ops, rank, local_bits, re, im):
+    from oracle import oracle as orc
+
+    run = orc.run_gates
+    for op in ops:
+        k, a, b, c, m = op["kind"], op["a"], op["b"], op["c"], op["m"]
+        if k == "u":
+            re, im = run([(0, a, 0, m)], re, im)
+        elif k == "cu":
+            re, im = run([(1, a, b, m)], re, im)
+        elif k == "fused":
+            re, im = run([(0, t, 0, gm) if cb < 0 else (1, cb, t, gm) for t, cb, gm in op["gates"]], re, im)
+        elif k == "swap_local":
+            re, im = run([(2, a, b, [0.0] * 8)], re, im)
+        elif k == "exchange":
+            other = _trade((re, im), rank ^ (1 << a))
+            g = (0, local_bits, 0, m) if c < 0 else (1, c, local_bits, m)
+            re, im = _paired(rank, a, re, im, other, lambda x, y: run([g], x, y))
+        elif k == "swap_lr":
+            other = _trade((re, im), rank ^ (1 << b))
+            re, im = _paired(rank, b, re, im, other, lambda x, y: run([(2, a, local_bits, [0.0] * 8)], x, y))
+        elif k == "swap_rr":
+            if ((rank >> a) & 1) != ((rank >> b) & 1):
+                re, im = _trade((re, im), rank ^ (1 << a) ^ (1 << b))
+        else:
+            raise AssertionError(k)
+    return re, im
+
+
+def _worker(rank, nranks, q, port, out_dir):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    import torch.distributed as dist
+
+    from lyth_b200.statevector import Plan
+    from oracle import oracle as orc
+    from tests.test_gpu_statevector import as_tuples
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=nranks)
+    lines = []
+    try:
+        L = (1 << q) // nranks
+        local_bits = L.bit_length() - 1
+        lo, hi = rank * L, (rank + 1) * L
+        for ci, (name, gates) in enumerate(circuits(q)):
+            re0, im0 = orc.random_state(400 + ci, q)
+            want_r, want_i = orc.run_gates(as_tuples(gates), re0, im0)
+            for fuse in (6, 3, 1):
+                for remap in (True, False):
+                    with Plan(q, rank, nranks) as p:
+                        p.set_fusion(fuse)
+                        p.set_remap(remap)
+                        p.apply(gates)
+                        p.finish()
+                        ops, st = p.ops(), p.stats()
+                    comm = [(o["kind"], o["a"], o["b"], partner_of(o, rank)) for o in ops if o["kind"] in COMM]
+                    comm = [e for e in comm if e[3] != rank]
+                    seqs = [None] * nranks
+                    dist.all_gather_object(seqs, comm)
+                    same = pairs_agree(seqs)
+                    re, im = replay(ops, rank, local_bits, np.ascontiguousarray(re0[lo:hi]),
+                                    np.ascontiguousarray(im0[lo:hi]))
+                    ok = np.array_equal(re.view(np.uint32), want_r[lo:hi].view(np.uint32)) and \
+                        np.array_equal(im.view(np.uint32), want_i[lo:hi].view(np.uint32))
+                    lines.append(f"{name}|{fuse}|{int(remap)}|{int(ok)}|{int(same)}|{len(comm)}|{st['exchanges']}")
+    finally:
+        dist.destroy_process_group()
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write("\n".join(lines) + "\n")
+
+
+@pytest.mark.parametrize("nranks,q", [(2, 9), (4, 10)])
+def test_sharded_plan_replays_bit_exact(nranks, q, tmp_path):
+    port = _free_port()
+    ctx = torch.multiprocessing.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, nranks, q, port, str(tmp_path))) for r in range(nranks)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for r, p in enumerate(procs):
+        if p.is_alive():
+            p.kill()
+        assert p.exitcode == 0, f"rank {r} exit {p.exitcode}"
+    total_comm = 0
+    for r in range(nranks):
+        for line in open(tmp_path / f"r{r}.txt").read().splitlines():
+            name, fuse, remap, ok, same, ncomm, _ = line.split("|")
+            assert ok == "1", f"rank {r}: {name} fuse={fuse} remap={remap}: shard differs"
+            assert same == "1", f"{name} fuse={fuse} remap={remap}: a pair of ranks disagree on their steps"
+            total_comm += int(ncomm)
+    assert total_comm > 0
+
+
+def test_plan_handle_needs_no_gpu():
+    # A plan handle loads and plans with no CUDA device and no NCCL; the fused group limits hold.
+    from lyth_b200 import circuit as cc
+    from lyth_b200.statevector import Plan
+
+    gates = cc.layered(12, 2, cc.Rng(cc.BENCH_SEED))
+    for k in range(1, 7):
+        with Plan(12, 0, 1) as p:
+            p.set_fusion(k)
+            p.apply(gates)
+            ops = p.ops()
+        assert all(o["kind"] in ("u", "cu", "fused", "swap_local") for o in ops)
+        for o in ops:
+            if o["kind"] == "fused":
+                assert 2 <= len(o["gates"]) <= 48
+                assert len({b for t, c, _ in o["gates"] for b in (t, c) if b >= 0}) <= k
+        if k == 1:
+            assert not any(o["kind"] == "fused" for o in ops)
+        # gates run = gates given minus swaps (relabels)
+        run = sum(len(o["gates"]) if o["kind"] == "fused" else 1 for o in ops)
+        assert run == sum(not isinstance(g, cc.Swap) for g in gates)

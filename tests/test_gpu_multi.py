@@ -40,11 +40,17 @@ def _worker(rank, nranks, q, case, nid, out_dir, remap=True):
         gr, gi = np.empty(L, np.float32), np.empty(L, np.float32)
         sv.get_local(gr, gi)
         st = sv.stats()
+    with lb.Plan(q, rank, nranks) as plan:  # the same planner, recording only
+        plan.set_remap(remap)
+        plan.apply(gates)
+        plan.finish()
+        pst = plan.stats()
+    same_plan = all(pst[k] == st[k] for k in ("passes", "exchanges", "bytes_sent"))
     wr, wi = orc.run_gates(as_tuples(gates), re0, im0)
     ok = np.array_equal(gr.view(np.uint32), wr[lo:hi].view(np.uint32)) and \
         np.array_equal(gi.view(np.uint32), wi[lo:hi].view(np.uint32))
     with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
-        f.write(f"{int(ok)} {st['exchanges']} {st['bytes_sent']}\n")
+        f.write(f"{int(ok)} {st['exchanges']} {st['bytes_sent']} {int(same_plan)}\n")
     del suite
 
 
@@ -79,6 +85,7 @@ def test_two_ranks_bit_exact(case, remap, tmp_path):
         p.join(timeout=300)
     for r, p in enumerate(procs):
         assert p.exitcode == 0, f"rank {r} exit {p.exitcode}"
-        ok, ex, sent = open(tmp_path / f"r{r}.txt").read().split()
+        ok, ex, sent, same_plan = open(tmp_path / f"r{r}.txt").read().split()
         assert ok == "1", f"rank {r}: shard differs from the evaluator"
+        assert same_plan == "1", f"rank {r}: the plan handle's counters differ from the engine's"
         assert int(ex) > 0, "the circuit must exercise the exchange"
