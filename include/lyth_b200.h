@@ -507,6 +507,7 @@ int lyth_sv_set_local(lyth_sv *sv, const float *re, const float *im);
 int lyth_sv_get_local(lyth_sv *sv, float *re, float *im);
 /* Apply `count` gates in order. Returns when the work is queued on lyth_sv_stream. */
 int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count);
+/* Wait for the handle's streams; LYTH_E_TIMEOUT if a pass gave up one of its bounded waits. */
 int lyth_sv_sync(lyth_sv *sv);
 /* Counters since creation: data passes run, exchange steps run, bytes sent over NCCL. */
 int lyth_sv_stats(const lyth_sv *sv, uint64_t *passes, uint64_t *exchanges, uint64_t *bytes_sent);

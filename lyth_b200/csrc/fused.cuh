@@ -25,5 +25,7 @@ struct FusedGroup {
 };
 
 int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaStream_t s);
+// LYTH_E_TIMEOUT (and clears the flag) if a staged pass gave up a bounded wait; else LYTH_OK.
+int fused_take_device_error();
 
 }  // namespace lyth

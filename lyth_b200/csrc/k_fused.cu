@@ -25,7 +25,11 @@
 // level swaps the partner's values in with shuffles and each lane computes its own row (row 0
 // with p0 = own, p1 = partner; row 1 with p0 = partner, p1 = own): the same chains on the same
 // values. A CU controlled by the split level runs only on the h = 1 lanes.
+#include <stdlib.h>
+#include <string.h>
+
 #include "fused.cuh"
+#include "mbar.cuh"
 
 namespace lyth {
 
@@ -133,36 +137,42 @@ LYTH_D void dispatch_gate(int t, int c, const U8 &m, float2 (&X)[1 << (KL - 1)],
     }
 }
 
-// A gate on the split level (lane pairs): partner values by shuffle, own row computed.
-// CMASK: -1 no control; 0 control on level 0 (only .y); c >= 1 control on pair-index bit c-1.
+// A gate on a lane level (lanes l and l ^ lm hold the two values of the target): partner
+// values by shuffle, own row computed. h = this lane's target bit: h = 0 computes row 0 of
+// (p0 = own, p1 = partner), h = 1 row 1 of (p0 = partner, p1 = own). Both are the row-0 chain
+// with the row's coefficients and operands selected per lane, so there is no divergent branch.
+// CL: -1 no control; 0 control on level 0 (only .y); c >= 1 control on pair-index bit c-1.
+// `on` = false keeps this lane's values (a control on another lane bit that is 0 here); every
+// lane still shuffles.
 template <int KL, int CL>
-LYTH_D void split_gate(const U8 &m, int h, float2 (&X)[1 << (KL - 1)], float2 (&Y)[1 << (KL - 1)]) {
+LYTH_D void split_gate(const U8 &m, int h, int lm, bool on, float2 (&X)[1 << (KL - 1)],
+                       float2 (&Y)[1 << (KL - 1)]) {
+    const U8 r{h ? m.cr : m.ar, h ? m.ci : m.ai, h ? m.dr : m.br, h ? m.di : m.bi, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < (1 << (KL - 1)); i++) {
         float2 oX, oY;
-        oX.x = __shfl_xor_sync(0xffffffffu, X[i].x, 16);
-        oX.y = __shfl_xor_sync(0xffffffffu, X[i].y, 16);
-        oY.x = __shfl_xor_sync(0xffffffffu, Y[i].x, 16);
-        oY.y = __shfl_xor_sync(0xffffffffu, Y[i].y, 16);
+        oX.x = __shfl_xor_sync(0xffffffffu, X[i].x, lm);
+        oX.y = __shfl_xor_sync(0xffffffffu, X[i].y, lm);
+        oY.x = __shfl_xor_sync(0xffffffffu, Y[i].x, lm);
+        oY.y = __shfl_xor_sync(0xffffffffu, Y[i].y, lm);
         if (CL >= 1 && !(i & (1 << (CL - 1)))) continue;
         if (CL == 0) {
             float a, b;
-            if (h == 0) row0(m, X[i].y, Y[i].y, oX.y, oY.y, a, b);
-            else row1(m, oX.y, oY.y, X[i].y, Y[i].y, a, b);
-            X[i].y = a; Y[i].y = b;
+            row0(r, h ? oX.y : X[i].y, h ? oY.y : Y[i].y, h ? X[i].y : oX.y, h ? Y[i].y : oY.y, a, b);
+            if (on) { X[i].y = a; Y[i].y = b; }
         } else {
             float2 a, b;
-            if (h == 0) row0_2(m, X[i], Y[i], oX, oY, a, b);
-            else row1_2(m, oX, oY, X[i], Y[i], a, b);
-            X[i] = a; Y[i] = b;
+            row0_2(r, h ? oX : X[i], h ? oY : Y[i], h ? X[i] : oX, h ? Y[i] : oY, a, b);
+            if (on) { X[i] = a; Y[i] = b; }
         }
     }
 }
 template <int KL, int CL = -1>
-LYTH_D void dispatch_split(int c, const U8 &m, int h, float2 (&X)[1 << (KL - 1)], float2 (&Y)[1 << (KL - 1)]) {
+LYTH_D void dispatch_split(int c, const U8 &m, int h, int lm, bool on, float2 (&X)[1 << (KL - 1)],
+                           float2 (&Y)[1 << (KL - 1)]) {
     if constexpr (CL < KL) {
-        if (c == CL) split_gate<KL, CL>(m, h, X, Y);
-        else dispatch_split<KL, CL + 1>(c, m, h, X, Y);
+        if (c == CL) split_gate<KL, CL>(m, h, lm, on, X, Y);
+        else dispatch_split<KL, CL + 1>(c, m, h, lm, on, X, Y);
     }
 }
 
@@ -216,7 +226,7 @@ __global__ void __launch_bounds__(256, fused_min_blocks<K, SPLIT>())
             const FusedGate &fg = G.gates[g];
             const U8 m{fg.m[0], fg.m[1], fg.m[2], fg.m[3], fg.m[4], fg.m[5], fg.m[6], fg.m[7]};
             if (SPLIT && fg.t == K - 1) {
-                dispatch_split<KL>(fg.c, m, h, X, Y);
+                dispatch_split<KL>(fg.c, m, h, 16, true, X, Y);
             } else if (SPLIT && fg.c == K - 1) {
                 if (h) dispatch_gate<KL>(fg.t, -1, m, X, Y);
             } else {
@@ -273,7 +283,448 @@ static FusedGroup arrange_levels(const FusedGroup &g, bool split) {
     return o;
 }
 
+// ------------------------------------------------------------------ the staged pass
+// For states of 2^14 amplitudes and more. The register pass above loads a whole tuple, computes,
+// and stores, so at most its resident warps' loads are in flight: it streams well below HBM
+// speed, and a group on the low address bits makes every warp load touch 32 lines. The staged
+// pass moves the state through shared memory in tiles instead:
+//
+//  * a tile is 2^13 amplitudes whose indices differ in 13 "tile bits": 5 lane bits, 5 register
+//    levels and 3 warp bits. Lane bits are address bits 0..4, except that when all six group
+//    bits are >= 5 the highest one takes lane bit 4: every warp access is then 64 contiguous
+//    bytes or more per lane half. Register levels are the group's other bits, filled up to five
+//    with the lowest free bits ("batch" levels: independent tuples side by side). Warp bits are
+//    the next free bits.
+//  * one persistent CTA per SM: a producer warp copies each tile's contiguous runs (>= 1 KiB)
+//    into a 3-stage ring of shared memory with 1-D bulk copies (cp.async.bulk, no multicast)
+//    completing on an mbarrier; two groups of 8 consumer warps take alternate tiles, read their
+//    32 amplitudes per lane from shared memory, release the stage, run the gates in registers
+//    and store to global memory directly (coalesced, streaming stores). Up to three tiles
+//    (192 KiB) are in flight per SM whatever the consumers are doing.
+//  * with a group bit on lane bit 4, the runs whose copy of that bit is 1 sit 16 words further
+//    along modulo 32 (a 32-word pad after every two runs, that bit the lowest run-index bit),
+//    so the two lane halves read disjoint banks.
+//  * gates on register levels run the packed chains above; a gate on a lane bit fetches both
+//    values of each pair from the two lanes by indexed shuffles and computes this lane's row.
+//    The arithmetic per amplitude is the same chain in the same order, so the result is
+//    bit-identical.
+constexpr int kStTileBits = 13;
+constexpr int kStTile = 1 << kStTileBits;            // amplitudes per tile
+constexpr int kStRegs = 5;                           // register levels: 32 amplitudes per lane
+constexpr int kStWarpBits = kStTileBits - 5 - kStRegs;
+constexpr int kStGroupWarps = 1 << kStWarpBits;      // consumer warps per tile
+constexpr int kStGroups = 2;                         // consumer groups, alternate tiles
+constexpr int kStStages = 3;
+constexpr int kStConsumers = kStGroups * kStGroupWarps;
+constexpr int kStThreads = kStConsumers * 32;      // no separate producer warp
+constexpr int kStMaxRuns = 32;
+constexpr int kStCompWords = kStTile + 32 * (kStMaxRuns / 2);  // one component of a stage, padded
+constexpr size_t kStBufBytes = (size_t)kStStages * 2 * kStCompWords * sizeof(float);
+constexpr size_t kStSmem = kStBufBytes + (kStGroups + 1) * kStStages * sizeof(uint64_t) +
+                          2 * kStGroups * kStStages * sizeof(uint32_t);
+constexpr uint32_t kStMinBits = 14;                  // local bits from which the staged pass runs
+
+// A gate of the staged pass. case_: target register level t and control register level c
+// (or -1) as t * 8 + c + 1; 64 + c + 1 for a target on lane bit `lt`. lc: a control on a lane
+// bit, or -1.
+struct StagedGate {
+    int16_t case_;
+    int8_t lt, lc;
+    float m[8];
+};
+
+struct StagedPlan {
+    uint32_t tile_bits[kStTileBits];  // the tile's address bits, ascending (for the tile base)
+    uint32_t run_bits;                // a run is address bits 0..run_bits-1: 2^run_bits amplitudes
+    uint32_t nruns;
+    uint32_t lane_w[5], reg_w[kStRegs], warp_w[kStWarpBits];  // shared-memory word weights
+    uint32_t lane_addr[5], reg_addr[kStRegs], warp_addr[kStWarpBits];
+    uint32_t run_word[kStMaxRuns];  // shared-memory word of run r
+    uint64_t run_off[kStMaxRuns];   // element offset of run r within a tile
+    uint64_t ntiles;
+    uint32_t ngates;
+    StagedGate gates[kFuseMaxGates];
+};
+
+__device__ int g_fused_error;
+
+LYTH_D uint64_t st_tile_base(const StagedPlan &P, uint64_t tile) {
+    uint64_t b = tile;
+#pragma unroll
+    for (int k = 0; k < kStTileBits; k++) b = insert_bit(b, P.tile_bits[k], 0);
+    return b;
+}
+
+// A gate on a lane bit: lane `lo` holds the pair's p0 and lane `hi` its p1 (lo = this lane with
+// the bit clear, hi = with it set); r = this lane's row coefficients in row-0 form. CL as in
+// split_gate. Pairs a register control excludes neither shuffle nor compute.
+template <int KL, int CL>
+LYTH_D void lane_gate(const U8 &r, int lo, int hi, bool on, float2 (&X)[1 << (KL - 1)], float2 (&Y)[1 << (KL - 1)]) {
+#pragma unroll
+    for (int i = 0; i < (1 << (KL - 1)); i++) {
+        if (CL >= 1 && !(i & (1 << (CL - 1)))) continue;
+        if (CL == 0) {
+            const float p0r = __shfl_sync(0xffffffffu, X[i].y, lo), p0i = __shfl_sync(0xffffffffu, Y[i].y, lo);
+            const float p1r = __shfl_sync(0xffffffffu, X[i].y, hi), p1i = __shfl_sync(0xffffffffu, Y[i].y, hi);
+            float a, b;
+            row0(r, p0r, p0i, p1r, p1i, a, b);
+            if (on) { X[i].y = a; Y[i].y = b; }
+        } else {
+            float2 p0r, p0i, p1r, p1i;
+            p0r.x = __shfl_sync(0xffffffffu, X[i].x, lo); p0r.y = __shfl_sync(0xffffffffu, X[i].y, lo);
+            p0i.x = __shfl_sync(0xffffffffu, Y[i].x, lo); p0i.y = __shfl_sync(0xffffffffu, Y[i].y, lo);
+            p1r.x = __shfl_sync(0xffffffffu, X[i].x, hi); p1r.y = __shfl_sync(0xffffffffu, X[i].y, hi);
+            p1i.x = __shfl_sync(0xffffffffu, Y[i].x, hi); p1i.y = __shfl_sync(0xffffffffu, Y[i].y, hi);
+            float2 a, b;
+            row0_2(r, p0r, p0i, p1r, p1i, a, b);
+            if (on) { X[i] = a; Y[i] = b; }
+        }
+    }
+}
+
+#define LYTH_ST_REG(T, C) \
+    case (T) * 8 + (C) + 1: gate_case<kStRegs, T, C>(m, X, Y); break;
+#define LYTH_ST_REG_T(T) \
+    LYTH_ST_REG(T, -1) LYTH_ST_C0(T) LYTH_ST_C1(T) LYTH_ST_C2(T) LYTH_ST_C3(T) LYTH_ST_C4(T)
+#define LYTH_ST_C0(T) LYTH_ST_IF(T, 0)
+#define LYTH_ST_C1(T) LYTH_ST_IF(T, 1)
+#define LYTH_ST_C2(T) LYTH_ST_IF(T, 2)
+#define LYTH_ST_C3(T) LYTH_ST_IF(T, 3)
+#define LYTH_ST_C4(T) LYTH_ST_IF(T, 4)
+// (T, C) with C == T never occurs; its label maps to no work
+#define LYTH_ST_IF(T, C) \
+    case (T) * 8 + (C) + 1: if constexpr ((T) != (C)) gate_case<kStRegs, T, ((T) != (C) ? (C) : -1)>(m, X, Y); break;
+#define LYTH_ST_LANE(C) \
+    case 64 + (C) + 1: lane_gate<kStRegs, C>(r, lo, hi, on, X, Y); break;
+
+// Issue tile `t`'s bulk copies into stage `stage` (the whole warp: lane 0 arms the barrier with
+// the tile's byte count, every lane issues its share of the runs).
+LYTH_D void st_issue(const StagedPlan &P, uint64_t t, float *sre, float *sim, uint32_t bar, const float *re,
+                     const float *im, int lane) {
+    if (lane == 0) mbar_expect_tx(bar, 2u * kStTile * (uint32_t)sizeof(float));
+    __syncwarp();
+    const uint32_t run_bytes = (1u << P.run_bits) * (uint32_t)sizeof(float);
+    const uint64_t base = st_tile_base(P, t);
+    for (uint32_t r = lane; r < P.nruns; r += 32) {
+        const uint64_t g = base + P.run_off[r];
+        bulk_load(smem_u32(sre + P.run_word[r]), re + g, run_bytes, bar);
+        bulk_load(smem_u32(sim + P.run_word[r]), im + g, run_bytes, bar);
+    }
+}
+
+__global__ void __launch_bounds__(kStThreads, 1)
+    staged_fused_kernel(const __grid_constant__ StagedPlan P, float *re, float *im) {
+    constexpr int NP = 1 << (kStRegs - 1);  // float2 pairs per lane
+    extern __shared__ __align__(128) uint8_t st_smem[];
+    float *buf = reinterpret_cast<float *>(st_smem);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(st_smem + kStBufBytes);
+    // Tiles of this CTA: t_j = blockIdx.x + j * gridDim.x. Tile j lives in stage j % 3 and is
+    // consumed by group j % 2; warp 0 of that group issues tile j + 3 into the same stage once
+    // all its warps have read tile j (the stage's `empty` barrier). A tile's arrival is signalled
+    // on the barrier of its (stage, group): a group consumes the uses of its barriers in order,
+    // so it never waits more than one phase ahead of one it has seen complete, however far the
+    // two groups drift apart.
+    auto full = [&](uint64_t j) { return smem_u32(bars + (j % kStStages) * kStGroups + (j % kStGroups)); };
+    auto full_parity = [&](uint64_t j) { return (uint32_t)(j / (kStStages * kStGroups)) & 1u; };
+    auto empty = [&](uint32_t s) { return smem_u32(bars + kStGroups * kStStages + s); };
+    auto sre_of = [&](uint32_t s) { return buf + (size_t)s * 2 * kStCompWords; };
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = warp / kStGroupWarps, wid = warp % kStGroupWarps;
+    const uint64_t ntiles = P.ntiles > blockIdx.x ? (P.ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    // Uses of each full barrier armed and consumed, for the wind-down: every use up to the last
+    // has completed except possibly the last armed one, so its parity is unambiguous.
+    constexpr int NB = kStStages * kStGroups;
+    uint32_t *n_armed = reinterpret_cast<uint32_t *>(bars + (kStGroups + 1) * kStStages);
+    uint32_t *n_used = n_armed + NB;
+    auto bar_of = [&](uint64_t j) { return (uint32_t)((j % kStStages) * kStGroups + (j % kStGroups)); };
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int b = 0; b < NB; b++) {
+                mbar_init(smem_u32(bars + b), 1);
+                n_armed[b] = 0;
+                n_used[b] = 0;
+            }
+            for (int s = 0; s < kStStages; s++) mbar_init(empty(s), kStGroupWarps);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncwarp();
+        for (uint32_t j = 0; j < (uint32_t)kStStages && j < ntiles; j++) {
+            st_issue(P, blockIdx.x + (uint64_t)j * gridDim.x, sre_of(j), sre_of(j) + kStCompWords, full(j), re, im, lane);
+            if (lane == 0) n_armed[bar_of(j)]++;
+        }
+    }
+    __syncthreads();
+
+    uint32_t lane_s = 0, warp_s = 0;
+    uint64_t lane_g = 0, warp_g = 0;
+#pragma unroll
+    for (int b = 0; b < 5; b++)
+        if ((lane >> b) & 1) { lane_s += P.lane_w[b]; lane_g += 1ull << P.lane_addr[b]; }
+#pragma unroll
+    for (int b = 0; b < kStWarpBits; b++)
+        if ((wid >> b) & 1) { warp_s += P.warp_w[b]; warp_g += 1ull << P.warp_addr[b]; }
+    for (uint64_t j = grp; j < ntiles; j += kStGroups) {
+        const uint64_t t = blockIdx.x + j * gridDim.x;
+        const uint32_t stage = (uint32_t)(j % kStStages), phase = (uint32_t)(j / kStStages) & 1u;
+        const bool ok = mbar_wait(full(j), full_parity(j), &g_fused_error);
+        if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform: the gates below shuffle
+        if (wid == 0 && lane == 0) n_used[bar_of(j)]++;
+        const float *sre = sre_of(stage);
+        const float *sim = sre + kStCompWords;
+        uint32_t ss[kStRegs];
+#pragma unroll
+        for (int l = 0; l < kStRegs; l++) {
+            ss[l] = P.reg_w[l];
+            asm volatile("" : "+r"(ss[l]));
+        }
+        float2 X[NP], Y[NP];
+#pragma unroll
+        for (int i = 0; i < NP; i++) {
+            uint32_t o = lane_s + warp_s;
+#pragma unroll
+            for (int l = 1; l < kStRegs; l++)
+                if (i & (1 << (l - 1))) o += ss[l];
+            X[i] = make_float2(sre[o], sre[o + ss[0]]);
+            Y[i] = make_float2(sim[o], sim[o + ss[0]]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty(stage));  // release: the reads above are ordered before
+        if (wid == 0 && j + kStStages < ntiles) {
+            // refill: wait until the whole group has read this stage, then issue tile j + 3
+            const bool free_ok = mbar_wait(empty(stage), phase, &g_fused_error);
+            if (!__all_sync(0xffffffffu, free_ok)) break;
+            st_issue(P, t + (uint64_t)kStStages * gridDim.x, sre_of(stage), sre_of(stage) + kStCompWords,
+                     full(j + kStStages), re, im, lane);
+            if (lane == 0) n_armed[bar_of(j + kStStages)]++;
+        }
+
+        for (uint32_t g = 0; g < P.ngates; g++) {
+            const StagedGate &sg = P.gates[g];
+            const U8 m{sg.m[0], sg.m[1], sg.m[2], sg.m[3], sg.m[4], sg.m[5], sg.m[6], sg.m[7]};
+            const bool on = sg.lc < 0 || ((lane >> sg.lc) & 1);
+            if (sg.case_ < 64) {
+                if (!on) continue;
+                switch (sg.case_) {
+                    LYTH_ST_REG_T(0) LYTH_ST_REG_T(1) LYTH_ST_REG_T(2) LYTH_ST_REG_T(3) LYTH_ST_REG_T(4)
+                    default: break;
+                }
+            } else {
+                const int h = (lane >> sg.lt) & 1;
+                const int lo = lane & ~(1 << sg.lt), hi = lane | (1 << sg.lt);
+                const U8 r{h ? m.cr : m.ar, h ? m.ci : m.ai, h ? m.dr : m.br, h ? m.di : m.bi, 0.f, 0.f, 0.f, 0.f};
+                switch (sg.case_) {
+                    LYTH_ST_LANE(-1) LYTH_ST_LANE(0) LYTH_ST_LANE(1) LYTH_ST_LANE(2) LYTH_ST_LANE(3) LYTH_ST_LANE(4)
+                    default: break;
+                }
+            }
+        }
+
+        uint64_t gs[kStRegs];
+#pragma unroll
+        for (int l = 0; l < kStRegs; l++) {
+            gs[l] = 1ull << P.reg_addr[l];
+            asm volatile("" : "+l"(gs[l]));
+        }
+        const uint64_t base = st_tile_base(P, t) + lane_g + warp_g;
+#pragma unroll
+        for (int i = 0; i < NP; i++) {
+            uint64_t a = base;
+#pragma unroll
+            for (int l = 1; l < kStRegs; l++)
+                if (i & (1 << (l - 1))) a += gs[l];
+            __stcs(re + a, X[i].x);
+            __stcs(re + a + gs[0], X[i].y);
+            __stcs(im + a, Y[i].x);
+            __stcs(im + a + gs[0], Y[i].y);
+        }
+    }
+    // Every armed tile has landed before the block may leave. Normally each was consumed; after
+    // a timed-out wait, one use per barrier may be outstanding (bounded wait for it).
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int b = 0; b < NB; b++)
+            if (n_armed[b] != n_used[b]) mbar_wait(smem_u32(bars + b), (n_armed[b] - 1u) & 1u, &g_fused_error);
+}
+#undef LYTH_ST_REG
+#undef LYTH_ST_REG_T
+#undef LYTH_ST_C0
+#undef LYTH_ST_C1
+#undef LYTH_ST_C2
+#undef LYTH_ST_C3
+#undef LYTH_ST_C4
+#undef LYTH_ST_IF
+#undef LYTH_ST_LANE
+
+// The staged layout of a group over L local bits (false: the register pass runs instead).
+static bool plan_staged(const FusedGroup &g, uint32_t L, StagedPlan &P) {
+    if (L < kStMinBits || g.k < 1 || g.k > kFuseMaxQubits) return false;
+    const int k = g.k;
+    int use[kFuseMaxQubits] = {0};
+    for (uint32_t i = 0; i < g.ngates; i++) {
+        use[g.gates[i].t]++;
+        if (g.gates[i].c >= 0) use[g.gates[i].c]++;
+    }
+    bool group[64] = {false};
+    for (int l = 0; l < k; l++) group[g.bits[l]] = true;
+    int code[kFuseMaxQubits];  // group level -> kernel level (0..4 register, 5 + b lane bit b)
+    for (int l = 0; l < k; l++) code[l] = g.bits[l] < 5 ? 5 + (int)g.bits[l] : -1;
+    // a sixth group bit >= 5 goes to lane bit 4: the highest one (it splits the fewest runs)
+    int nhi = 0, top_l = -1;
+    for (int l = 0; l < k; l++)
+        if (g.bits[l] >= 5) {
+            nhi++;
+            if (top_l < 0 || g.bits[l] > g.bits[top_l]) top_l = l;
+        }
+    const int nstar = nhi > kStRegs ? 1 : 0;
+    uint32_t lane_addr[5] = {0, 1, 2, 3, 4};
+    bool star[64] = {false};
+    if (nstar) {
+        lane_addr[4] = g.bits[top_l];
+        code[top_l] = 5 + 4;
+        star[g.bits[top_l]] = true;
+    }
+    bool used[64] = {false};
+    for (int b = 0; b < 5; b++) used[lane_addr[b]] = true;
+    auto next_free = [&]() -> uint32_t {
+        for (uint32_t b = 0; b < 64; b++)
+            if (!used[b] && !group[b]) { used[b] = true; return b; }
+        return 64;
+    };
+    // register levels: level 0 a batch bit when there is one (no gate touches it, so every gate
+    // runs on packed pairs), else the group bit used least
+    int regs_l[kStRegs], nreg = 0;
+    for (int l = 0; l < k; l++)
+        if (code[l] < 0) regs_l[nreg++] = l;
+    uint32_t reg_addr[kStRegs];
+    int r = 0;
+    if (nreg < kStRegs) {
+        reg_addr[r++] = next_free();
+    } else {
+        int best = 0;
+        for (int i = 1; i < nreg; i++)
+            if (use[regs_l[i]] < use[regs_l[best]]) best = i;
+        const int t = regs_l[0]; regs_l[0] = regs_l[best]; regs_l[best] = t;
+    }
+    for (int i = 0; i < nreg; i++) {
+        code[regs_l[i]] = r;
+        reg_addr[r++] = g.bits[regs_l[i]];
+        used[g.bits[regs_l[i]]] = true;
+    }
+    while (r < kStRegs) reg_addr[r++] = next_free();
+    uint32_t warp_addr[kStWarpBits];
+    for (int b = 0; b < kStWarpBits; b++) warp_addr[b] = next_free();
+
+    uint32_t all[kStTileBits];
+    int n = 0;
+    for (int b = 0; b < 5; b++) all[n++] = lane_addr[b];
+    for (int b = 0; b < kStRegs; b++) all[n++] = reg_addr[b];
+    for (int b = 0; b < kStWarpBits; b++) all[n++] = warp_addr[b];
+    for (int i = 0; i < n; i++)
+        if (all[i] >= L) return false;
+    for (int i = 1; i < n; i++)
+        for (int j = i; j > 0 && all[j - 1] > all[j]; j--) { const uint32_t t = all[j]; all[j] = all[j - 1]; all[j - 1] = t; }
+    for (int i = 1; i < n; i++)
+        if (all[i] == all[i - 1]) return false;
+    bool tile[64] = {false};
+    for (int i = 0; i < n; i++) tile[all[i]] = true;
+    // runs: address bits 0..m-1, all tile bits and none the lane group bit
+    uint32_t m = 0;
+    while (m < 64 && tile[m] && !star[m]) m++;
+    // run-index bits: the lane group bit first, then the other tile bits above the run
+    uint32_t ridx[kStTileBits];
+    int nr = 0;
+    if (nstar) ridx[nr++] = lane_addr[4];
+    for (int i = 0; i < n; i++)
+        if (all[i] >= m && !star[all[i]]) ridx[nr++] = all[i];
+    if (m < 8 || (1 << nr) > kStMaxRuns || (uint32_t)nr + m != (uint32_t)kStTileBits) return false;
+    const uint32_t RL = 1u << m;
+    const uint32_t gstride = nstar ? 2 * RL + 32u : RL, jstride = RL + 16u;
+    uint32_t weight[64] = {0};  // shared-memory word weight of each tile bit
+    for (uint32_t b = 0; b < m; b++) weight[b] = 1u << b;
+    for (int q = 0; q < nr; q++)
+        weight[ridx[q]] = q < nstar ? jstride : (1u << (q - nstar)) * gstride;
+    memset(&P, 0, sizeof P);
+    for (int i = 0; i < n; i++) P.tile_bits[i] = all[i];
+    P.run_bits = m;
+    P.nruns = 1u << nr;
+    uint32_t top = 0;
+    for (uint32_t run = 0; run < P.nruns; run++) {
+        uint64_t off = 0;
+        uint32_t w = 0;
+        for (int q = 0; q < nr; q++)
+            if ((run >> q) & 1) { off += 1ull << ridx[q]; w += weight[ridx[q]]; }
+        P.run_off[run] = off;
+        P.run_word[run] = w;
+        if (w + RL > top) top = w + RL;
+    }
+    if (top > (uint32_t)kStCompWords) return false;
+    for (int b = 0; b < 5; b++) { P.lane_addr[b] = lane_addr[b]; P.lane_w[b] = weight[lane_addr[b]]; }
+    for (int b = 0; b < kStRegs; b++) { P.reg_addr[b] = reg_addr[b]; P.reg_w[b] = weight[reg_addr[b]]; }
+    for (int b = 0; b < kStWarpBits; b++) { P.warp_addr[b] = warp_addr[b]; P.warp_w[b] = weight[warp_addr[b]]; }
+    P.ntiles = 1ull << (L - kStTileBits);
+    P.ngates = g.ngates;
+    for (uint32_t i = 0; i < g.ngates; i++) {
+        const FusedGate &fg = g.gates[i];
+        StagedGate &sg = P.gates[i];
+        const int t = code[fg.t], c = fg.c >= 0 ? code[fg.c] : -1;
+        const int creg = c >= 0 && c < kStRegs ? c : -1;
+        sg.lc = (int8_t)(c >= kStRegs ? c - 5 : -1);
+        if (t < kStRegs) {
+            sg.case_ = (int16_t)(t * 8 + creg + 1);
+            sg.lt = -1;
+        } else {
+            sg.case_ = (int16_t)(64 + creg + 1);
+            sg.lt = (int8_t)(t - 5);
+        }
+        memcpy(sg.m, fg.m, sizeof sg.m);
+    }
+    return true;
+}
+
+static int launch_staged(const StagedPlan &P, float *re, float *im, cudaStream_t s) {
+    static bool attr_done[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return LYTH_E_INVALID;
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(staged_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStSmem);
+        if (e != cudaSuccess) return status_of(e);
+        attr_done[dev] = true;
+    }
+    const uint64_t sms = (uint64_t)device_sms();
+    const unsigned grid = (unsigned)(P.ntiles < sms ? P.ntiles : sms);
+    staged_fused_kernel<<<grid, kStThreads, kStSmem, s>>>(P, re, im);
+    return last_launch_status();
+}
+
+int fused_take_device_error() {
+    int v = 0;
+    const cudaError_t e = cudaMemcpyFromSymbol(&v, g_fused_error, sizeof(int));
+    if (e != cudaSuccess) return status_of(e);
+    if (v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_fused_error, &zero, sizeof(int));
+        return LYTH_E_TIMEOUT;
+    }
+    return LYTH_OK;
+}
+
+static bool staging_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char *v = getenv("LYTH_FUSED_STAGING");
+        on = !(v && v[0] == '0');
+    }
+    return on == 1;
+}
+
 int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaStream_t s) {
+    if (staging_enabled() && len && !(len & (len - 1)) && !(((uintptr_t)re | (uintptr_t)im) & 15)) {
+        uint32_t L = 0;
+        while ((1ull << L) < len) L++;
+        StagedPlan P;
+        if (plan_staged(g, L, P)) return launch_staged(P, re, im, s);
+    }
     const bool split = g.k >= 5;
     const FusedGroup o = arrange_levels(g, split);
     const uint64_t threads = split ? (len >> g.k) * 2 : (len >> g.k);

@@ -20,7 +20,8 @@
 // lyth_b200_device_error) and the kernel winds down instead of hanging.
 #include <cuda.h>
 
-#include "common.cuh"
+#include "fused.cuh"
+#include "mbar.cuh"
 
 namespace lyth {
 
@@ -31,8 +32,6 @@ constexpr int MM_B_BYTES = MM_BN * MM_BK * 2;               // 32 KiB
 constexpr int MM_STAGE_BYTES = MM_A_BYTES + MM_B_BYTES;     // 48 KiB
 constexpr int MM_TMEM_COLS = 2 * MM_BN;                     // two f32 accumulators
 constexpr int MM_THREADS = 192;
-constexpr uint32_t MM_WAIT_LIMIT = 1u << 24;                 // try_wait polls before giving up
-constexpr uint64_t MM_WAIT_NS = 2000000000ull;               // or 2 s of wall time, whichever first
 constexpr size_t MM_SMEM = 1024 + (size_t)MM_STAGES * MM_STAGE_BYTES + 256;
 
 __device__ int g_device_error;
@@ -43,47 +42,8 @@ __device__ int g_device_error;
 constexpr uint32_t MM_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) |
                               ((uint32_t)(MM_BN >> 3) << 17) | ((uint32_t)(MM_BM >> 4) << 24);
 
-LYTH_D uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-LYTH_D void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-LYTH_D uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Wait for the phase of parity `parity` to complete. Bounded twice: by a poll count and by
-// wall time (MM_WAIT_NS of the global timer), since one try_wait may itself suspend for an
-// implementation-defined interval. On the limit: set the error flag and return false.
-LYTH_D bool mbar_wait(uint32_t bar, uint32_t parity) {
-    uint64_t t0 = 0;
-    for (uint32_t i = 0; i < MM_WAIT_LIMIT; ++i) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if ((i & 255u) == 0) {
-            const uint64_t t = global_ns();
-            if (i == 0) t0 = t;
-            else if (t - t0 > MM_WAIT_NS) break;
-        }
-    }
-    atomicExch(&g_device_error, 1);
-    return false;
-}
-LYTH_D void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-LYTH_D void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
+// Bounded mbarrier wait (mbar.cuh) reporting to this kernel's error flag.
+LYTH_D bool mm_wait(uint32_t bar, uint32_t parity) { return mbar_wait(bar, parity, &g_device_error); }
 LYTH_D void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -176,7 +136,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             for (uint32_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
                 const int m0 = (int)((tile % tiles_m) * MM_BM), n0 = (int)((tile / tiles_m) * MM_BN);
                 for (uint32_t kb = 0; kb < kblocks; kb++) {
-                    if (!mbar_wait(empty(stage), phase ^ 1)) { ok = false; break; }
+                    if (!mm_wait(empty(stage), phase ^ 1)) { ok = false; break; }
                     mbar_expect_tx(full(stage), MM_STAGE_BYTES);
                     const int k0 = (int)(kb * MM_BK);
                     tma_load_2d(smem_u32(sA + stage * MM_A_BYTES), &tmA, k0, m0, full(stage));
@@ -192,7 +152,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             // bounded chance to land before the block leaves.
             if (!ok) {
                 for (int s = 0; s < MM_STAGES; s++) {
-                    mbar_wait(full(stage), phase);
+                    mm_wait(full(stage), phase);
                     if (++stage == MM_STAGES) { stage = 0; phase ^= 1; }
                 }
             }
@@ -203,11 +163,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             bool ok = true;
             for (uint32_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, local++) {
                 const uint32_t ab = local & 1, aphase = (local >> 1) & 1;
-                if (!mbar_wait(tempty(ab), aphase ^ 1)) break;
+                if (!mm_wait(tempty(ab), aphase ^ 1)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + ab * MM_BN;
                 for (uint32_t kb = 0; kb < kblocks; kb++) {
-                    if (!mbar_wait(full(stage), phase)) { ok = false; break; }
+                    if (!mm_wait(full(stage), phase)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_base = smem_u32(sA + stage * MM_A_BYTES);
                     const uint32_t b_base = smem_u32(sB + stage * MM_B_BYTES);
@@ -231,7 +191,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         uint32_t local = 0;
         for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, local++) {
             const uint32_t ab = local & 1, aphase = (local >> 1) & 1;
-            if (!mbar_wait(tfull(ab), aphase)) break;
+            if (!mm_wait(tfull(ab), aphase)) break;
             tc_fence_after();
             const uint32_t m0 = (tile % tiles_m) * MM_BM, n0 = (tile / tiles_m) * MM_BN;
             const uint32_t row = m0 + quad * 32 + lane;
@@ -324,6 +284,8 @@ extern "C" int lyth_b200_matmul_bf16(uint32_t m, uint32_t n, uint32_t k, const u
 }
 
 extern "C" int lyth_b200_device_error(void) {
+    const int fused = fused_take_device_error();
+    if (fused != LYTH_OK) return fused;
     int v = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
     if (e != cudaSuccess) return status_of(e);

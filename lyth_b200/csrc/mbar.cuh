@@ -1,0 +1,65 @@
+// mbarrier and bulk-copy helpers shared by the TMA-fed kernels (inline PTX, sm_100a).
+//
+// Every wait is bounded twice -- by a poll count and by wall time on the global timer, since
+// one try_wait may itself suspend for an implementation-defined interval -- and a wait that
+// runs out sets the caller's device error flag and returns false, so a kernel winds down
+// instead of hanging. No copy here uses cluster multicast.
+#pragma once
+
+#include "common.cuh"
+
+namespace lyth {
+
+constexpr uint32_t kWaitPolls = 1u << 24;        // try_wait polls before giving up
+constexpr uint64_t kWaitNs = 2000000000ull;      // or 2 s of wall time, whichever first
+
+LYTH_D uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+LYTH_D void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+LYTH_D uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for the phase of parity `parity` to complete; on the limit set *err and return false.
+LYTH_D bool mbar_wait(uint32_t bar, uint32_t parity, int *err) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((i & 255u) == 0) {
+            const uint64_t t = global_ns();
+            if (i == 0) t0 = t;
+            else if (t - t0 > kWaitNs) break;
+        }
+    }
+    atomicExch(err, 1);
+    return false;
+}
+LYTH_D void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+LYTH_D void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completion counted in bytes on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+LYTH_D void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"((uint64_t)src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+}  // namespace lyth

@@ -844,7 +844,8 @@ int lyth_sv_sync(lyth_sv *sv) {
     DeviceGuard guard(sv);
     int st = status_of(cudaStreamSynchronize(sv->comm_stream));
     if (st) return st;
-    return status_of(cudaStreamSynchronize(sv->stream));
+    if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
+    return fused_take_device_error();  // a staged pass that gave up a bounded wait
 }
 
 uint64_t lyth_sv_launches(const lyth_sv *sv) { return sv ? sv->launches : 0; }

@@ -109,3 +109,49 @@ def test_unitarity_physics_check(cuda):
     re0, im0 = orc.random_state(5, q)
     gr, gi, _ = run_engine(q, gates, re0, im0)
     assert np.max(np.abs(gr - re0)) < 1e-6 and np.max(np.abs(gi - im0)) < 1e-6
+
+
+def on_bits(bits, n, rng):
+    """n random U / CU gates whose qubits all lie in `bits` (so fusion makes one group of them)."""
+    g = []
+    for _ in range(n):
+        t = bits[rng.below(len(bits))]
+        m = cc.zyz(rng.angle(), rng.angle(), rng.angle())
+        if len(bits) > 1 and rng.below(3):
+            c = bits[rng.below(len(bits))]
+            while c == t:
+                c = bits[rng.below(len(bits))]
+            g.append(cc.CU(c, t, m))
+        else:
+            g.append(cc.U(t, m))
+    return g
+
+
+# The staged pass (2^14 amplitudes and more) places group bits below 5 on lanes (shuffle gates),
+# the rest in registers, and with six bits all >= 5 one of them on lane bit 4; controls on lane
+# bits and on register levels in every combination.
+STAGED_BITS = [
+    (0, 1, 2, 3, 4, 5), (10, 11, 12, 13, 14, 15), (5, 6, 7, 8, 9, 10), (1, 3, 7, 9, 12, 14),
+    (0, 5, 6, 7, 8, 9), (2, 3, 4), (4, 13), (0,), (15,), (3, 4, 5, 6, 7),
+]
+
+
+@pytest.mark.parametrize("bits_", STAGED_BITS, ids=[",".join(map(str, b)) for b in STAGED_BITS])
+def test_staged_groups_bit_exact(cuda, bits_):
+    q = 16
+    gates = on_bits(bits_, 40, cc.Rng(hash(bits_) & 0xFFFF))
+    re0, im0 = orc.random_state(500 + len(bits_), q)
+    wr, wi = orc.run_gates(as_tuples(gates), re0, im0)
+    gr, gi, st = run_engine(q, gates, re0, im0)
+    assert np.array_equal(bits(gr), bits(wr)) and np.array_equal(bits(gi), bits(wi))
+    assert st["passes"] == 1  # one fused group
+
+
+def test_staged_ring_wraps_bit_exact(cuda):
+    # 2^24 amplitudes: 2^11 tiles over at most 148 CTAs, so every CTA's 3-stage ring wraps.
+    q = 24
+    gates = cc.layered(q, 1, cc.Rng(cc.BENCH_SEED)) + on_bits((0, 1, 2, 20, 21, 22), 30, cc.Rng(9))
+    re0, im0 = orc.random_state(600, q)
+    wr, wi = orc.run_gates(as_tuples(gates), re0, im0)
+    gr, gi, _ = run_engine(q, gates, re0, im0)
+    assert np.array_equal(bits(gr), bits(wr)) and np.array_equal(bits(gi), bits(wi))
