@@ -295,12 +295,14 @@ static FusedGroup arrange_levels(const FusedGroup &g, bool split) {
 //    bytes or more per lane half. Register levels are the group's other bits, filled up to five
 //    with the lowest free bits ("batch" levels: independent tuples side by side). Warp bits are
 //    the next free bits.
-//  * one persistent CTA per SM: a producer warp copies each tile's contiguous runs (>= 1 KiB)
-//    into a 3-stage ring of shared memory with 1-D bulk copies (cp.async.bulk, no multicast)
-//    completing on an mbarrier; two groups of 8 consumer warps take alternate tiles, read their
-//    32 amplitudes per lane from shared memory, release the stage, run the gates in registers
-//    and store to global memory directly (coalesced, streaming stores). Up to three tiles
-//    (192 KiB) are in flight per SM whatever the consumers are doing.
+//  * one persistent CTA per SM, 16 warps in two groups of 8 that take alternate tiles. A tile's
+//    contiguous runs (>= 512 B) are copied into a 3-stage ring of shared memory with 1-D bulk
+//    copies (cp.async.bulk, no multicast) completing on an mbarrier; each warp reads its 32
+//    amplitudes per lane from shared memory and releases the stage, and warp 0 of the group,
+//    once its whole group has read the stage, issues the tile three ahead into it. The gates
+//    then run in registers and the results go to global memory directly (coalesced streaming
+//    stores). Up to three tiles (192 KiB) are in flight per SM whatever the warps are doing,
+//    and no warp is set aside for copies (16 warps x 128 registers fill the register file).
 //  * with a group bit on lane bit 4, the runs whose copy of that bit is 1 sit 16 words further
 //    along modulo 32 (a 32-word pad after every two runs, that bit the lowest run-index bit),
 //    so the two lane halves read disjoint banks.
@@ -317,7 +319,7 @@ constexpr int kStGroups = 2;                         // consumer groups, alterna
 constexpr int kStStages = 3;
 constexpr int kStConsumers = kStGroups * kStGroupWarps;
 constexpr int kStThreads = kStConsumers * 32;      // no separate producer warp
-constexpr int kStMaxRuns = 32;
+constexpr int kStMaxRuns = 64;
 constexpr int kStCompWords = kStTile + 32 * (kStMaxRuns / 2);  // one component of a stage, padded
 constexpr size_t kStBufBytes = (size_t)kStStages * 2 * kStCompWords * sizeof(float);
 constexpr size_t kStSmem = kStBufBytes + (kStGroups + 1) * kStStages * sizeof(uint64_t) +
@@ -340,6 +342,13 @@ struct StagedPlan {
     uint32_t lane_w[5], reg_w[kStRegs], warp_w[kStWarpBits];  // shared-memory word weights
     uint32_t lane_addr[5], reg_addr[kStRegs], warp_addr[kStWarpBits];
     uint32_t run_word[kStMaxRuns];  // shared-memory word of run r
+    // Box copies (tma = 1): dimension k of the tensor maps covers address bits
+    // [dim_lo[k], dim_lo[k] + dim_len[k]) and its box the lowest dim_box[k] of them; nbox boxes
+    // per component, box b at word b * box_words with the address bits box_off[b] set.
+    uint32_t tma;
+    uint32_t dim_lo[5], dim_len[5], dim_box[5];
+    uint32_t nbox, box_words;
+    uint64_t box_off[8];
     uint64_t run_off[kStMaxRuns];   // element offset of run r within a tile
     uint64_t ntiles;
     uint32_t ngates;
@@ -399,12 +408,24 @@ LYTH_D void lane_gate(const U8 &r, int lo, int hi, bool on, float2 (&X)[1 << (KL
 
 // Issue tile `t`'s bulk copies into stage `stage` (the whole warp: lane 0 arms the barrier with
 // the tile's byte count, every lane issues its share of the runs).
-LYTH_D void st_issue(const StagedPlan &P, uint64_t t, float *sre, float *sim, uint32_t bar, const float *re,
-                     const float *im, int lane) {
+LYTH_D void st_issue(const StagedPlan &P, const CUtensorMap *tre, const CUtensorMap *tim, uint64_t t, float *sre,
+                     float *sim, uint32_t bar, const float *re, const float *im, int lane) {
     if (lane == 0) mbar_expect_tx(bar, 2u * kStTile * (uint32_t)sizeof(float));
     __syncwarp();
-    const uint32_t run_bytes = (1u << P.run_bits) * (uint32_t)sizeof(float);
     const uint64_t base = st_tile_base(P, t);
+    if (P.tma) {
+        if ((uint32_t)lane < P.nbox) {
+            const uint64_t a = base + P.box_off[lane];
+            int c[5];
+#pragma unroll
+            for (int k = 0; k < 5; k++) c[k] = (int)((a >> P.dim_lo[k]) & ((1ull << P.dim_len[k]) - 1));
+            const uint32_t w = (uint32_t)lane * P.box_words;
+            tensor_load_5d(smem_u32(sre + w), tre, c[0], c[1], c[2], c[3], c[4], bar);
+            tensor_load_5d(smem_u32(sim + w), tim, c[0], c[1], c[2], c[3], c[4], bar);
+        }
+        return;
+    }
+    const uint32_t run_bytes = (1u << P.run_bits) * (uint32_t)sizeof(float);
     for (uint32_t r = lane; r < P.nruns; r += 32) {
         const uint64_t g = base + P.run_off[r];
         bulk_load(smem_u32(sre + P.run_word[r]), re + g, run_bytes, bar);
@@ -413,7 +434,8 @@ LYTH_D void st_issue(const StagedPlan &P, uint64_t t, float *sre, float *sim, ui
 }
 
 __global__ void __launch_bounds__(kStThreads, 1)
-    staged_fused_kernel(const __grid_constant__ StagedPlan P, float *re, float *im) {
+    staged_fused_kernel(const __grid_constant__ StagedPlan P, const __grid_constant__ CUtensorMap tre,
+                        const __grid_constant__ CUtensorMap tim, float *re, float *im) {
     constexpr int NP = 1 << (kStRegs - 1);  // float2 pairs per lane
     extern __shared__ __align__(128) uint8_t st_smem[];
     float *buf = reinterpret_cast<float *>(st_smem);
@@ -449,7 +471,8 @@ __global__ void __launch_bounds__(kStThreads, 1)
         }
         __syncwarp();
         for (uint32_t j = 0; j < (uint32_t)kStStages && j < ntiles; j++) {
-            st_issue(P, blockIdx.x + (uint64_t)j * gridDim.x, sre_of(j), sre_of(j) + kStCompWords, full(j), re, im, lane);
+            st_issue(P, &tre, &tim, blockIdx.x + (uint64_t)j * gridDim.x, sre_of(j), sre_of(j) + kStCompWords, full(j),
+                     re, im, lane);
             if (lane == 0) n_armed[bar_of(j)]++;
         }
     }
@@ -493,7 +516,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
             // refill: wait until the whole group has read this stage, then issue tile j + 3
             const bool free_ok = mbar_wait(empty(stage), phase, &g_fused_error);
             if (!__all_sync(0xffffffffu, free_ok)) break;
-            st_issue(P, t + (uint64_t)kStStages * gridDim.x, sre_of(stage), sre_of(stage) + kStCompWords,
+            st_issue(P, &tre, &tim, t + (uint64_t)kStStages * gridDim.x, sre_of(stage), sre_of(stage) + kStCompWords,
                      full(j + kStStages), re, im, lane);
             if (lane == 0) n_armed[bar_of(j + kStStages)]++;
         }
@@ -556,7 +579,70 @@ __global__ void __launch_bounds__(kStThreads, 1)
 #undef LYTH_ST_LANE
 
 // The staged layout of a group over L local bits (false: the register pass runs instead).
-static bool plan_staged(const FusedGroup &g, uint32_t L, StagedPlan &P) {
+// Box layout of the tile bits (tensor-map copies): dimension 0 = address bits 0..3 (with a lane
+// group bit) or the contiguous tile bits from 0, then the lane group bit (so the two lane halves
+// sit 16 words apart), then each further range of consecutive tile bits; beyond five dimensions
+// the smallest ranges are iterated as separate boxes (at most 8). Fills weight[] (word weight of
+// each tile bit) and the plan's dim / box fields; false when the tile does not fit the form.
+static bool layout_boxes(const bool *tile, int star, uint32_t L, uint32_t *weight, StagedPlan &P) {
+    struct Dim { uint32_t lo, box; };
+    Dim d[kStTileBits];
+    int nd = 0;
+    bool placed[64] = {false};
+    uint32_t b0 = 0;
+    if (star >= 0) b0 = 4;
+    else while (b0 < 8 && tile[b0]) b0++;
+    for (uint32_t b = 0; b < b0; b++) if (!tile[b]) return false;
+    d[nd++] = {0, b0};
+    for (uint32_t b = 0; b < b0; b++) placed[b] = true;
+    if (star >= 0) { d[nd++] = {(uint32_t)star, 1}; placed[star] = true; }
+    for (uint32_t b = 0; b < 64; b++) {
+        if (!tile[b] || placed[b]) continue;
+        uint32_t e = b;
+        while (e < 64 && tile[e] && !placed[e] && e - b < 8) e++;
+        d[nd++] = {b, e - b};
+        for (uint32_t x = b; x < e; x++) placed[x] = true;
+    }
+    uint32_t iter[3];
+    int ni = 0;
+    while (nd > 5) {  // iterate the smallest range (ties: the highest), never dimension 0 or the star
+        int pick = -1;
+        for (int k = (star >= 0 ? 2 : 1); k < nd; k++)
+            if (pick < 0 || d[k].box < d[pick].box || (d[k].box == d[pick].box && d[k].lo > d[pick].lo)) pick = k;
+        if (ni + (int)d[pick].box > 3) return false;
+        for (uint32_t i = 0; i < d[pick].box; i++) iter[ni++] = d[pick].lo + i;
+        for (int k = pick; k + 1 < nd; k++) d[k] = d[k + 1];
+        nd--;
+    }
+    // coverage: from each dimension's first bit to the next dimension's first bit in address order
+    for (int k = 0; k < nd; k++) {
+        uint32_t hi = L;
+        for (int q = 0; q < nd; q++)
+            if (d[q].lo > d[k].lo && d[q].lo < hi) hi = d[q].lo;
+        if (hi - d[k].lo < d[k].box || hi - d[k].lo > 31) return false;
+        P.dim_lo[k] = d[k].lo;
+        P.dim_len[k] = hi - d[k].lo;
+        P.dim_box[k] = d[k].box;
+    }
+    if (d[0].box < 2) return false;  // the inner box must span >= 16 bytes
+    for (int k = nd; k < 5; k++) { P.dim_lo[k] = 0; P.dim_len[k] = 0; P.dim_box[k] = 0; }
+    uint32_t w = 1;
+    for (int k = 0; k < nd; k++)
+        for (uint32_t i = 0; i < d[k].box; i++) { weight[d[k].lo + i] = w; w <<= 1; }
+    P.box_words = w;
+    P.nbox = 1u << ni;
+    for (int i = 0; i < ni; i++) weight[iter[i]] = w << i;
+    for (uint32_t bx = 0; bx < P.nbox; bx++) {
+        uint64_t off = 0;
+        for (int i = 0; i < ni; i++)
+            if ((bx >> i) & 1) off += 1ull << iter[i];
+        P.box_off[bx] = off;
+    }
+    P.tma = 1;
+    return true;
+}
+
+static bool plan_staged(const FusedGroup &g, uint32_t L, bool boxes, StagedPlan &P) {
     if (L < kStMinBits || g.k < 1 || g.k > kFuseMaxQubits) return false;
     const int k = g.k;
     int use[kFuseMaxQubits] = {0};
@@ -627,37 +713,45 @@ static bool plan_staged(const FusedGroup &g, uint32_t L, StagedPlan &P) {
         if (all[i] == all[i - 1]) return false;
     bool tile[64] = {false};
     for (int i = 0; i < n; i++) tile[all[i]] = true;
-    // runs: address bits 0..m-1, all tile bits and none the lane group bit
-    uint32_t m = 0;
-    while (m < 64 && tile[m] && !star[m]) m++;
-    // run-index bits: the lane group bit first, then the other tile bits above the run
-    uint32_t ridx[kStTileBits];
-    int nr = 0;
-    if (nstar) ridx[nr++] = lane_addr[4];
-    for (int i = 0; i < n; i++)
-        if (all[i] >= m && !star[all[i]]) ridx[nr++] = all[i];
-    if (m < 8 || (1 << nr) > kStMaxRuns || (uint32_t)nr + m != (uint32_t)kStTileBits) return false;
-    const uint32_t RL = 1u << m;
-    const uint32_t gstride = nstar ? 2 * RL + 32u : RL, jstride = RL + 16u;
-    uint32_t weight[64] = {0};  // shared-memory word weight of each tile bit
-    for (uint32_t b = 0; b < m; b++) weight[b] = 1u << b;
-    for (int q = 0; q < nr; q++)
-        weight[ridx[q]] = q < nstar ? jstride : (1u << (q - nstar)) * gstride;
     memset(&P, 0, sizeof P);
     for (int i = 0; i < n; i++) P.tile_bits[i] = all[i];
-    P.run_bits = m;
-    P.nruns = 1u << nr;
-    uint32_t top = 0;
-    for (uint32_t run = 0; run < P.nruns; run++) {
-        uint64_t off = 0;
-        uint32_t w = 0;
+    uint32_t weight[64] = {0};  // shared-memory word weight of each tile bit
+    // Runs of >= 2 KiB copy fastest as plain bulk copies; shorter ones (a tile of many small
+    // runs) as tensor-map boxes, one or a few per component.
+    uint32_t m_runs = 0;
+    while (m_runs < 64 && tile[m_runs] && !star[m_runs]) m_runs++;
+    if (m_runs >= 9) boxes = false;
+    if (!(boxes && layout_boxes(tile, nstar ? (int)lane_addr[4] : -1, L, weight, P))) {
+        // runs: address bits 0..m-1, all tile bits and none the lane group bit
+        P.tma = 0;
+        uint32_t m = 0;
+        while (m < 64 && tile[m] && !star[m]) m++;
+        // run-index bits: the lane group bit first, then the other tile bits above the run
+        uint32_t ridx[kStTileBits];
+        int nr = 0;
+        if (nstar) ridx[nr++] = lane_addr[4];
+        for (int i = 0; i < n; i++)
+            if (all[i] >= m && !star[all[i]]) ridx[nr++] = all[i];
+        if (m < 7 || (1 << nr) > kStMaxRuns || (uint32_t)nr + m != (uint32_t)kStTileBits) return false;
+        const uint32_t RL = 1u << m;
+        const uint32_t gstride = nstar ? 2 * RL + 32u : RL, jstride = RL + 16u;
+        for (uint32_t b = 0; b < m; b++) weight[b] = 1u << b;
         for (int q = 0; q < nr; q++)
-            if ((run >> q) & 1) { off += 1ull << ridx[q]; w += weight[ridx[q]]; }
-        P.run_off[run] = off;
-        P.run_word[run] = w;
-        if (w + RL > top) top = w + RL;
+            weight[ridx[q]] = q < nstar ? jstride : (1u << (q - nstar)) * gstride;
+        P.run_bits = m;
+        P.nruns = 1u << nr;
+        uint32_t top = 0;
+        for (uint32_t run = 0; run < P.nruns; run++) {
+            uint64_t off = 0;
+            uint32_t w = 0;
+            for (int q = 0; q < nr; q++)
+                if ((run >> q) & 1) { off += 1ull << ridx[q]; w += weight[ridx[q]]; }
+            P.run_off[run] = off;
+            P.run_word[run] = w;
+            if (w + RL > top) top = w + RL;
+        }
+        if (top > (uint32_t)kStCompWords) return false;
     }
-    if (top > (uint32_t)kStCompWords) return false;
     for (int b = 0; b < 5; b++) { P.lane_addr[b] = lane_addr[b]; P.lane_w[b] = weight[lane_addr[b]]; }
     for (int b = 0; b < kStRegs; b++) { P.reg_addr[b] = reg_addr[b]; P.reg_w[b] = weight[reg_addr[b]]; }
     for (int b = 0; b < kStWarpBits; b++) { P.warp_addr[b] = warp_addr[b]; P.warp_w[b] = weight[warp_addr[b]]; }
@@ -681,7 +775,29 @@ static bool plan_staged(const FusedGroup &g, uint32_t L, StagedPlan &P) {
     return true;
 }
 
-static int launch_staged(const StagedPlan &P, float *re, float *im, cudaStream_t s) {
+// The two tensor maps of a box plan (re and im over 2^L f32 amplitudes). Unused dimensions have
+// extent 1.
+static bool encode_boxes(const StagedPlan &P, uint32_t L, float *re, float *im, CUtensorMap &tre, CUtensorMap &tim) {
+    PFN_encode_tiled enc = tensor_map_encoder();
+    if (!enc) return false;
+    cuuint64_t dims[5], strides[4];
+    cuuint32_t box[5], estr[5] = {1, 1, 1, 1, 1};
+    for (int k = 0; k < 5; k++) {
+        const bool used = P.dim_len[k] > 0;
+        dims[k] = used ? (1ull << P.dim_len[k]) : 1;
+        box[k] = used ? (1u << P.dim_box[k]) : 1;
+        if (k > 0) strides[k - 1] = used ? (1ull << P.dim_lo[k]) * sizeof(float) : (1ull << L) * sizeof(float);
+    }
+    auto one = [&](CUtensorMap &map, float *base) {
+        return enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    return one(tre, re) && one(tim, im);
+}
+
+static int launch_staged(const StagedPlan &P, const CUtensorMap &tre, const CUtensorMap &tim, float *re, float *im,
+                         cudaStream_t s) {
     static bool attr_done[64] = {false};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return LYTH_E_INVALID;
@@ -693,7 +809,7 @@ static int launch_staged(const StagedPlan &P, float *re, float *im, cudaStream_t
     }
     const uint64_t sms = (uint64_t)device_sms();
     const unsigned grid = (unsigned)(P.ntiles < sms ? P.ntiles : sms);
-    staged_fused_kernel<<<grid, kStThreads, kStSmem, s>>>(P, re, im);
+    staged_fused_kernel<<<grid, kStThreads, kStSmem, s>>>(P, tre, tim, re, im);
     return last_launch_status();
 }
 
@@ -723,7 +839,12 @@ int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaSt
         uint32_t L = 0;
         while ((1ull << L) < len) L++;
         StagedPlan P;
-        if (plan_staged(g, L, P)) return launch_staged(P, re, im, s);
+        CUtensorMap tre, tim;
+        memset(&tre, 0, sizeof tre);
+        memset(&tim, 0, sizeof tim);
+        bool ok = plan_staged(g, L, true, P);
+        if (ok && P.tma && !encode_boxes(P, L, re, im, tre, tim)) ok = plan_staged(g, L, false, P);  // runs instead
+        if (ok) return launch_staged(P, tre, tim, re, im, s);
     }
     const bool split = g.k >= 5;
     const FusedGroup o = arrange_levels(g, split);

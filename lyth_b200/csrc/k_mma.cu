@@ -221,30 +221,10 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
     }
 }
 
-// ---- host: tensor maps through the driver entry point (no link-time libcuda).
-typedef CUresult (*PFN_encode_tiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                     const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
-                                     CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                     CUtensorMapFloatOOBfill);
-
-static PFN_encode_tiled encode_fn() {
-    static PFN_encode_tiled fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_encode_tiled>(p);
-    }
-    return fn;
-}
-
 // A 2-D bf16 tensor map: inner extent `inner` (contiguous), outer `outer`, box inner 64
 // (128 bytes, the swizzle span) x box_outer, 128-byte swizzle.
 static bool make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint32_t box_outer) {
-    PFN_encode_tiled enc = encode_fn();
+    PFN_encode_tiled enc = tensor_map_encoder();
     if (!enc) return false;
     cuuint64_t dims[2] = {inner, outer};
     cuuint64_t strides[1] = {inner * 2};

@@ -1,4 +1,4 @@
-// mbarrier and bulk-copy helpers shared by the TMA-fed kernels (inline PTX, sm_100a).
+// mbarrier, bulk-copy and tensor-copy helpers shared by the TMA-fed kernels (inline PTX, sm_100a).
 //
 // Every wait is bounded twice -- by a poll count and by wall time on the global timer, since
 // one try_wait may itself suspend for an implementation-defined interval -- and a wait that
@@ -60,6 +60,36 @@ LYTH_D void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t ba
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
         "l"((uint64_t)src), "r"(bytes), "r"(bar)
         : "memory");
+}
+
+// Tiled tensor-map copy of a rank-5 box into this CTA's shared memory (no multicast).
+LYTH_D void tensor_load_5d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2, int c3, int c4,
+                           uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5, %6}], [%7];" ::"r"(dst),
+        "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+        : "memory");
+}
+
+// ---- host: tensor maps through the driver entry point (no link-time libcuda).
+typedef CUresult (*PFN_encode_tiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                     const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                     CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                     CUtensorMapFloatOOBfill);
+
+inline PFN_encode_tiled tensor_map_encoder() {
+    static PFN_encode_tiled fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encode_tiled>(p);
+    }
+    return fn;
 }
 
 }  // namespace lyth
