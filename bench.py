@@ -10,8 +10,10 @@ One JSON line on rank 0:
                random normalised state resident in HBM; one step = one layer; strong scaling
                (33 qubits at every N, sharded on the high qubits). Device time (CUDA events on
                the engine's stream), max over ranks.
-  * roofline   the dominant kernel (the in-place 1-qubit pass): algorithmic bytes (16 B per
-               amplitude) / its average device duration inside the timed region.
+  * roofline   the dominant kernel (the fused pass, staged_fused_kernel: one pass per group of
+               consecutive gates on <= 6 qubits): algorithmic bytes (16 B per amplitude: read
+               and write re and im once) / its average device duration inside the timed region;
+               traffic = DRAM bytes per launch from an ncu capture of the same kernel, scaled.
   * e2e        the same metric through the public API with host buffers: each step uploads the
                shard from pinned host memory, applies the layer, and reads the shard back.
   * cpu_baseline  the host evaluator port (oracle/) on a bounded sample, rank 0, N = 1.
@@ -39,6 +41,12 @@ if ROOT not in sys.path:
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}
 METRIC = "33-qubit statevector gates/s (HBM GB/s per kernel alongside)"
+# DRAM bytes (read + write) per amplitude of one staged fused pass: the mean over the 21 launches
+# of two layers of the benchmark circuit at 2^28 amplitudes (a 4 GiB state, 32x L2), ncu
+# dram__bytes_read.sum + dram__bytes_write.sum (8.006 + 7.781); the algorithmic figure is 16.
+# Traffic grows with the amplitudes a launch processes, so a launch's traffic is this x its
+# amplitudes.
+FUSED_PASS_DRAM_BYTES_PER_AMP = 15.787
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -499,8 +507,8 @@ def ours(a, dist: Dist) -> None:
     roofline = {"bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4) if achieved else None, "traffic": None,
                 "peak_source": pk_kind,
-                "kernel": "fused_pass_kernel (in place, <= 5 qubits per pass)" if dominant == "fused"
-                else "gate_q_kernel (in-place 1-qubit pass)",
+                "kernel": "staged_fused_kernel (fused pass: <= 6 qubits, in place, TMA-staged tiles)"
+                if dominant == "fused" else "gate_q_kernel (in-place 1-qubit pass)",
                 "algorithmic_bytes_per_launch": int(pass_bytes), "avg_launch_ms": round(d_avg, 4),
                 "launches_timed": d_n,
                 "share_of_timed_region": round(d_ms / ms, 4) if ms else None,
@@ -508,9 +516,8 @@ def ours(a, dist: Dist) -> None:
                 "single_cu_pass": cls_row(tim["cu"], 8.0 * sv.local_len),
                 "exchange": {"gates": tim["exchange"][0],
                              "avg_ms": round(tim["exchange"][1] / tim["exchange"][0], 4) if tim["exchange"][0] else None}}
-    traffic_ratio = os.environ.get("LYTH_PASS_TRAFFIC_RATIO")
-    if traffic_ratio:
-        roofline["traffic"] = int(float(traffic_ratio) * pass_bytes)
+    if dominant == "fused" and FUSED_PASS_DRAM_BYTES_PER_AMP:
+        roofline["traffic"] = int(FUSED_PASS_DRAM_BYTES_PER_AMP * sv.local_len)
 
     # e2e: upload the shard from pinned host memory, apply one layer, read the shard back.
     e2e = None
