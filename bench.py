@@ -515,7 +515,12 @@ def ours(a, dist: Dist) -> None:
                 "single_u_pass": cls_row(tim["u"], pass_bytes),
                 "single_cu_pass": cls_row(tim["cu"], 8.0 * sv.local_len),
                 "exchange": {"gates": tim["exchange"][0],
-                             "avg_ms": round(tim["exchange"][1] / tim["exchange"][0], 4) if tim["exchange"][0] else None}}
+                             "avg_ms": round(tim["exchange"][1] / tim["exchange"][0], 4) if tim["exchange"][0] else None},
+                "swap_in": {"count": tim["swap"][0],
+                            "avg_ms": round(tim["swap"][1] / tim["swap"][0], 4) if tim["swap"][0] else None,
+                            "GB_s_each_way": round(4.0 * sv.local_len / (tim["swap"][1] / tim["swap"][0] * 1e-3) / 1e9, 1)
+                            if tim["swap"][0] else None,
+                            "share_of_timed_region": round(tim["swap"][1] / ms, 4) if ms else None}}
     if dominant == "fused" and FUSED_PASS_DRAM_BYTES_PER_AMP:
         roofline["traffic"] = int(FUSED_PASS_DRAM_BYTES_PER_AMP * sv.local_len)
 

@@ -521,6 +521,8 @@ uint64_t lyth_sv_launches(const lyth_sv *sv);
 #define LYTH_SV_T_CU 1
 #define LYTH_SV_T_EXCHANGE 2
 #define LYTH_SV_T_FUSED 3
+/* 4 = a rank-bit qubit swapped into a local bit (pack, transfer and unpack of half the shard). */
+#define LYTH_SV_T_SWAP 4
 /* Fusion (lyth-circuit fuse, lib.rs:72-100; docs/ADR-0030): consecutive local gates touching at
  * most `max_qubits` (1..6) bits run as one pass with the same chains in circuit order, bit-exact
  * with the unfused passes. 1 = one pass per gate. The default is 6. */

@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(256) scale_kernel(uint64_t len, const double *
 // Pack / unpack the local indices whose bit `lb` equals `v` (a half of the shard), taking the
 // k-th such index for k in [k0, k0 + count). With lb >= 2 (and count, k0 multiples of 4) four
 // consecutive k are four consecutive indices, so both sides move as 128-bit vectors.
-__global__ void __launch_bounds__(256) pack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
+__global__ void __launch_bounds__(1024) pack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
                                                         const float *re, const float *im, float *ore, float *oim) {
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t nth = (uint64_t)gridDim.x * blockDim.x;
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(256) pack_half_kernel(uint64_t count, uint64_t
         oim[k] = im[i];
     }
 }
-__global__ void __launch_bounds__(256) unpack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
+__global__ void __launch_bounds__(1024) unpack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
                                                           float *re, float *im, const float *ire, const float *iim) {
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t nth = (uint64_t)gridDim.x * blockDim.x;
@@ -181,8 +181,8 @@ struct lyth_sv {
     struct Mark { int cls; cudaEvent_t a, b; };
     std::vector<Mark> marks;
     std::vector<cudaEvent_t> pool;
-    uint64_t t_count[4] = {0, 0, 0, 0};
-    double t_ms[4] = {0, 0, 0, 0};
+    uint64_t t_count[5] = {0, 0, 0, 0, 0};
+    double t_ms[5] = {0, 0, 0, 0, 0};
     // Fusion (lyth_sv_set_fusion): the open group of consecutive local gates, on physical bits.
     int fuse_k = kFuseMaxQubits;
     FusedGroup open{};
@@ -438,6 +438,11 @@ int add_local(lyth_sv *sv, int c, uint32_t t, const U8 &m) {
 // is on the wire and the receive buffers double-buffered.
 int physical_swap_local_global(lyth_sv *sv, uint32_t lb, uint32_t gb) {
     const uint64_t half = sv->local_len >> 1;
+    // Pack / unpack run on half the SMs (one block of 1024 threads on every other SM), leaving
+    // the rest to NCCL's kernels for the chunk on the wire: measured, NCCL's point-to-point
+    // bandwidth halves when a memory-bound kernel shares every SM with it.
+    const unsigned xgrid_cap = (unsigned)device_sms() / 2u;
+    auto xgrid = [&](uint64_t len) { const unsigned g = stream_grid(len / 4 + 1, 1024); return g < xgrid_cap ? g : xgrid_cap; };
     if (sv->plan) {
         record(sv, LYTH_SV_OP_SWAP_LR, (int)lb, (int)gb, 0);
         sv->bytes_sent += 2 * half * sizeof(float);
@@ -447,6 +452,7 @@ int physical_swap_local_global(lyth_sv *sv, uint32_t lb, uint32_t gb) {
     const int partner = sv->rank ^ (1 << gb);
     const uint64_t v = (uint64_t)rank_bit(sv, gb) ^ 1ull;  // local bit value of what leaves and arrives
     const uint64_t nchunks = (half + sv->chunk - 1) / sv->chunk;
+    const int mk = mark_begin(sv, LYTH_SV_T_SWAP);
     int st = status_of(cudaEventRecord(sv->ev_start, sv->stream));
     if (st) return st;
     if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_start, 0)))) return st;
@@ -454,7 +460,7 @@ int physical_swap_local_global(lyth_sv *sv, uint32_t lb, uint32_t gb) {
     auto pack = [&](uint64_t c) -> int {
         const int b = (int)(c & 1);
         const uint64_t len = len_of(c);
-        pack_half_kernel<<<stream_grid(len / 4 + 1, 256), 256, 0, sv->stream>>>(len, c * sv->chunk, lb, v, sv->re,
+        pack_half_kernel<<<xgrid(len), 1024, 0, sv->stream>>>(len, c * sv->chunk, lb, v, sv->re,
                                                                               sv->im, sv->sre[b], sv->sim[b]);
         sv->launches++;
         int r = last_launch_status();
@@ -480,12 +486,13 @@ int physical_swap_local_global(lyth_sv *sv, uint32_t lb, uint32_t gb) {
         // (b ^ 1) was last read by transfer c - 1, which unpack(c - 1) already waited for.
         if (c + 1 < nchunks && (st = pack(c + 1))) return st;
         if ((st = status_of(cudaStreamWaitEvent(sv->stream, sv->ev_recv[b], 0)))) return st;
-        unpack_half_kernel<<<stream_grid(len / 4 + 1, 256), 256, 0, sv->stream>>>(len, c * sv->chunk, lb, v, sv->re,
+        unpack_half_kernel<<<xgrid(len), 1024, 0, sv->stream>>>(len, c * sv->chunk, lb, v, sv->re,
                                                                                 sv->im, sv->rre[b], sv->rim[b]);
         sv->launches++;
         if ((st = last_launch_status())) return st;
         if ((st = status_of(cudaEventRecord(sv->ev_done[b], sv->stream)))) return st;
     }
+    mark_end(sv, mk);
     sv->exchanges++;
     return LYTH_OK;
 }
@@ -713,7 +720,11 @@ int lyth_sv_create(lyth_sv **out, uint32_t qubits, int device, int rank, int nra
         }
     }
     if ((st = status_of(cudaStreamCreateWithFlags(&sv->stream, cudaStreamNonBlocking)))) return fail(st);
-    if ((st = status_of(cudaStreamCreateWithFlags(&sv->comm_stream, cudaStreamNonBlocking)))) return fail(st);
+    // The communication stream runs NCCL's kernels beside the pack / unpack of the next chunk;
+    // at the highest priority their blocks are placed first as SM slots come free.
+    int prio_lo = 0, prio_hi = 0;
+    cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi);
+    if ((st = status_of(cudaStreamCreateWithPriority(&sv->comm_stream, cudaStreamNonBlocking, prio_hi)))) return fail(st);
     for (int b = 0; b < 2; b++) {
         if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_recv[b], cudaEventDisableTiming)))) return fail(st);
         if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_done[b], cudaEventDisableTiming)))) return fail(st);
@@ -857,7 +868,7 @@ int lyth_sv_set_timing(lyth_sv *sv, int on) {
 }
 
 int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms) {
-    if (!sv || cls < 0 || cls > 3) return LYTH_E_INVALID;
+    if (!sv || cls < 0 || cls > LYTH_SV_T_SWAP) return LYTH_E_INVALID;
     DeviceGuard guard(sv);
     int st = fold_timing(sv);
     if (st) return st;
@@ -870,7 +881,7 @@ int lyth_sv_reset_timing(lyth_sv *sv) {
     if (!sv) return LYTH_E_INVALID;
     DeviceGuard guard(sv);
     int st = fold_timing(sv);
-    for (int c = 0; c < 4; c++) { sv->t_count[c] = 0; sv->t_ms[c] = 0.0; }
+    for (int c = 0; c <= LYTH_SV_T_SWAP; c++) { sv->t_count[c] = 0; sv->t_ms[c] = 0.0; }
     return st;
 }
 

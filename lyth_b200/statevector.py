@@ -109,9 +109,9 @@ class StateVector:
 
     def timing(self) -> dict:
         """{class: (count, total ms)}: 'u' (1-qubit passes), 'cu' (2-qubit), 'exchange',
-        'fused' (fused multi-gate passes)."""
+        'fused' (fused multi-gate passes), 'swap' (rank-bit qubits swapped into local bits)."""
         out = {}
-        for cls, name in enumerate(("u", "cu", "exchange", "fused")):
+        for cls, name in enumerate(("u", "cu", "exchange", "fused", "swap")):
             n, ms = C.c_uint64(), C.c_double()
             check(lib.lyth_sv_timing(self._h, cls, C.byref(n), C.byref(ms)), "timing")
             out[name] = (n.value, ms.value)
