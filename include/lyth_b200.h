@@ -532,6 +532,17 @@ int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits);
  * then runs the gate as a local (fusable) pass; on = 0 exchanges the whole shard with the partner
  * rank and computes this rank's row of the gate. Both are bit-exact. */
 int lyth_sv_set_remap(lyth_sv *sv, int on);
+/* With remap on: the most rank-bit qubits one swap-in brings in together (1..6, default 6). Extra
+ * ones join only while each is needed before the local qubit it displaces; k of them cost one
+ * exchange of (2^k - 1) / 2^k of the shard among 2^k ranks instead of k half-shard swaps. 1 = one
+ * at a time. Bit-exact either way. */
+int lyth_sv_set_swap_batch(lyth_sv *sv, int max_qubits);
+/* Transport of swap-ins on a multi-rank handle: 1 = copy engines (each rank pulls its partners'
+ * packed chunks over NVLink with cudaMemcpyAsync through CUDA IPC mappings, ordered by sequence
+ * flags; the default when every rank could map every peer), 0 = NCCL send / recv. Collective:
+ * every rank sets the same value at the same point. lyth_sv_transport reports the one in use. */
+int lyth_sv_set_transport(lyth_sv *sv, int copy_engine);
+int lyth_sv_transport(const lyth_sv *sv);
 int lyth_sv_set_timing(lyth_sv *sv, int on);
 int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms);
 int lyth_sv_reset_timing(lyth_sv *sv);
@@ -553,12 +564,15 @@ int lyth_sv_reset_timing(lyth_sv *sv);
 #define LYTH_SV_OP_SWAP_LOCAL 4  /* swap local bits a, b */
 #define LYTH_SV_OP_SWAP_LR 5     /* swap local bit a with rank bit b (half the shard each way) */
 #define LYTH_SV_OP_SWAP_RR 6     /* swap rank bits a, b (whole shards, where the bits differ) */
+#define LYTH_SV_OP_SWAP_MULTI 7  /* swap local bits bits[j] with rank bits rbits[j], j < k (k >= 2):
+                                    one exchange among the 2^k ranks differing in those bits */
 typedef struct lyth_sv_op {
     int32_t kind;
     int32_t a, b, c;
     float m[8];                                /* U, CU, EXCHANGE */
     int32_t k;                                 /* FUSED: levels */
-    uint32_t bits[LYTH_SV_FUSE_MAX_QUBITS];    /* FUSED: level -> local bit */
+    uint32_t bits[LYTH_SV_FUSE_MAX_QUBITS];    /* FUSED: level -> local bit; SWAP_MULTI: local bits */
+    uint32_t rbits[LYTH_SV_FUSE_MAX_QUBITS];   /* SWAP_MULTI: rank bits */
     uint32_t ngates;                           /* FUSED */
     int8_t gt[LYTH_SV_FUSE_MAX_GATES];         /* FUSED: target level of gate i */
     int8_t gc[LYTH_SV_FUSE_MAX_GATES];         /* FUSED: control level of gate i, or -1 */

@@ -59,14 +59,14 @@ class Gate(C.Structure):
 
 
 SV_OP_U, SV_OP_CU, SV_OP_FUSED, SV_OP_EXCHANGE = 0, 1, 2, 3
-SV_OP_SWAP_LOCAL, SV_OP_SWAP_LR, SV_OP_SWAP_RR = 4, 5, 6
+SV_OP_SWAP_LOCAL, SV_OP_SWAP_LR, SV_OP_SWAP_RR, SV_OP_SWAP_MULTI = 4, 5, 6, 7
 
 
 class SvOp(C.Structure):
     """``lyth_sv_op``: one step a plan handle recorded (include/lyth_b200.h)."""
 
     _fields_ = [("kind", C.c_int32), ("a", C.c_int32), ("b", C.c_int32), ("c", C.c_int32),
-                ("m", _f32 * 8), ("k", C.c_int32), ("bits", _u32 * 6), ("ngates", _u32),
+                ("m", _f32 * 8), ("k", C.c_int32), ("bits", _u32 * 6), ("rbits", _u32 * 6), ("ngates", _u32),
                 ("gt", C.c_int8 * 48), ("gc", C.c_int8 * 48), ("gm", (_f32 * 8) * 48)]
 
 
@@ -117,6 +117,9 @@ _sig("lyth_sv_timing", _i32, [_vp, _i32, C.POINTER(_u64), C.POINTER(C.c_double)]
 _sig("lyth_sv_reset_timing", _i32, [_vp])
 _sig("lyth_sv_set_fusion", _i32, [_vp, _i32])
 _sig("lyth_sv_set_remap", _i32, [_vp, _i32])
+_sig("lyth_sv_set_swap_batch", _i32, [_vp, _i32])
+_sig("lyth_sv_set_transport", _i32, [_vp, _i32])
+_sig("lyth_sv_transport", _i32, [_vp])
 _sig("lyth_sv_plan_create", _i32, [C.POINTER(_vp), _u32, _i32, _i32])
 _sig("lyth_sv_plan_count", _u64, [_vp])
 _sig("lyth_sv_plan_op", _i32, [_vp, _u64, C.POINTER(SvOp)])

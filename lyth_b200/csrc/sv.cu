@@ -21,10 +21,12 @@
 // NCCL is opened with dlopen on first use by a multi-rank handle, so the library itself loads
 // (and serves every single-GPU entry point) without it.
 #include <dlfcn.h>
+#include <unistd.h>
 #include <math.h>
 #include <nccl.h>
 #include <string.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "fused.cuh"
@@ -42,6 +44,7 @@ struct NcclApi {
     ncclResult_t (*GroupEnd)() = nullptr;
     ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
 };
@@ -63,6 +66,7 @@ static bool load_nccl() {
     LYTH_SYM(Send, "ncclSend");
     LYTH_SYM(Recv, "ncclRecv");
     LYTH_SYM(AllReduce, "ncclAllReduce");
+    LYTH_SYM(AllGather, "ncclAllGather");
 #undef LYTH_SYM
     g_nccl.ok = g_nccl.GetUniqueId && g_nccl.CommInitRank && g_nccl.CommDestroy && g_nccl.GroupStart &&
                 g_nccl.GroupEnd && g_nccl.Send && g_nccl.Recv && g_nccl.AllReduce;
@@ -117,43 +121,102 @@ __global__ void __launch_bounds__(256) scale_kernel(uint64_t len, const double *
     }
 }
 
-// Pack / unpack the local indices whose bit `lb` equals `v` (a half of the shard), taking the
-// k-th such index for k in [k0, k0 + count). With lb >= 2 (and count, k0 multiples of 4) four
-// consecutive k are four consecutive indices, so both sides move as 128-bit vectors.
-__global__ void __launch_bounds__(1024) pack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
-                                                        const float *re, const float *im, float *ore, float *oim) {
+// A swap of k local bits with k rank bits: the shard splits into 2^k subsets by the values of the
+// local bits, one per partner rank (and the one this rank keeps); subset `pattern` is the local
+// indices whose bits vs[0..k) (ascending) equal the pattern's bits. Partner y = blockIdx.y takes
+// elements [k0, k0 + count) of its subset, in ascending order of the other bits, to / from slice y
+// of the chunk buffers. With vs[0] >= 2 four consecutive elements are four consecutive indices.
+struct MultiPat {
+    uint32_t k;
+    uint32_t vs[8];
+    uint32_t pattern[64];  // per partner: bit s = value at vs[s]
+};
+LYTH_D uint64_t insert_pattern(uint64_t x, const MultiPat &mp, uint32_t pat) {
+    for (uint32_t s = 0; s < mp.k; s++) x = insert_bit(x, mp.vs[s], (pat >> s) & 1u);
+    return x;
+}
+__global__ void __launch_bounds__(1024) pack_multi_kernel(uint64_t count, uint64_t k0, const __grid_constant__ MultiPat mp,
+                                                         const float *re, const float *im, float *ore, float *oim) {
+    const uint32_t y = blockIdx.y, pat = mp.pattern[y];
+    ore += (uint64_t)y * count;
+    oim += (uint64_t)y * count;
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t nth = (uint64_t)gridDim.x * blockDim.x;
-    if (lb >= 2 && (count & 3) == 0 && (k0 & 3) == 0) {
+    if (mp.vs[0] >= 2 && (count & 3) == 0 && (k0 & 3) == 0) {
         for (uint64_t g = tid; g < (count >> 2); g += nth) {
-            const uint64_t i = insert_bit(k0 + 4 * g, lb, v);
+            const uint64_t i = insert_pattern(k0 + 4 * g, mp, pat);
             st4(ore + 4 * g, ld_stream4(re + i));
             st4(oim + 4 * g, ld_stream4(im + i));
         }
         return;
     }
-    for (uint64_t k = tid; k < count; k += nth) {
-        const uint64_t i = insert_bit(k0 + k, lb, v);
-        ore[k] = re[i];
-        oim[k] = im[i];
+    for (uint64_t e = tid; e < count; e += nth) {
+        const uint64_t i = insert_pattern(k0 + e, mp, pat);
+        ore[e] = re[i];
+        oim[e] = im[i];
     }
 }
-__global__ void __launch_bounds__(1024) unpack_half_kernel(uint64_t count, uint64_t k0, unsigned lb, uint64_t v,
-                                                          float *re, float *im, const float *ire, const float *iim) {
+__global__ void __launch_bounds__(1024) unpack_multi_kernel(uint64_t count, uint64_t k0, const __grid_constant__ MultiPat mp,
+                                                           float *re, float *im, const float *ire, const float *iim) {
+    const uint32_t y = blockIdx.y, pat = mp.pattern[y];
+    ire += (uint64_t)y * count;
+    iim += (uint64_t)y * count;
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t nth = (uint64_t)gridDim.x * blockDim.x;
-    if (lb >= 2 && (count & 3) == 0 && (k0 & 3) == 0) {
+    if (mp.vs[0] >= 2 && (count & 3) == 0 && (k0 & 3) == 0) {
         for (uint64_t g = tid; g < (count >> 2); g += nth) {
-            const uint64_t i = insert_bit(k0 + 4 * g, lb, v);
+            const uint64_t i = insert_pattern(k0 + 4 * g, mp, pat);
             st4(re + i, ld_stream4(ire + 4 * g));
             st4(im + i, ld_stream4(iim + 4 * g));
         }
         return;
     }
-    for (uint64_t k = tid; k < count; k += nth) {
-        const uint64_t i = insert_bit(k0 + k, lb, v);
-        re[i] = ire[k];
-        im[i] = iim[k];
+    for (uint64_t e = tid; e < count; e += nth) {
+        const uint64_t i = insert_pattern(k0 + e, mp, pat);
+        re[i] = ire[e];
+        im[i] = iim[e];
+    }
+}
+
+// Cross-GPU sequence flags of the copy-engine transport. Every rank polls only its own flag block
+// and peers signal it by remote stores into it, so every remote write is awaited by the rank it
+// targets before that rank frees anything.
+__device__ int g_sv_error;
+
+struct FlagPut {
+    uint32_t n;
+    uint64_t *flag[64];
+};
+// Thread t stores `value` into flag t (a peer's block), after this stream's earlier writes.
+__global__ void flags_put_kernel(const __grid_constant__ FlagPut fp, uint64_t value) {
+    const uint32_t t = threadIdx.x;
+    if (t >= fp.n) return;
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(fp.flag[t]), "l"(value) : "memory");
+}
+
+struct FlagSet {
+    uint32_t n;
+    const uint64_t *flag[64];
+};
+// Wait until every flag is >= target (thread t polls flag t). Bounded by 2 s of global-timer time;
+// on the limit set g_sv_error and return.
+__global__ void flag_wait_kernel(const __grid_constant__ FlagSet fs, uint64_t target) {
+    const uint32_t t = threadIdx.x;
+    if (t >= fs.n) return;
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+        uint64_t v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(fs.flag[t]) : "memory");
+        if (v >= target) return;
+        uint64_t now;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+        if (now - t0 > 2000000000ull) {
+            atomicExch(&g_sv_error, 1);
+            return;
+        }
+        __nanosleep(200);
     }
 }
 
@@ -170,6 +233,8 @@ struct lyth_sv {
     float *sre[2] = {nullptr, nullptr}, *sim[2] = {nullptr, nullptr};  // packed send chunks
     double *scratch = nullptr;  // norm partials
     cudaStream_t stream = nullptr, comm_stream = nullptr;
+    cudaStream_t copy_stream = nullptr;  // second copy-engine queue (the im halves of the pulls)
+    cudaEvent_t ev_pull = nullptr, ev_copied = nullptr;
     cudaEvent_t ev_recv[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_start = nullptr;
     cudaEvent_t ev_packed[2] = {nullptr, nullptr};
     ncclComm_t comm = nullptr;
@@ -190,6 +255,21 @@ struct lyth_sv {
     // exchange of the whole shard and compute this rank's row.
     int remap = 1;
     uint64_t swaps_in = 0;
+    // Most rank-bit qubits one swap-in may bring in together (lyth_sv_set_swap_batch).
+    int swap_batch = 6;
+    // Copy-engine transport for swap-ins (multi-rank): every rank's send chunks and flag block
+    // mapped through CUDA IPC; a rank pulls its partners' packed slices with cudaMemcpyAsync on
+    // the copy engines. Flag block (kFlagWords u64): [r * 2 + b] = last chunk rank r packed for
+    // this rank into its send slot b; [kPulledAt + r * 2 + b] = last chunk rank r pulled from this
+    // rank's send slot b.
+    bool ce = false;
+    uint64_t *flags = nullptr;
+    std::vector<float *> peer_sre[2], peer_sim[2];
+    std::vector<uint64_t *> peer_flags;  // every rank's flag block (own included)
+    std::vector<void *> ipc_opened;
+    uint64_t xseq = 0;                       // chunk sequence number, identical on every rank
+    uint64_t slot_seq[2] = {0, 0};           // last chunk packed into send slot b
+    std::vector<int> slot_partners[2];       // the ranks that pull it
     // Plan handle (lyth_sv_plan_create): no device state; each step is appended here instead.
     bool plan = false;
     std::vector<lyth_sv_op> ops;
@@ -431,69 +511,166 @@ int add_local(lyth_sv *sv, int c, uint32_t t, const U8 &m) {
     return LYTH_OK;
 }
 
-// Physical swap of local bit lb with rank bit gb: the half of the shard whose bit lb differs
-// from this rank's bit gb goes to the partner and lands at the same index (same other bits), and
-// the partner's matching half comes back into the positions it vacated. Chunked and pipelined
-// over two streams: pack(c) -> send/recv(c) -> unpack(c), with pack(c+1) running while chunk c
-// is on the wire and the receive buffers double-buffered.
-int physical_swap_local_global(lyth_sv *sv, uint32_t lb, uint32_t gb) {
-    const uint64_t half = sv->local_len >> 1;
-    // Pack / unpack run on half the SMs (one block of 1024 threads on every other SM), leaving
-    // the rest to NCCL's kernels for the chunk on the wire: measured, NCCL's point-to-point
-    // bandwidth halves when a memory-bound kernel shares every SM with it.
-    const unsigned xgrid_cap = (unsigned)device_sms() / 2u;
-    auto xgrid = [&](uint64_t len) { const unsigned g = stream_grid(len / 4 + 1, 1024); return g < xgrid_cap ? g : xgrid_cap; };
+constexpr int kFlagRanks = 64, kPulledAt = 2 * kFlagRanks, kFlagWords = 4 * kFlagRanks;
+
+// Wait on `stream` until this rank's own flags [base + r * 2 + b] for the listed ranks are >= target.
+int wait_own(lyth_sv *sv, cudaStream_t stream, const std::vector<int> &ranks, int base, int b, uint64_t target) {
+    FlagSet fs{};
+    fs.n = (uint32_t)ranks.size();
+    for (uint32_t i = 0; i < fs.n; i++) fs.flag[i] = sv->flags + base + ranks[i] * 2 + b;
+    flag_wait_kernel<<<1, 64, 0, stream>>>(fs, target);
+    sv->launches++;
+    return last_launch_status();
+}
+// Store `value` into flag [base + rank * 2 + b] of each listed rank's block (after `stream`'s work).
+int put_peers(lyth_sv *sv, cudaStream_t stream, const std::vector<int> &ranks, int base, int b, uint64_t value) {
+    FlagPut fp{};
+    fp.n = (uint32_t)ranks.size();
+    for (uint32_t i = 0; i < fp.n; i++) fp.flag[i] = sv->peer_flags[ranks[i]] + base + sv->rank * 2 + b;
+    flags_put_kernel<<<1, 64, 0, stream>>>(fp, value);
+    sv->launches++;
+    return last_launch_status();
+}
+
+// Swap of local bits V[j] with physical rank bits Gp[j], j < k: one exchange among the 2^k ranks
+// that differ only in those rank bits. Rank r keeps the subset whose local bits equal its own rank
+// bits and trades subset q with the rank whose rank bits are q, into the same positions:
+// (2^k - 1) / 2^k of the shard each way (half for k = 1). Pipelined chunk by chunk on two streams:
+// pack(c + 1) on the compute stream while chunk c moves on the communication stream, unpack(c) as
+// it lands, send and receive chunks double-buffered.
+//
+// Transport: with the copy-engine path (CUDA IPC maps every rank's send chunks and flags), a rank
+// pulls its slice of each partner's packed chunk with cudaMemcpyAsync -- copy engines over NVLink,
+// no SMs -- after the partner's `packed` flag reaches the chunk's sequence number, then raises its
+// own `pulled` flag; a rank re-packs a send slot only after every partner that pulls from it has
+// raised `pulled` past it. Otherwise NCCL send / recv in one group per chunk. NCCL's transfer runs
+// on SMs: measured on B200, its point-to-point bandwidth halves when a memory-bound kernel shares
+// every SM with it, so on that path pack / unpack take half the SMs.
+int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::vector<uint32_t> &Gp) {
+    const uint32_t k = (uint32_t)V.size(), L = sv->local_bits;
+    const uint32_t P = (1u << k) - 1;
+    const uint64_t sub = sv->local_len >> k;
+    uint32_t qself = 0;
+    for (uint32_t j = 0; j < k; j++) qself |= (uint32_t)rank_bit(sv, Gp[j] - L) << j;
+    MultiPat mp{};
+    mp.k = k;
+    uint32_t order[8];
+    for (uint32_t j = 0; j < k; j++) order[j] = j;
+    for (uint32_t a = 1; a < k; a++)
+        for (uint32_t b = a; b > 0 && V[order[b - 1]] > V[order[b]]; b--) { const uint32_t t = order[b]; order[b] = order[b - 1]; order[b - 1] = t; }
+    for (uint32_t s = 0; s < k; s++) mp.vs[s] = V[order[s]];
+    std::vector<int> partner;
+    std::vector<uint32_t> myslice;  // the slice of partner y's send chunk that holds this rank's data
+    for (uint32_t q = 0; q <= P; q++) {
+        if (q == qself) continue;
+        int r = sv->rank;
+        uint32_t pat = 0;
+        for (uint32_t j = 0; j < k; j++)
+            r = (r & ~(1 << (Gp[j] - L))) | (int)(((q >> j) & 1u) << (Gp[j] - L));
+        for (uint32_t s = 0; s < k; s++) pat |= ((q >> order[s]) & 1u) << s;
+        mp.pattern[partner.size()] = pat;
+        partner.push_back(r);
+        myslice.push_back(qself < q ? qself : qself - 1);
+    }
+    auto remap_bits = [&]() {
+        for (uint32_t j = 0; j < k; j++) {
+            const uint32_t p1 = V[j], p2 = Gp[j];
+            const uint32_t q1 = sv->inv[p1], q2 = sv->inv[p2];
+            sv->pos[q1] = p2; sv->pos[q2] = p1;
+            sv->inv[p1] = q2; sv->inv[p2] = q1;
+        }
+    };
     if (sv->plan) {
-        record(sv, LYTH_SV_OP_SWAP_LR, (int)lb, (int)gb, 0);
-        sv->bytes_sent += 2 * half * sizeof(float);
+        if (k == 1) {
+            record(sv, LYTH_SV_OP_SWAP_LR, (int)V[0], (int)(Gp[0] - L), 0);
+        } else {
+            lyth_sv_op &op = record(sv, LYTH_SV_OP_SWAP_MULTI, 0, 0, 0);
+            op.k = (int32_t)k;
+            for (uint32_t j = 0; j < k; j++) { op.bits[j] = V[j]; op.rbits[j] = Gp[j] - L; }
+        }
+        sv->bytes_sent += 2 * P * sub * sizeof(float);
         sv->exchanges++;
+        remap_bits();
         return LYTH_OK;
     }
-    const int partner = sv->rank ^ (1 << gb);
-    const uint64_t v = (uint64_t)rank_bit(sv, gb) ^ 1ull;  // local bit value of what leaves and arrives
-    const uint64_t nchunks = (half + sv->chunk - 1) / sv->chunk;
+    // elements per partner per chunk: a chunk buffer holds P slices
+    uint64_t C = sv->chunk >> (k == 1 ? 0 : k);
+    if (C > sub) C = sub;
+    const uint64_t nchunks = sub / C;
+    const unsigned gx_cap = sv->ce ? (unsigned)device_sms() * 2u : (unsigned)device_sms() / 2u;
+    unsigned gx = stream_grid(C / 4 + 1, 1024);
+    if (gx * P > gx_cap) gx = gx_cap / P > 0 ? gx_cap / P : 1;
+    const dim3 grid(gx, P);
     const int mk = mark_begin(sv, LYTH_SV_T_SWAP);
     int st = status_of(cudaEventRecord(sv->ev_start, sv->stream));
     if (st) return st;
     if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_start, 0)))) return st;
-    auto len_of = [&](uint64_t c) { return (half - c * sv->chunk) < sv->chunk ? (half - c * sv->chunk) : sv->chunk; };
+    const uint64_t seq0 = sv->xseq;
     auto pack = [&](uint64_t c) -> int {
         const int b = (int)(c & 1);
-        const uint64_t len = len_of(c);
-        pack_half_kernel<<<xgrid(len), 1024, 0, sv->stream>>>(len, c * sv->chunk, lb, v, sv->re,
-                                                                              sv->im, sv->sre[b], sv->sim[b]);
+        int r;
+        // the send slot is re-packed once every rank that pulls its last chunk has done so
+        if (sv->ce && sv->slot_seq[b] && (r = wait_own(sv, sv->stream, sv->slot_partners[b], kPulledAt, b, sv->slot_seq[b])))
+            return r;
+        pack_multi_kernel<<<grid, 1024, 0, sv->stream>>>(C, c * C, mp, sv->re, sv->im, sv->sre[b], sv->sim[b]);
         sv->launches++;
-        int r = last_launch_status();
-        if (r) return r;
+        if ((r = last_launch_status())) return r;
+        if (sv->ce) {
+            if ((r = put_peers(sv, sv->stream, partner, 0, b, seq0 + c + 1))) return r;
+            sv->slot_seq[b] = seq0 + c + 1;
+            sv->slot_partners[b] = partner;
+        }
         return status_of(cudaEventRecord(sv->ev_packed[b], sv->stream));
     };
     if ((st = pack(0))) return st;
     for (uint64_t c = 0; c < nchunks; c++) {
         const int b = (int)(c & 1);
-        const uint64_t len = len_of(c);
-        // wire: after pack(c); into receive buffer b once unpack(c - 2) has drained it
-        if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_packed[b], 0)))) return st;
+        const uint64_t seq = seq0 + c + 1;
+        // receive slot b is free once unpack(c - 2) has drained it
         if (c >= 2 && (st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_done[b], 0)))) return st;
-        if ((st = nccl_status(g_nccl.GroupStart()))) return st;
-        g_nccl.Send(sv->sre[b], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
-        g_nccl.Send(sv->sim[b], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
-        g_nccl.Recv(sv->rre[b], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
-        g_nccl.Recv(sv->rim[b], len, ncclFloat32, partner, sv->comm, sv->comm_stream);
-        if ((st = nccl_status(g_nccl.GroupEnd()))) return st;
+        if (sv->ce) {
+            // re halves on the communication stream, im halves on a second stream: two copy
+            // engines in flight
+            if ((st = wait_own(sv, sv->comm_stream, partner, 0, b, seq))) return st;
+            if ((st = status_of(cudaEventRecord(sv->ev_pull, sv->comm_stream)))) return st;
+            if ((st = status_of(cudaStreamWaitEvent(sv->copy_stream, sv->ev_pull, 0)))) return st;
+            for (uint32_t y = 0; y < P; y++) {
+                const uint64_t off = (uint64_t)y * C, src = (uint64_t)myslice[y] * C;
+                if ((st = status_of(cudaMemcpyAsync(sv->rre[b] + off, sv->peer_sre[b][partner[y]] + src, C * sizeof(float),
+                                                    cudaMemcpyDeviceToDevice, sv->comm_stream))))
+                    return st;
+                if ((st = status_of(cudaMemcpyAsync(sv->rim[b] + off, sv->peer_sim[b][partner[y]] + src, C * sizeof(float),
+                                                    cudaMemcpyDeviceToDevice, sv->copy_stream))))
+                    return st;
+            }
+            if ((st = status_of(cudaEventRecord(sv->ev_copied, sv->copy_stream)))) return st;
+            if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_copied, 0)))) return st;
+            if ((st = put_peers(sv, sv->comm_stream, partner, kPulledAt, b, seq))) return st;
+        } else {
+            if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_packed[b], 0)))) return st;
+            if ((st = nccl_status(g_nccl.GroupStart()))) return st;
+            for (uint32_t y = 0; y < P; y++) {
+                const uint64_t off = (uint64_t)y * C;
+                g_nccl.Send(sv->sre[b] + off, C, ncclFloat32, partner[y], sv->comm, sv->comm_stream);
+                g_nccl.Send(sv->sim[b] + off, C, ncclFloat32, partner[y], sv->comm, sv->comm_stream);
+                g_nccl.Recv(sv->rre[b] + off, C, ncclFloat32, partner[y], sv->comm, sv->comm_stream);
+                g_nccl.Recv(sv->rim[b] + off, C, ncclFloat32, partner[y], sv->comm, sv->comm_stream);
+            }
+            if ((st = nccl_status(g_nccl.GroupEnd()))) return st;
+        }
         if ((st = status_of(cudaEventRecord(sv->ev_recv[b], sv->comm_stream)))) return st;
-        sv->bytes_sent += 2 * len * sizeof(float);
-        // compute stream: pack the next chunk while this one is on the wire; its send buffer
-        // (b ^ 1) was last read by transfer c - 1, which unpack(c - 1) already waited for.
+        sv->bytes_sent += 2 * P * C * sizeof(float);
         if (c + 1 < nchunks && (st = pack(c + 1))) return st;
         if ((st = status_of(cudaStreamWaitEvent(sv->stream, sv->ev_recv[b], 0)))) return st;
-        unpack_half_kernel<<<xgrid(len), 1024, 0, sv->stream>>>(len, c * sv->chunk, lb, v, sv->re,
-                                                                                sv->im, sv->rre[b], sv->rim[b]);
+        unpack_multi_kernel<<<grid, 1024, 0, sv->stream>>>(C, c * C, mp, sv->re, sv->im, sv->rre[b], sv->rim[b]);
         sv->launches++;
         if ((st = last_launch_status())) return st;
         if ((st = status_of(cudaEventRecord(sv->ev_done[b], sv->stream)))) return st;
     }
+    sv->xseq = seq0 + nchunks;
     mark_end(sv, mk);
     sv->exchanges++;
+    remap_bits();
     return LYTH_OK;
 }
 
@@ -543,7 +720,7 @@ int physical_swap(lyth_sv *sv, uint32_t p1, uint32_t p2) {
         sv->passes++;
         sv->launches++;
     } else if (p1 < L) {
-        st = physical_swap_local_global(sv, p1, p2 - L);
+        return physical_swap_multi(sv, std::vector<uint32_t>{p1}, std::vector<uint32_t>{p2});  // updates the map
     } else {
         st = physical_swap_global_global(sv, p1 - L, p2 - L);
     }
@@ -565,9 +742,12 @@ int normalize(lyth_sv *sv) {
     return LYTH_OK;
 }
 
-// Bring the qubit on rank bit (gp - L) into a local bit: the victim is the local bit whose
+// Bring the qubit on physical rank bit gp into a local bit. The victim is the local bit whose
 // logical qubit is next used furthest ahead in gates[i..count) (never used: best), ties to the
-// highest bit. The choice depends only on the map and the gate list, so every rank makes it.
+// highest bit. With a swap batch > 1, other rank-bit qubits come in with it, soonest-used first,
+// each while its next use precedes the next use of the victim it would displace (the next-furthest
+// local bit): one exchange among 2^k ranks then replaces k single swaps. Every choice depends only
+// on the map and the gate list, so every rank makes it.
 int swap_in(lyth_sv *sv, uint32_t gp, const lyth_gate *gates, uint64_t count, uint64_t i) {
     int st = flush_group(sv);
     if (st) return st;
@@ -584,19 +764,27 @@ int swap_in(lyth_sv *sv, uint32_t gp, const lyth_gate *gates, uint64_t count, ui
                 seen++;
             }
     }
-    uint32_t victim = L - 1;
-    uint64_t best = 0;
-    bool any = false;
-    for (int b = (int)L - 1; b >= 0; b--) {
-        const uint64_t nu = next[sv->inv[b]];
-        if (!any || nu > best) {
-            best = nu;
-            victim = (uint32_t)b;
-            any = true;
+    // local bits by next use, furthest first (ties: highest bit)
+    std::vector<uint32_t> loc(L);
+    for (uint32_t b = 0; b < L; b++) loc[b] = L - 1 - b;
+    std::stable_sort(loc.begin(), loc.end(), [&](uint32_t x, uint32_t y) { return next[sv->inv[x]] > next[sv->inv[y]]; });
+    // the other rank bits by next use, soonest first
+    std::vector<uint32_t> glob;
+    for (uint32_t b = L; b < sv->qubits; b++)
+        if (b != gp) glob.push_back(b);
+    std::stable_sort(glob.begin(), glob.end(), [&](uint32_t x, uint32_t y) { return next[sv->inv[x]] < next[sv->inv[y]]; });
+    std::vector<uint32_t> V{loc[0]}, G{gp};
+    for (uint32_t j = 0; j < glob.size() && (int)V.size() < sv->swap_batch && V.size() < L; j++) {
+        if (next[sv->inv[glob[j]]] < next[sv->inv[loc[V.size()]]]) {
+            V.push_back(loc[V.size()]);
+            G.push_back(glob[j]);
+        } else {
+            break;
         }
     }
-    sv->swaps_in++;
-    return physical_swap(sv, victim, gp);
+    sv->swaps_in += V.size();
+    if (V.size() == 1) return physical_swap(sv, V[0], gp);
+    return physical_swap_multi(sv, V, G);
 }
 
 int apply_one(lyth_sv *sv, const lyth_gate *gates, uint64_t count, uint64_t i) {
@@ -641,8 +829,119 @@ int apply_one(lyth_sv *sv, const lyth_gate *gates, uint64_t count, uint64_t i) {
     }
 }
 
+// Copy-engine transport set-up (collective over the handle's ranks): map every rank's send chunks
+// and flag block through CUDA IPC. Every rank ends with the same `ce` (false: NCCL for swaps).
+struct IpcRec {
+    int32_t ok, pad;
+    cudaIpcMemHandle_t h[5];  // sre[0], sre[1], sim[0], sim[1], flags
+};
+
+void close_ipc(lyth_sv *sv) {
+    for (void *p : sv->ipc_opened) cudaIpcCloseMemHandle(p);
+    sv->ipc_opened.clear();
+    for (int b = 0; b < 2; b++) { sv->peer_sre[b].clear(); sv->peer_sim[b].clear(); }
+    sv->peer_flags.clear();
+    sv->ce = false;
+}
+
+int setup_ce(lyth_sv *sv) {
+    const int n = sv->nranks;
+    IpcRec mine{};
+    mine.ok = 1;
+    if (cudaMalloc(&sv->flags, kFlagWords * sizeof(uint64_t)) != cudaSuccess) {
+        sv->flags = nullptr;
+        mine.ok = 0;
+    } else if (cudaMemset(sv->flags, 0, kFlagWords * sizeof(uint64_t)) != cudaSuccess) {
+        mine.ok = 0;
+    }
+    void *exported[5] = {sv->sre[0], sv->sre[1], sv->sim[0], sv->sim[1], sv->flags};
+    for (int i = 0; i < 5 && mine.ok; i++)
+        if (cudaIpcGetMemHandle(&mine.h[i], exported[i]) != cudaSuccess) mine.ok = 0;
+    if (n > kFlagRanks) mine.ok = 0;
+    cudaGetLastError();
+    IpcRec *d = nullptr;
+    if (cudaMalloc(&d, sizeof(IpcRec) * (n + 1)) != cudaSuccess) {
+        cudaGetLastError();
+        return LYTH_E_OOM;
+    }
+    int st = status_of(cudaMemcpy(d + n, &mine, sizeof mine, cudaMemcpyHostToDevice));
+    if (!st) st = nccl_status(g_nccl.AllGather(d + n, d, sizeof(IpcRec), ncclUint8, sv->comm, sv->stream));
+    if (!st) st = status_of(cudaStreamSynchronize(sv->stream));
+    std::vector<IpcRec> all(n);
+    if (!st) st = status_of(cudaMemcpy(all.data(), d, sizeof(IpcRec) * n, cudaMemcpyDeviceToHost));
+    if (st) { cudaFree(d); return st; }
+    bool every = true;
+    for (int r = 0; r < n; r++) every = every && all[r].ok;
+    int32_t opened = every ? 1 : 0;
+    if (every) {
+        for (int b = 0; b < 2; b++) { sv->peer_sre[b].assign(n, nullptr); sv->peer_sim[b].assign(n, nullptr); }
+        sv->peer_flags.assign(n, nullptr);
+        for (int r = 0; r < n && opened; r++) {
+            if (r == sv->rank) {
+                for (int b = 0; b < 2; b++) { sv->peer_sre[b][r] = sv->sre[b]; sv->peer_sim[b][r] = sv->sim[b]; }
+                sv->peer_flags[r] = sv->flags;
+                continue;
+            }
+            void *p[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+            for (int i = 0; i < 5; i++) {
+                if (cudaIpcOpenMemHandle(&p[i], all[r].h[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                    cudaGetLastError();
+                    opened = 0;
+                    break;
+                }
+                sv->ipc_opened.push_back(p[i]);
+            }
+            if (!opened) break;
+            sv->peer_sre[0][r] = (float *)p[0]; sv->peer_sre[1][r] = (float *)p[1];
+            sv->peer_sim[0][r] = (float *)p[2]; sv->peer_sim[1][r] = (float *)p[3];
+            sv->peer_flags[r] = (uint64_t *)p[4];
+        }
+    }
+    // every rank must agree: the transport is used only if every rank mapped every peer
+    int32_t *dok = reinterpret_cast<int32_t *>(d);
+    st = status_of(cudaMemcpy(dok, &opened, sizeof opened, cudaMemcpyHostToDevice));
+    if (!st) st = nccl_status(g_nccl.AllReduce(dok, dok, 1, ncclInt32, ncclMin, sv->comm, sv->stream));
+    if (!st) st = status_of(cudaStreamSynchronize(sv->stream));
+    int32_t agreed = 0;
+    if (!st) st = status_of(cudaMemcpy(&agreed, dok, sizeof agreed, cudaMemcpyDeviceToHost));
+    cudaFree(d);
+    if (st) { close_ipc(sv); return st; }
+    if (agreed) sv->ce = true;
+    else close_ipc(sv);
+    return LYTH_OK;
+}
+
+int device_sv_error() {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_sv_error, sizeof v) != cudaSuccess) return LYTH_E_INVALID;
+    if (v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_sv_error, &zero, sizeof zero);
+        return LYTH_E_TIMEOUT;
+    }
+    return LYTH_OK;
+}
+
+// Before a rank's buffers and flag block go: every partner has pulled the last chunk of each send
+// slot (the pulled flags arrive in this rank's own block, so no peer writes to it afterwards, and
+// every flag this rank wrote to a peer was awaited by that peer before its own teardown).
+void teardown_ce(lyth_sv *sv) {
+    if (!sv->ce) return;
+    cudaStreamSynchronize(sv->stream);
+    cudaStreamSynchronize(sv->comm_stream);
+    cudaStreamSynchronize(sv->copy_stream);
+    for (int b = 0; b < 2; b++)
+        if (sv->slot_seq[b]) wait_own(sv, sv->stream, sv->slot_partners[b], kPulledAt, b, sv->slot_seq[b]);
+    cudaStreamSynchronize(sv->stream);
+    // After a timed-out wait a peer may still be inside its own bounded waits: outlast them.
+    if (device_sv_error() != LYTH_OK) usleep(5000000);
+    close_ipc(sv);
+}
+
 void free_all(lyth_sv *sv) {
+    teardown_ce(sv);
     if (sv->comm && g_nccl.CommDestroy) g_nccl.CommDestroy(sv->comm);
+    cudaFree(sv->flags);
     cudaFree(sv->re);
     cudaFree(sv->im);
     for (int b = 0; b < 2; b++) {
@@ -658,8 +957,11 @@ void free_all(lyth_sv *sv) {
     for (auto &mk : sv->marks) { cudaEventDestroy(mk.a); cudaEventDestroy(mk.b); }
     for (auto e : sv->pool) cudaEventDestroy(e);
     if (sv->ev_start) cudaEventDestroy(sv->ev_start);
+    if (sv->ev_pull) cudaEventDestroy(sv->ev_pull);
+    if (sv->ev_copied) cudaEventDestroy(sv->ev_copied);
     if (sv->stream) cudaStreamDestroy(sv->stream);
     if (sv->comm_stream) cudaStreamDestroy(sv->comm_stream);
+    if (sv->copy_stream) cudaStreamDestroy(sv->copy_stream);
 }
 
 }  // namespace
@@ -725,6 +1027,9 @@ int lyth_sv_create(lyth_sv **out, uint32_t qubits, int device, int rank, int nra
     int prio_lo = 0, prio_hi = 0;
     cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi);
     if ((st = status_of(cudaStreamCreateWithPriority(&sv->comm_stream, cudaStreamNonBlocking, prio_hi)))) return fail(st);
+    if ((st = status_of(cudaStreamCreateWithPriority(&sv->copy_stream, cudaStreamNonBlocking, prio_hi)))) return fail(st);
+    if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_pull, cudaEventDisableTiming)))) return fail(st);
+    if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_copied, cudaEventDisableTiming)))) return fail(st);
     for (int b = 0; b < 2; b++) {
         if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_recv[b], cudaEventDisableTiming)))) return fail(st);
         if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_done[b], cudaEventDisableTiming)))) return fail(st);
@@ -738,6 +1043,7 @@ int lyth_sv_create(lyth_sv **out, uint32_t qubits, int device, int rank, int nra
             sv->comm = nullptr;
             return fail(LYTH_E_NCCL);
         }
+        if ((st = setup_ce(sv))) return fail(st);
     }
     *out = sv;
     return LYTH_OK;
@@ -836,6 +1142,33 @@ int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count) {
     return flush_group(sv);
 }
 
+int lyth_sv_set_transport(lyth_sv *sv, int copy_engine) {
+    if (!sv) return LYTH_E_INVALID;
+    if (copy_engine && sv->peer_flags.empty()) return LYTH_E_UNSUPPORTED;
+    if (!sv->plan) {
+        DeviceGuard guard(sv);
+        // drain the current transport before switching: partners must have pulled every chunk
+        int st = status_of(cudaStreamSynchronize(sv->comm_stream));
+        if (!st) st = status_of(cudaStreamSynchronize(sv->stream));
+        if (st) return st;
+        if (sv->ce && !copy_engine)
+            for (int b = 0; b < 2; b++)
+                if (sv->slot_seq[b]) wait_own(sv, sv->stream, sv->slot_partners[b], kPulledAt, b, sv->slot_seq[b]);
+        if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
+    }
+    sv->ce = copy_engine != 0;
+    return LYTH_OK;
+}
+
+int lyth_sv_transport(const lyth_sv *sv) { return sv && sv->ce ? 1 : 0; }
+
+int lyth_sv_set_swap_batch(lyth_sv *sv, int max_qubits) {
+    if (!sv) return LYTH_E_INVALID;
+    if (max_qubits < 1 || max_qubits > 6) return LYTH_E_UNSUPPORTED;
+    sv->swap_batch = max_qubits;
+    return LYTH_OK;
+}
+
 int lyth_sv_set_remap(lyth_sv *sv, int on) {
     if (!sv) return LYTH_E_INVALID;
     sv->remap = on != 0;
@@ -856,7 +1189,8 @@ int lyth_sv_sync(lyth_sv *sv) {
     int st = status_of(cudaStreamSynchronize(sv->comm_stream));
     if (st) return st;
     if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
-    return fused_take_device_error();  // a staged pass that gave up a bounded wait
+    if ((st = fused_take_device_error())) return st;  // a staged pass that gave up a bounded wait
+    return sv->ce ? device_sv_error() : LYTH_OK;       // a transport flag wait that did
 }
 
 uint64_t lyth_sv_launches(const lyth_sv *sv) { return sv ? sv->launches : 0; }

@@ -107,6 +107,19 @@ class StateVector:
         whole shard and compute this rank's row (False)."""
         check(lib.lyth_sv_set_remap(self._h, int(on)), "set_remap")
 
+    def set_swap_batch(self, max_qubits: int) -> None:
+        """Most rank-bit qubits one swap-in brings in together (1 = one at a time; default 6)."""
+        check(lib.lyth_sv_set_swap_batch(self._h, max_qubits), "set_swap_batch")
+
+    def set_transport(self, copy_engine: bool) -> None:
+        """Swap-in transport: copy engines over CUDA IPC (True, the default when available) or
+        NCCL (False). Collective: every rank sets the same value at the same point."""
+        check(lib.lyth_sv_set_transport(self._h, int(copy_engine)), "set_transport")
+
+    @property
+    def transport(self) -> str:
+        return "copy_engine" if lib.lyth_sv_transport(self._h) else "nccl"
+
     def timing(self) -> dict:
         """{class: (count, total ms)}: 'u' (1-qubit passes), 'cu' (2-qubit), 'exchange',
         'fused' (fused multi-gate passes), 'swap' (rank-bit qubits swapped into local bits)."""
@@ -121,7 +134,7 @@ class StateVector:
         check(lib.lyth_sv_reset_timing(self._h), "reset_timing")
 
 
-_OP_NAMES = ("u", "cu", "fused", "exchange", "swap_local", "swap_lr", "swap_rr")
+_OP_NAMES = ("u", "cu", "fused", "exchange", "swap_local", "swap_lr", "swap_rr", "swap_multi")
 
 
 class Plan:
@@ -133,7 +146,9 @@ class Plan:
     * ``fused``: ``gates`` = [(target bit, control bit or -1, m), ...] in order;
     * ``exchange``: the gate ``m`` on rank bit ``a`` (control local bit ``c`` or -1), with the
       partner rank ^ (1 << a); this rank keeps its row;
-    * ``swap_local`` (bits a, b), ``swap_lr`` (local bit a, rank bit b), ``swap_rr`` (rank bits).
+    * ``swap_local`` (bits a, b), ``swap_lr`` (local bit a, rank bit b), ``swap_rr`` (rank bits);
+    * ``swap_multi``: local bits ``bits[j]`` with rank bits ``rbits[j]`` in one exchange among the
+      2^k ranks that differ only in those rank bits.
     """
 
     def __init__(self, qubits: int, rank: int = 0, nranks: int = 1):
@@ -166,6 +181,9 @@ class Plan:
     def set_remap(self, on: bool) -> None:
         check(lib.lyth_sv_set_remap(self._h, int(on)), "set_remap")
 
+    def set_swap_batch(self, max_qubits: int) -> None:
+        check(lib.lyth_sv_set_swap_batch(self._h, max_qubits), "set_swap_batch")
+
     def apply(self, gates) -> None:
         arr = gates if isinstance(gates, C.Array) else gates_array(gates)
         check(lib.lyth_sv_apply(self._h, arr, len(gates)), "apply")
@@ -188,6 +206,8 @@ class Plan:
         for i in range(int(lib.lyth_sv_plan_count(self._h))):
             check(lib.lyth_sv_plan_op(self._h, i, C.byref(op)), "plan_op")
             d = {"kind": _OP_NAMES[op.kind], "a": op.a, "b": op.b, "c": op.c, "m": tuple(op.m)}
+            if op.kind == 7:
+                d["bits"], d["rbits"] = list(op.bits[: op.k]), list(op.rbits[: op.k])
             if op.kind == 2:
                 bits = list(op.bits[: op.k])
                 d["gates"] = [(bits[op.gt[j]], bits[op.gc[j]] if op.gc[j] >= 0 else -1, tuple(op.gm[j]))

@@ -15,7 +15,7 @@ import pytest
 import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-COMM = ("exchange", "swap_lr", "swap_rr")
+COMM = ("exchange", "swap_lr", "swap_rr", "swap_multi")
 
 
 def _free_port():
@@ -67,8 +67,17 @@ def _paired(rank, bit, re, im, partner_state, fn):
     return np.ascontiguousarray(cr[sl]), np.ascontiguousarray(ci[sl])
 
 
+def partners_of(op, rank):
+    """The ranks a communication step trades with (none: no data moves)."""
+    if op["kind"] == "swap_multi":
+        mask = sum(1 << b for b in op["rbits"])
+        return [r for r in range(rank & ~mask, (rank | mask) + 1) if (r & ~mask) == (rank & ~mask) and r != rank]
+    p = partner_of(op, rank)
+    return [] if p == rank else [p]
+
+
 def partner_of(op, rank):
-    """The rank a communication step trades with (this rank itself: no data moves)."""
+    """The rank a pairwise communication step trades with (this rank itself: no data moves)."""
     if op["kind"] == "exchange":
         return rank ^ (1 << op["a"])
     if op["kind"] == "swap_lr":
@@ -87,6 +96,42 @@ def pairs_agree(seqs):
             if p != r and [e[:3] for e in seq if e[3] == p] != [e[:3] for e in seqs[p] if e[3] == r]:
                 return False
     return True
+
+
+def _swap_multi(vbits, rbits, rank, local_bits, re, im, run):
+    """Local bits vbits[j] <-> rank bits rbits[j]: gather the 2^k shards of the ranks that differ in
+    those rank bits (ordered by their values), swap bit vbits[j] with bit local_bits + j of the
+    combined state, and keep this rank's part."""
+    import torch.distributed as dist
+
+    k = len(vbits)
+    mask = sum(1 << b for b in rbits)
+    def rank_of(q):
+        r = rank & ~mask
+        for j, b in enumerate(rbits):
+            r |= ((q >> j) & 1) << b
+        return r
+    qself = sum(((rank >> b) & 1) << j for j, b in enumerate(rbits))
+    mine = torch.from_numpy(np.concatenate([re, im]))
+    parts = {qself: (re, im)}
+    reqs, bufs = [], {}
+    for q in range(1 << k):
+        if q == qself:
+            continue
+        bufs[q] = torch.empty_like(mine)
+        reqs.append(dist.isend(mine, rank_of(q)))
+        reqs.append(dist.irecv(bufs[q], rank_of(q)))
+    for r in reqs:
+        r.wait()
+    n = re.size
+    for q, t in bufs.items():
+        b = t.numpy()
+        parts[q] = (np.ascontiguousarray(b[:n]), np.ascontiguousarray(b[n:]))
+    cr = np.concatenate([parts[q][0] for q in range(1 << k)])
+    ci = np.concatenate([parts[q][1] for q in range(1 << k)])
+    cr, ci = run([(2, v, local_bits + j, [0.0] * 8) for j, v in enumerate(vbits)], cr, ci)
+    sl = slice(qself * n, (qself + 1) * n)
+    return np.ascontiguousarray(cr[sl]), np.ascontiguousarray(ci[sl])
 
 
 def replay(ops, rank, local_bits, re, im):
@@ -113,6 +158,8 @@ def replay(ops, rank, local_bits, re, im):
         elif k == "swap_rr":
             if ((rank >> a) & 1) != ((rank >> b) & 1):
                 re, im = _trade((re, im), rank ^ (1 << a) ^ (1 << b))
+        elif k == "swap_multi":
+            re, im = _swap_multi(op["bits"], op["rbits"], rank, local_bits, re, im, run)
         else:
             raise AssertionError(k)
     return re, im
@@ -137,16 +184,18 @@ def _worker(rank, nranks, q, port, out_dir):
         for ci, (name, gates) in enumerate(circuits(q)):
             re0, im0 = orc.random_state(400 + ci, q)
             want_r, want_i = orc.run_gates(as_tuples(gates), re0, im0)
-            for fuse in (6, 3, 1):
-                for remap in (True, False):
+            for fuse, remap, batch in ((6, True, 6), (6, True, 1), (3, True, 6), (1, True, 6), (6, False, 6),
+                                       (1, False, 6)):
+                if True:
                     with Plan(q, rank, nranks) as p:
                         p.set_fusion(fuse)
                         p.set_remap(remap)
+                        p.set_swap_batch(batch)
                         p.apply(gates)
                         p.finish()
                         ops, st = p.ops(), p.stats()
-                    comm = [(o["kind"], o["a"], o["b"], partner_of(o, rank)) for o in ops if o["kind"] in COMM]
-                    comm = [e for e in comm if e[3] != rank]
+                    comm = [(o["kind"], o["a"], o["b"], p) for o in ops if o["kind"] in COMM
+                            for p in partners_of(o, rank)]
                     seqs = [None] * nranks
                     dist.all_gather_object(seqs, comm)
                     same = pairs_agree(seqs)
@@ -154,14 +203,15 @@ def _worker(rank, nranks, q, port, out_dir):
                                     np.ascontiguousarray(im0[lo:hi]))
                     ok = np.array_equal(re.view(np.uint32), want_r[lo:hi].view(np.uint32)) and \
                         np.array_equal(im.view(np.uint32), want_i[lo:hi].view(np.uint32))
-                    lines.append(f"{name}|{fuse}|{int(remap)}|{int(ok)}|{int(same)}|{len(comm)}|{st['exchanges']}")
+                    nmulti = sum(o["kind"] == "swap_multi" for o in ops)
+                    lines.append(f"{name}|{fuse}|{int(remap)}/{batch}|{int(ok)}|{int(same)}|{len(comm)}|{nmulti}")
     finally:
         dist.destroy_process_group()
     with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
         f.write("\n".join(lines) + "\n")
 
 
-@pytest.mark.parametrize("nranks,q", [(2, 9), (4, 10)])
+@pytest.mark.parametrize("nranks,q", [(2, 9), (4, 10), (8, 11)])
 def test_sharded_plan_replays_bit_exact(nranks, q, tmp_path):
     port = _free_port()
     ctx = torch.multiprocessing.get_context("spawn")
@@ -174,14 +224,17 @@ def test_sharded_plan_replays_bit_exact(nranks, q, tmp_path):
         if p.is_alive():
             p.kill()
         assert p.exitcode == 0, f"rank {r} exit {p.exitcode}"
-    total_comm = 0
+    total_comm = total_multi = 0
     for r in range(nranks):
         for line in open(tmp_path / f"r{r}.txt").read().splitlines():
-            name, fuse, remap, ok, same, ncomm, _ = line.split("|")
-            assert ok == "1", f"rank {r}: {name} fuse={fuse} remap={remap}: shard differs"
-            assert same == "1", f"{name} fuse={fuse} remap={remap}: a pair of ranks disagree on their steps"
+            name, fuse, remap, ok, same, ncomm, nmulti = line.split("|")
+            assert ok == "1", f"rank {r}: {name} fuse={fuse} remap/batch={remap}: shard differs"
+            assert same == "1", f"{name} fuse={fuse} remap/batch={remap}: a pair of ranks disagree on their steps"
             total_comm += int(ncomm)
+            total_multi += int(nmulti)
     assert total_comm > 0
+    if nranks >= 4:
+        assert total_multi > 0, "batched swap-ins must be exercised"
 
 
 def test_plan_handle_needs_no_gpu():

@@ -17,7 +17,7 @@ def _ngpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _worker(rank, nranks, q, case, nid, out_dir, remap=True):
+def _worker(rank, nranks, q, case, nid, out_dir, remap=True, batch=6, ce=True):
     import sys
 
     sys.path.insert(0, ROOT)
@@ -34,6 +34,9 @@ def _worker(rank, nranks, q, case, nid, out_dir, remap=True):
     lo, hi = rank * L, (rank + 1) * L
     with lb.StateVector(q, device=rank, rank=rank, nranks=nranks, nccl_id=nid) as sv:
         sv.set_remap(remap)
+        sv.set_swap_batch(batch)
+        sv.set_transport(ce)
+        transport = sv.transport
         sv.set_local(np.ascontiguousarray(re0[lo:hi]), np.ascontiguousarray(im0[lo:hi]))
         sv.apply(gates)
         sv.sync()
@@ -42,6 +45,7 @@ def _worker(rank, nranks, q, case, nid, out_dir, remap=True):
         st = sv.stats()
     with lb.Plan(q, rank, nranks) as plan:  # the same planner, recording only
         plan.set_remap(remap)
+        plan.set_swap_batch(batch)
         plan.apply(gates)
         plan.finish()
         pst = plan.stats()
@@ -50,7 +54,7 @@ def _worker(rank, nranks, q, case, nid, out_dir, remap=True):
     ok = np.array_equal(gr.view(np.uint32), wr[lo:hi].view(np.uint32)) and \
         np.array_equal(gi.view(np.uint32), wi[lo:hi].view(np.uint32))
     with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
-        f.write(f"{int(ok)} {st['exchanges']} {st['bytes_sent']} {int(same_plan)}\n")
+        f.write(f"{int(ok)} {st['exchanges']} {st['bytes_sent']} {int(same_plan)} {transport}\n")
     del suite
 
 
@@ -68,16 +72,12 @@ def case_gates(case, q):
     return "rank-bit gates", q, g
 
 
-@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("remap", [True, False])
-@pytest.mark.parametrize("case", [0, 1, 2])
-def test_two_ranks_bit_exact(case, remap, tmp_path):
+def _run_ranks(nranks, q, case, remap, batch, tmp_path, ce=True):
     import lyth_b200 as lb
 
-    nranks, q = 2, 18
     nid = lb.unique_id()
     ctx = torch.multiprocessing.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, nranks, q, case, nid, str(tmp_path), remap))
+    procs = [ctx.Process(target=_worker, args=(r, nranks, q, case, nid, str(tmp_path), remap, batch, ce))
              for r in range(nranks)]
     for p in procs:
         p.start()
@@ -85,7 +85,41 @@ def test_two_ranks_bit_exact(case, remap, tmp_path):
         p.join(timeout=300)
     for r, p in enumerate(procs):
         assert p.exitcode == 0, f"rank {r} exit {p.exitcode}"
-        ok, ex, sent, same_plan = open(tmp_path / f"r{r}.txt").read().split()
+        ok, ex, sent, same_plan, transport = open(tmp_path / f"r{r}.txt").read().split()
+        assert transport == ("copy_engine" if ce else "nccl")
         assert ok == "1", f"rank {r}: shard differs from the evaluator"
         assert same_plan == "1", f"rank {r}: the plan handle's counters differ from the engine's"
         assert int(ex) > 0, "the circuit must exercise the exchange"
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("remap", [True, False])
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_two_ranks_bit_exact(case, remap, tmp_path):
+    _run_ranks(2, 18, case, remap, 6, tmp_path)
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("case", [0, 2])
+def test_two_ranks_nccl_transport(case, tmp_path):
+    _run_ranks(2, 18, case, True, 6, tmp_path, ce=False)
+
+
+@pytest.mark.skipif(_ngpus() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("batch", [6, 1])
+@pytest.mark.parametrize("case", [0, 2])
+def test_four_ranks_bit_exact(case, batch, tmp_path):
+    # two rank bits: batch 6 takes the batched (all-to-all among 4 ranks) swap-ins
+    _run_ranks(4, 19, case, True, batch, tmp_path)
+
+
+@pytest.mark.skipif(_ngpus() < 4, reason="needs 4 GPUs")
+def test_four_ranks_nccl_transport(tmp_path):
+    _run_ranks(4, 19, 0, True, 6, tmp_path, ce=False)
+
+
+@pytest.mark.skipif(_ngpus() < 8, reason="needs 8 GPUs")
+@pytest.mark.parametrize("case", [0, 2])
+def test_eight_ranks_bit_exact(case, tmp_path):
+    # three rank bits: batched swap-ins among up to 8 ranks over the copy engines
+    _run_ranks(8, 20, case, True, 6, tmp_path)
