@@ -467,6 +467,14 @@ int lyth_b200_cu(uint64_t n, uint64_t wc, uint64_t wt, const float *m, const flo
 int lyth_b200_swap(uint64_t n, uint64_t wc, uint64_t wt, const float *re, const float *im, float *qr,
                    float *qi, cudaStream_t stream);
 
+/* Host-only self-test of the fused pass's tile layouts (no counterpart in the reference; no device
+ * is touched): plans `groups` random gate groups over 14..33 local qubits and checks that the
+ * copies into shared memory and the warps' reads agree on every amplitude, that tensor-map boxes
+ * tile the index space with aligned origins, that no warp read has a bank conflict, and that each
+ * gate lands on its group's bits. LYTH_OK, or a negative code naming the first failed check;
+ * `planned` / `boxes` (may be NULL) count the plans and those that copy by tensor-map boxes. */
+int lyth_b200_fused_layout_selftest(uint64_t seed, uint32_t groups, uint32_t *planned, uint32_t *boxes);
+
 /* ---- the state vector (lyth-circuit, crates/lyth-circuit/src/lib.rs:327-371, re-designed:
  * in place, a qubit map that makes SWAP a relabel, and sharded over ranks on its high qubits
  * with pairwise NCCL exchange for gates on those qubits). One handle per rank/GPU. ---------- */

@@ -28,6 +28,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <vector>
+
 #include "fused.cuh"
 #include "mbar.cuh"
 
@@ -642,7 +644,8 @@ static bool layout_boxes(const bool *tile, int star, uint32_t L, uint32_t *weigh
     return true;
 }
 
-static bool plan_staged(const FusedGroup &g, uint32_t L, bool boxes, StagedPlan &P) {
+// boxes: 0 = runs only, 1 = boxes where runs would be short (< 2 KiB), 2 = boxes where they fit.
+static bool plan_staged(const FusedGroup &g, uint32_t L, int boxes, StagedPlan &P) {
     if (L < kStMinBits || g.k < 1 || g.k > kFuseMaxQubits) return false;
     const int k = g.k;
     int use[kFuseMaxQubits] = {0};
@@ -720,7 +723,7 @@ static bool plan_staged(const FusedGroup &g, uint32_t L, bool boxes, StagedPlan 
     // runs) as tensor-map boxes, one or a few per component.
     uint32_t m_runs = 0;
     while (m_runs < 64 && tile[m_runs] && !star[m_runs]) m_runs++;
-    if (m_runs >= 9) boxes = false;
+    if (boxes == 1 && m_runs >= 9) boxes = 0;
     if (!(boxes && layout_boxes(tile, nstar ? (int)lane_addr[4] : -1, L, weight, P))) {
         // runs: address bits 0..m-1, all tile bits and none the lane group bit
         P.tma = 0;
@@ -842,8 +845,8 @@ int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaSt
         CUtensorMap tre, tim;
         memset(&tre, 0, sizeof tre);
         memset(&tim, 0, sizeof tim);
-        bool ok = plan_staged(g, L, true, P);
-        if (ok && P.tma && !encode_boxes(P, L, re, im, tre, tim)) ok = plan_staged(g, L, false, P);  // runs instead
+        bool ok = plan_staged(g, L, 1, P);
+        if (ok && P.tma && !encode_boxes(P, L, re, im, tre, tim)) ok = plan_staged(g, L, 0, P);  // runs instead
         if (ok) return launch_staged(P, tre, tim, re, im, s);
     }
     const bool split = g.k >= 5;
@@ -863,3 +866,152 @@ int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaSt
 }
 
 }  // namespace lyth
+
+// ------------------------------------------------------------------ host-only layout self-test
+// The staged pass is correct only if its planner's maps agree: for random groups it checks that
+// every tile element has exactly one shared-memory word, that the copies (runs or tensor-map
+// boxes, with the box coordinates rebuilt from the tile base) and the warps' reads agree on it,
+// that the tensor-map dimensions partition the index space with 16-byte-aligned box origins,
+// that no warp read hits a bank twice, and that every gate's target / control land on the
+// group's bits. No device is touched.
+namespace lyth {
+namespace {
+struct SplitMix {
+    uint64_t s;
+    uint64_t next() {
+        uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    }
+    uint32_t below(uint32_t n) { return (uint32_t)(next() % n); }
+};
+
+int check_layout(const FusedGroup &g, uint32_t L, const StagedPlan &P, SplitMix &rng) {
+    std::vector<int64_t> word2off(kStCompWords, -1);
+    if (P.tma) {
+        if (P.box_words * P.nbox != (uint32_t)kStTile) return -10;
+        std::vector<int> cover(L, 0);
+        for (int d = 0; d < 5; d++) {
+            if (!P.dim_len[d]) continue;
+            if (d > 0 && P.dim_lo[d] < 2) return -11;  // global strides must be multiples of 16 B
+            for (uint32_t x = 0; x < P.dim_len[d]; x++) {
+                if (P.dim_lo[d] + x >= L) return -12;
+                cover[P.dim_lo[d] + x]++;
+            }
+        }
+        for (uint32_t x = 0; x < L; x++)
+            if (cover[x] != 1) return -13;
+        for (uint32_t b = 0; b < P.nbox; b++)
+            for (uint32_t e = 0; e < P.box_words; e++) {
+                uint32_t rest = e;
+                uint64_t a = P.box_off[b];
+                for (int d = 0; d < 5; d++) {
+                    if (!P.dim_len[d]) continue;
+                    a += (uint64_t)(rest & ((1u << P.dim_box[d]) - 1)) << P.dim_lo[d];
+                    rest >>= P.dim_box[d];
+                }
+                const uint32_t w = b * P.box_words + e;
+                if (word2off[w] != -1) return -14;
+                word2off[w] = (int64_t)a;
+            }
+        uint64_t base = rng.next() % P.ntiles;
+        for (int t = 0; t < kStTileBits; t++) base = insert_bit(base, P.tile_bits[t], 0);
+        for (uint32_t b = 0; b < P.nbox; b++) {
+            const uint64_t a = base + P.box_off[b];
+            uint64_t back = 0;
+            for (int d = 0; d < 5; d++) {
+                if (!P.dim_len[d]) continue;
+                const uint64_t c = (a >> P.dim_lo[d]) & ((1ull << P.dim_len[d]) - 1);
+                if (c & ((1ull << P.dim_box[d]) - 1)) return -15;  // box origin off its alignment
+                back += c << P.dim_lo[d];
+            }
+            if (back != a) return -16;
+        }
+    } else {
+        for (uint32_t r = 0; r < P.nruns; r++)
+            for (uint32_t o = 0; o < (1u << P.run_bits); o++) {
+                const uint32_t w = P.run_word[r] + o;
+                if (w >= (uint32_t)kStCompWords || word2off[w] != -1) return -17;
+                word2off[w] = (int64_t)(P.run_off[r] + o);
+            }
+    }
+    std::vector<uint8_t> hit(kStTile, 0);
+    for (int wp = 0; wp < kStGroupWarps; wp++)
+        for (int i = 0; i < (1 << kStRegs); i++) {
+            uint32_t banks = 0;
+            for (int lane = 0; lane < 32; lane++) {
+                uint32_t w = 0;
+                uint64_t a = 0;
+                for (int b = 0; b < 5; b++)
+                    if ((lane >> b) & 1) { w += P.lane_w[b]; a += 1ull << P.lane_addr[b]; }
+                for (int b = 0; b < kStWarpBits; b++)
+                    if ((wp >> b) & 1) { w += P.warp_w[b]; a += 1ull << P.warp_addr[b]; }
+                for (int b = 0; b < kStRegs; b++)
+                    if ((i >> b) & 1) { w += P.reg_w[b]; a += 1ull << P.reg_addr[b]; }
+                if (w >= (uint32_t)kStCompWords || word2off[w] != (int64_t)a) return -18;
+                uint32_t idx = 0;  // the element's position among the tile bits
+                for (int t = 0; t < kStTileBits; t++)
+                    if ((a >> P.tile_bits[t]) & 1) idx |= 1u << t;
+                if (hit[idx]++) return -19;
+                banks |= 1u << (w % 32);
+            }
+            if (banks != 0xffffffffu) return -20;
+        }
+    for (uint32_t gi = 0; gi < g.ngates; gi++) {
+        const StagedGate &sg = P.gates[gi];
+        int64_t tb, cb = -1;
+        if (sg.case_ < 64) {
+            tb = P.reg_addr[sg.case_ / 8];
+            if (sg.case_ % 8 > 0) cb = P.reg_addr[sg.case_ % 8 - 1];
+        } else {
+            tb = P.lane_addr[sg.lt];
+            if (sg.case_ > 64) cb = P.reg_addr[sg.case_ - 65];
+        }
+        if (sg.lc >= 0) {
+            if (cb >= 0) return -21;
+            cb = P.lane_addr[sg.lc];
+        }
+        if (tb != (int64_t)g.bits[g.gates[gi].t]) return -22;
+        if (cb != (g.gates[gi].c >= 0 ? (int64_t)g.bits[g.gates[gi].c] : -1)) return -23;
+    }
+    return LYTH_OK;
+}
+}  // namespace
+}  // namespace lyth
+
+using namespace lyth;
+
+extern "C" int lyth_b200_fused_layout_selftest(uint64_t seed, uint32_t groups, uint32_t *planned,
+                                               uint32_t *boxes) {
+    SplitMix rng{seed};
+    uint32_t n_planned = 0, n_boxes = 0;
+    for (uint32_t it = 0; it < groups; it++) {
+        const uint32_t L = kStMinBits + rng.below(34 - kStMinBits);
+        FusedGroup g{};
+        g.k = 1 + (int32_t)rng.below(kFuseMaxQubits);
+        // a third of the groups on the low bits, where lanes hold group bits
+        const uint32_t span = (it % 3 == 0) ? 12 : L;
+        uint32_t used = 0;
+        for (int l = 0; l < g.k;) {
+            const uint32_t b = rng.below(span);
+            if (b >= 32 || (used >> b) & 1) continue;
+            used |= 1u << b;
+            g.bits[l++] = b;
+        }
+        g.ngates = 1 + rng.below(12);
+        for (uint32_t i = 0; i < g.ngates; i++) {
+            g.gates[i].t = (int8_t)rng.below((uint32_t)g.k);
+            g.gates[i].c = (int8_t)(g.k > 1 && rng.below(2) ? (g.gates[i].t + 1 + rng.below((uint32_t)g.k - 1)) % g.k : -1);
+        }
+        StagedPlan P;
+        if (!plan_staged(g, L, (int)(it % 3), P)) return LYTH_E_UNSUPPORTED;  // every such group must plan
+        n_planned++;
+        n_boxes += P.tma;
+        const int st = check_layout(g, L, P, rng);
+        if (st) return st;
+    }
+    if (planned) *planned = n_planned;
+    if (boxes) *boxes = n_boxes;
+    return LYTH_OK;
+}

@@ -137,3 +137,16 @@ def test_sv_create_refuses_bad_arguments_without_a_device():
     assert lb.lib.lyth_sv_create(C.byref(h), 10, 0, 2, 2, None) == lb.E_INVALID  # rank out of range
     assert lb.lib.lyth_sv_create(C.byref(h), 10, 0, 0, 2, None) == lb.E_INVALID  # no id
     assert lb.lib.lyth_sv_create(C.byref(h), 2, 0, 0, 4, b"x" * 128) == lb.E_INVALID  # too few qubits
+
+
+def test_fused_layout_selftest():
+    # The staged fused pass's planner, on the host: random groups over 14..33 local qubits, runs
+    # and tensor-map boxes, every map consistent and every warp read free of bank conflicts.
+    import ctypes as C
+
+    import lyth_b200 as lb
+
+    planned, boxes = C.c_uint32(), C.c_uint32()
+    st = lb.lib.lyth_b200_fused_layout_selftest(20_260_930, 4000, C.byref(planned), C.byref(boxes))
+    assert st == 0, f"layout check {st} failed"
+    assert planned.value == 4000 and boxes.value > 500
