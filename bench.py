@@ -72,7 +72,11 @@ def args_():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-qubits", type=int, default=25)
-    ap.add_argument("--fuse", type=int, default=None, help="max qubits per fused pass (1..5; default: the engine's)")
+    ap.add_argument("--fuse", type=int, default=None, help="max qubits per fused pass (1..6; default: the engine's)")
+    ap.add_argument("--swap-batch", type=int, default=None,
+                    help="most rank-bit qubits per swap-in (1..6; default: the engine's)")
+    ap.add_argument("--transport", choices=["copy_engine", "nccl"], default=None,
+                    help="swap-in transport at N > 1 (default: the engine's)")
     ap.add_argument("--case", default=None, help="run one kernel case (small config) and exit")
     ap.add_argument("--case-reps", type=int, default=3)
     ap.add_argument("--list-cases", action="store_true")
@@ -452,6 +456,10 @@ def ours(a, dist: Dist) -> None:
     sv = lb.StateVector(q, device=dist.local, rank=dist.rank, nranks=dist.world, nccl_id=nid)
     if a.fuse:
         sv.set_fusion(a.fuse)
+    if a.swap_batch:
+        sv.set_swap_batch(a.swap_batch)
+    if a.transport and dist.world > 1:
+        sv.set_transport(a.transport == "copy_engine")
     total_layers = a.warmup + a.steps
     gates = cc.layered(q, total_layers, cc.Rng(cc.BENCH_SEED))
     per = len(gates) // total_layers

@@ -540,10 +540,11 @@ int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits);
  * then runs the gate as a local (fusable) pass; on = 0 exchanges the whole shard with the partner
  * rank and computes this rank's row of the gate. Both are bit-exact. */
 int lyth_sv_set_remap(lyth_sv *sv, int on);
-/* With remap on: the most rank-bit qubits one swap-in brings in together (1..6, default 6). Extra
- * ones join only while each is needed before the local qubit it displaces; k of them cost one
- * exchange of (2^k - 1) / 2^k of the shard among 2^k ranks instead of k half-shard swaps. 1 = one
- * at a time. Bit-exact either way. */
+/* With remap on: the most rank-bit qubits one swap-in brings in together (1..6, default 1 = one at
+ * a time). Extra ones join only while each is needed before the local qubit it displaces; k of
+ * them cost one exchange of (2^k - 1) / 2^k of the shard among 2^k ranks instead of k half-shard
+ * swaps (fewer bytes, but a pull from several partners runs slower than a pairwise one on B200).
+ * Bit-exact either way. */
 int lyth_sv_set_swap_batch(lyth_sv *sv, int max_qubits);
 /* Transport of swap-ins on a multi-rank handle: 1 = copy engines (each rank pulls its partners'
  * packed chunks over NVLink with cudaMemcpyAsync through CUDA IPC mappings, ordered by sequence

@@ -255,8 +255,10 @@ struct lyth_sv {
     // exchange of the whole shard and compute this rank's row.
     int remap = 1;
     uint64_t swaps_in = 0;
-    // Most rank-bit qubits one swap-in may bring in together (lyth_sv_set_swap_batch).
-    int swap_batch = 6;
+    // Most rank-bit qubits one swap-in may bring in together (lyth_sv_set_swap_batch). One at a
+    // time by default: measured at 4 GPUs, a pairwise pull runs at 516 GB/s each way and a pull
+    // from three partners at ~390 in aggregate, so single swaps win despite the larger volume.
+    int swap_batch = 1;
     // Copy-engine transport for swap-ins (multi-rank): every rank's send chunks and flag block
     // mapped through CUDA IPC; a rank pulls its partners' packed slices with cudaMemcpyAsync on
     // the copy engines. Flag block (kFlagWords u64): [r * 2 + b] = last chunk rank r packed for

@@ -108,7 +108,7 @@ class StateVector:
         check(lib.lyth_sv_set_remap(self._h, int(on)), "set_remap")
 
     def set_swap_batch(self, max_qubits: int) -> None:
-        """Most rank-bit qubits one swap-in brings in together (1 = one at a time; default 6)."""
+        """Most rank-bit qubits one swap-in brings in together (default 1 = one at a time)."""
         check(lib.lyth_sv_set_swap_batch(self._h, max_qubits), "set_swap_batch")
 
     def set_transport(self, copy_engine: bool) -> None:
