@@ -5,18 +5,21 @@
 //  * updates the state in place (one copy of 2^q amplitudes: 33 qubits is 64 GiB, which leaves
 //    room on a 180 GB part), with the same fma chains as the out-of-place kernels, so every
 //    amplitude is bit-identical to the reference's;
+//  * fuses consecutive local gates on at most 6 qubits into one pass (k_fused.cu), applying them
+//    in circuit order, bit-identical to the unfused passes (lyth-circuit fuse, lib.rs:72-100);
 //  * keeps a logical -> physical qubit map, so a SWAP moves no data: it relabels two qubits.
 //    The map is undone by real permutation passes only when the state is read out, which is
 //    exact because a swap is a permutation;
 //  * skips the control=0 half of a CU (it is a copy in the reference: identity in place);
-//  * shards 2^q amplitudes over 2^g ranks on the g highest physical bits: rank r holds global
-//    indices [r * 2^L, (r+1) * 2^L), L = q - g. A gate on a local bit is a local pass. A CU
-//    whose control is a rank bit runs (as a local U) only on the ranks whose bit is 1. A gate
-//    whose target is a rank bit pairs rank r with r ^ (1 << b): each sends its shard to the
-//    other in chunks with NCCL (ncclSend / ncclRecv in a group, on a communication stream)
-//    into a double-buffered receive area, and computes its own row of the gate from (own,
-//    received) as each chunk lands -- receive-then-compute, no remote loads. The chunk's
-//    compute and the next chunk's transfer overlap.
+//  * shards 2^q amplitudes over 2^g ranks on the g highest physical bits: rank r holds physical
+//    indices [r * 2^L, (r+1) * 2^L), L = q - g. A gate on a local bit is a local (fusable) pass.
+//    A CU whose control is a rank bit runs (as a local U) only on the ranks whose bit is 1. A gate
+//    whose target is a rank bit first swaps that qubit into a local bit (the local qubit used
+//    furthest ahead leaves): half the shard is packed, moved to the partner and unpacked into
+//    the positions it vacated, chunk by chunk, the move on the copy engines (cudaMemcpyAsync
+//    pulls through CUDA IPC mappings, ordered by sequence flags) or NCCL. With remap off the
+//    pair exchanges whole shards instead and each computes its own row of the gate as chunks
+//    land. Receive-then-compute throughout: no kernel loads a peer's memory.
 //
 // NCCL is opened with dlopen on first use by a multi-rank handle, so the library itself loads
 // (and serves every single-GPU entry point) without it.
@@ -254,7 +257,6 @@ struct lyth_sv {
     // Rank-bit gates: 1 = swap the qubit into a local bit first (default), 0 = pairwise
     // exchange of the whole shard and compute this rank's row.
     int remap = 1;
-    uint64_t swaps_in = 0;
     // Most rank-bit qubits one swap-in may bring in together (lyth_sv_set_swap_batch). One at a
     // time by default: measured at 4 GPUs, a pairwise pull runs at 516 GB/s each way and a pull
     // from three partners at ~390 in aggregate, so single swaps win despite the larger volume.
@@ -784,7 +786,6 @@ int swap_in(lyth_sv *sv, uint32_t gp, const lyth_gate *gates, uint64_t count, ui
             break;
         }
     }
-    sv->swaps_in += V.size();
     if (V.size() == 1) return physical_swap(sv, V[0], gp);
     return physical_swap_multi(sv, V, G);
 }
