@@ -575,13 +575,15 @@ int lyth_sv_reset_timing(lyth_sv *sv);
 #define LYTH_SV_OP_SWAP_RR 6     /* swap rank bits a, b (whole shards, where the bits differ) */
 #define LYTH_SV_OP_SWAP_MULTI 7  /* swap local bits bits[j] with rank bits rbits[j], j < k (k >= 2):
                                     one exchange among the 2^k ranks differing in those bits */
+#define LYTH_SV_OP_PERMUTE 8     /* one pass moving local bit bits[j] to local bit rbits[j], j < k
+                                    (the read-out's undoing of the qubit map) */
 typedef struct lyth_sv_op {
     int32_t kind;
     int32_t a, b, c;
     float m[8];                                /* U, CU, EXCHANGE */
     int32_t k;                                 /* FUSED: levels */
     uint32_t bits[LYTH_SV_FUSE_MAX_QUBITS];    /* FUSED: level -> local bit; SWAP_MULTI: local bits */
-    uint32_t rbits[LYTH_SV_FUSE_MAX_QUBITS];   /* SWAP_MULTI: rank bits */
+    uint32_t rbits[LYTH_SV_FUSE_MAX_QUBITS];   /* SWAP_MULTI: rank bits; PERMUTE: destination bits */
     uint32_t ngates;                           /* FUSED */
     int8_t gt[LYTH_SV_FUSE_MAX_GATES];         /* FUSED: target level of gate i */
     int8_t gc[LYTH_SV_FUSE_MAX_GATES];         /* FUSED: control level of gate i, or -1 */

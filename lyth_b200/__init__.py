@@ -59,7 +59,7 @@ class Gate(C.Structure):
 
 
 SV_OP_U, SV_OP_CU, SV_OP_FUSED, SV_OP_EXCHANGE = 0, 1, 2, 3
-SV_OP_SWAP_LOCAL, SV_OP_SWAP_LR, SV_OP_SWAP_RR, SV_OP_SWAP_MULTI = 4, 5, 6, 7
+SV_OP_SWAP_LOCAL, SV_OP_SWAP_LR, SV_OP_SWAP_RR, SV_OP_SWAP_MULTI, SV_OP_PERMUTE = 4, 5, 6, 7, 8
 
 
 class SvOp(C.Structure):

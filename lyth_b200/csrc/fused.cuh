@@ -25,6 +25,12 @@ struct FusedGroup {
 };
 
 int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaStream_t s);
+// Move the amplitude at i to the index whose bit dst[j] is bit src[j] of i (k <= 6 bits, dst a
+// permutation of src), in one in-place pass. LYTH_E_UNSUPPORTED below the staged pass's size.
+int launch_permute(uint64_t len, const uint32_t *src, const uint32_t *dst, int k, float *re, float *im,
+                   cudaStream_t s);
+// Whether launch_permute takes these bits at this size (host only, no launch).
+bool permute_supported(uint64_t len, const uint32_t *src, int k);
 // LYTH_E_TIMEOUT (and clears the flag) if a staged pass gave up a bounded wait; else LYTH_OK.
 int fused_take_device_error();
 

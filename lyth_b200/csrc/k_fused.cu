@@ -343,6 +343,9 @@ struct StagedPlan {
     uint32_t nruns;
     uint32_t lane_w[5], reg_w[kStRegs], warp_w[kStWarpBits];  // shared-memory word weights
     uint32_t lane_addr[5], reg_addr[kStRegs], warp_addr[kStWarpBits];
+    // Where each lane / register / warp bit's value is stored: the bit itself, or for a
+    // permutation pass its image (a permutation of tile bits keeps every tile in place).
+    uint32_t dlane_addr[5], dreg_addr[kStRegs], dwarp_addr[kStWarpBits];
     uint32_t run_word[kStMaxRuns];  // shared-memory word of run r
     // Box copies (tma = 1): dimension k of the tensor maps covers address bits
     // [dim_lo[k], dim_lo[k] + dim_len[k]) and its box the lowest dim_box[k] of them; nbox boxes
@@ -484,10 +487,10 @@ __global__ void __launch_bounds__(kStThreads, 1)
     uint64_t lane_g = 0, warp_g = 0;
 #pragma unroll
     for (int b = 0; b < 5; b++)
-        if ((lane >> b) & 1) { lane_s += P.lane_w[b]; lane_g += 1ull << P.lane_addr[b]; }
+        if ((lane >> b) & 1) { lane_s += P.lane_w[b]; lane_g += 1ull << P.dlane_addr[b]; }
 #pragma unroll
     for (int b = 0; b < kStWarpBits; b++)
-        if ((wid >> b) & 1) { warp_s += P.warp_w[b]; warp_g += 1ull << P.warp_addr[b]; }
+        if ((wid >> b) & 1) { warp_s += P.warp_w[b]; warp_g += 1ull << P.dwarp_addr[b]; }
     for (uint64_t j = grp; j < ntiles; j += kStGroups) {
         const uint64_t t = blockIdx.x + j * gridDim.x;
         const uint32_t stage = (uint32_t)(j % kStStages), phase = (uint32_t)(j / kStStages) & 1u;
@@ -547,7 +550,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
         uint64_t gs[kStRegs];
 #pragma unroll
         for (int l = 0; l < kStRegs; l++) {
-            gs[l] = 1ull << P.reg_addr[l];
+            gs[l] = 1ull << P.dreg_addr[l];
             asm volatile("" : "+l"(gs[l]));
         }
         const uint64_t base = st_tile_base(P, t) + lane_g + warp_g;
@@ -756,6 +759,9 @@ static bool plan_staged(const FusedGroup &g, uint32_t L, int boxes, StagedPlan &
         if (top > (uint32_t)kStCompWords) return false;
     }
     for (int b = 0; b < 5; b++) { P.lane_addr[b] = lane_addr[b]; P.lane_w[b] = weight[lane_addr[b]]; }
+    for (int b = 0; b < 5; b++) P.dlane_addr[b] = lane_addr[b];
+    for (int b = 0; b < kStRegs; b++) P.dreg_addr[b] = reg_addr[b];
+    for (int b = 0; b < kStWarpBits; b++) P.dwarp_addr[b] = warp_addr[b];
     for (int b = 0; b < kStRegs; b++) { P.reg_addr[b] = reg_addr[b]; P.reg_w[b] = weight[reg_addr[b]]; }
     for (int b = 0; b < kStWarpBits; b++) { P.warp_addr[b] = warp_addr[b]; P.warp_w[b] = weight[warp_addr[b]]; }
     P.ntiles = 1ull << (L - kStTileBits);
@@ -863,6 +869,49 @@ int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaSt
         default: return LYTH_E_UNSUPPORTED;
     }
     return last_launch_status();
+}
+
+// A permutation pass: the amplitude at index i moves to the index whose bit dst[j] is bit src[j]
+// of i (j < k <= 6; dst a permutation of src; other bits unchanged). The staged pass with no gates
+// and each tile bit stored at its image: the permuted bits are tile bits, so every tile maps onto
+// itself and the pass runs in place. LYTH_E_UNSUPPORTED when the state is too small for tiles.
+bool permute_supported(uint64_t len, const uint32_t *src, int k) {
+    if (k < 1 || k > kFuseMaxQubits || !len || (len & (len - 1))) return false;
+    uint32_t L = 0;
+    while ((1ull << L) < len) L++;
+    FusedGroup g{};
+    g.k = k;
+    for (int j = 0; j < k; j++) g.bits[j] = src[j];
+    StagedPlan P;
+    return plan_staged(g, L, 0, P);
+}
+
+int launch_permute(uint64_t len, const uint32_t *src, const uint32_t *dst, int k, float *re, float *im,
+                   cudaStream_t s) {
+    if (k < 1 || k > kFuseMaxQubits || !len || (len & (len - 1)) || (((uintptr_t)re | (uintptr_t)im) & 15))
+        return LYTH_E_UNSUPPORTED;
+    uint32_t L = 0;
+    while ((1ull << L) < len) L++;
+    FusedGroup g{};
+    g.k = k;
+    for (int j = 0; j < k; j++) g.bits[j] = src[j];
+    g.ngates = 0;
+    StagedPlan P;
+    CUtensorMap tre, tim;
+    memset(&tre, 0, sizeof tre);
+    memset(&tim, 0, sizeof tim);
+    bool ok = plan_staged(g, L, 1, P);
+    if (ok && P.tma && !encode_boxes(P, L, re, im, tre, tim)) ok = plan_staged(g, L, 0, P);
+    if (!ok) return LYTH_E_UNSUPPORTED;
+    auto image = [&](uint32_t a) {
+        for (int j = 0; j < k; j++)
+            if (src[j] == a) return dst[j];
+        return a;
+    };
+    for (int b = 0; b < 5; b++) P.dlane_addr[b] = image(P.lane_addr[b]);
+    for (int b = 0; b < kStRegs; b++) P.dreg_addr[b] = image(P.reg_addr[b]);
+    for (int b = 0; b < kStWarpBits; b++) P.dwarp_addr[b] = image(P.warp_addr[b]);
+    return launch_staged(P, tre, tim, re, im, s);
 }
 
 }  // namespace lyth

@@ -735,14 +735,84 @@ int physical_swap(lyth_sv *sv, uint32_t p1, uint32_t p2) {
     return LYTH_OK;
 }
 
-// Undo the qubit map with real swaps, so physical bit q holds logical qubit q.
-int normalize(lyth_sv *sv) {
-    for (uint32_t q = 0; q < sv->qubits; q++) {
-        if (sv->pos[q] != q) {
-            int st = physical_swap(sv, q, sv->pos[q]);
-            if (st) return st;
-        }
+// Move local bits src[j] -> dst[j] (j < k <= 6, dst a permutation of src) in one in-place pass
+// and update the map. LYTH_E_UNSUPPORTED: the state is below the staged pass's size.
+int permute_local(lyth_sv *sv, const std::vector<uint32_t> &src, const std::vector<uint32_t> &dst) {
+    const int k = (int)src.size();
+    if (sv->plan) {
+        if (!permute_supported(sv->local_len, src.data(), k)) return LYTH_E_UNSUPPORTED;  // as the engine
+        lyth_sv_op &op = record(sv, LYTH_SV_OP_PERMUTE, 0, 0, 0);
+        op.k = k;
+        for (int j = 0; j < k; j++) { op.bits[j] = src[j]; op.rbits[j] = dst[j]; }
+    } else {
+        const int st = launch_permute(sv->local_len, src.data(), dst.data(), k, sv->re, sv->im, sv->stream);
+        if (st) return st;
+        sv->launches++;
     }
+    sv->passes++;
+    std::vector<uint32_t> moved(k);
+    for (int j = 0; j < k; j++) moved[j] = sv->inv[src[j]];
+    for (int j = 0; j < k; j++) {
+        sv->inv[dst[j]] = moved[j];
+        sv->pos[moved[j]] = dst[j];
+    }
+    return LYTH_OK;
+}
+
+// Undo the qubit map, so physical bit q holds logical qubit q. The qubits that belong on rank bits
+// come home first by swaps; the local bits then hold a permutation of the local qubits, applied by
+// permutation passes of up to 6 bits each (a cycle of the permutation, several short ones
+// together, or a piece of a long one) instead of one swap pass per transposition.
+int normalize(lyth_sv *sv) {
+    const uint32_t L = sv->local_bits;
+    int st;
+    for (uint32_t q = L; q < sv->qubits; q++)
+        if (sv->pos[q] != q && (st = physical_swap(sv, q, sv->pos[q]))) return st;
+    // the cycles of sigma on the local bits (physical bit a's value belongs at bit inv[a]), all
+    // taken from the map before any pass
+    std::vector<std::vector<uint32_t>> cycles;
+    std::vector<bool> seen(L, false);
+    for (uint32_t p = 0; p < L; p++) {
+        if (seen[p] || sv->inv[p] == p) continue;
+        std::vector<uint32_t> cyc{p};
+        seen[p] = true;
+        for (uint32_t a = sv->inv[p]; a != p; a = sv->inv[a]) {
+            cyc.push_back(a);
+            seen[a] = true;
+        }
+        cycles.push_back(cyc);
+    }
+    std::vector<uint32_t> src, dst;
+    auto flush = [&]() -> int {
+        if (src.empty()) return LYTH_OK;
+        const int r = permute_local(sv, src, dst);
+        src.clear();
+        dst.clear();
+        return r;
+    };
+    st = LYTH_OK;
+    for (auto &cyc : cycles) {
+        while (cyc.size() > 1 && !st) {
+            const size_t m = cyc.size() < (size_t)kFuseMaxQubits ? cyc.size() : (size_t)kFuseMaxQubits;
+            if (src.size() + m > (size_t)kFuseMaxQubits && (st = flush())) break;
+            // bits cyc[0..m) rotate: cyc[i] -> cyc[i + 1], cyc[m - 1] -> cyc[0]
+            for (size_t i = 0; i < m; i++) {
+                src.push_back(cyc[i]);
+                dst.push_back(cyc[(i + 1) % m]);
+            }
+            if (m == cyc.size()) break;
+            // a longer cycle: cyc[0] now holds what belongs at cyc[m], and the rest is still a
+            // cycle through cyc[0], which needs a later pass
+            st = flush();
+            cyc.erase(cyc.begin() + 1, cyc.begin() + (long)m);
+        }
+        if (st) break;
+    }
+    if (!st) st = flush();
+    if (st && st != LYTH_E_UNSUPPORTED) return st;
+    // below the staged pass's size: one swap pass per transposition
+    for (uint32_t q = 0; q < L; q++)
+        if (sv->pos[q] != q && (st = physical_swap(sv, q, sv->pos[q]))) return st;
     return LYTH_OK;
 }
 

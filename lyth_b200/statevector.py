@@ -134,7 +134,7 @@ class StateVector:
         check(lib.lyth_sv_reset_timing(self._h), "reset_timing")
 
 
-_OP_NAMES = ("u", "cu", "fused", "exchange", "swap_local", "swap_lr", "swap_rr", "swap_multi")
+_OP_NAMES = ("u", "cu", "fused", "exchange", "swap_local", "swap_lr", "swap_rr", "swap_multi", "permute")
 
 
 class Plan:
@@ -148,7 +148,8 @@ class Plan:
       partner rank ^ (1 << a); this rank keeps its row;
     * ``swap_local`` (bits a, b), ``swap_lr`` (local bit a, rank bit b), ``swap_rr`` (rank bits);
     * ``swap_multi``: local bits ``bits[j]`` with rank bits ``rbits[j]`` in one exchange among the
-      2^k ranks that differ only in those rank bits.
+      2^k ranks that differ only in those rank bits;
+    * ``permute``: one local pass moving bit ``bits[j]`` to bit ``rbits[j]`` (the read-out).
     """
 
     def __init__(self, qubits: int, rank: int = 0, nranks: int = 1):
@@ -206,7 +207,7 @@ class Plan:
         for i in range(int(lib.lyth_sv_plan_count(self._h))):
             check(lib.lyth_sv_plan_op(self._h, i, C.byref(op)), "plan_op")
             d = {"kind": _OP_NAMES[op.kind], "a": op.a, "b": op.b, "c": op.c, "m": tuple(op.m)}
-            if op.kind == 7:
+            if op.kind in (7, 8):
                 d["bits"], d["rbits"] = list(op.bits[: op.k]), list(op.rbits[: op.k])
             if op.kind == 2:
                 bits = list(op.bits[: op.k])

@@ -134,6 +134,20 @@ def _swap_multi(vbits, rbits, rank, local_bits, re, im, run):
     return np.ascontiguousarray(cr[sl]), np.ascontiguousarray(ci[sl])
 
 
+def _permute(src, dst, re, im):
+    """The value at index i moves to the index whose bit dst[j] is bit src[j] of i."""
+    idx = np.arange(re.size, dtype=np.int64)
+    to = idx.copy()
+    for b in src:
+        to &= ~(1 << b)
+    for s_, d_ in zip(src, dst):
+        to |= ((idx >> s_) & 1) << d_
+    out_r, out_i = np.empty_like(re), np.empty_like(im)
+    out_r[to] = re
+    out_i[to] = im
+    return out_r, out_i
+
+
 def replay(ops, rank, local_bits, re, im):
     from oracle import oracle as orc
 
@@ -160,6 +174,8 @@ def replay(ops, rank, local_bits, re, im):
                 re, im = _trade((re, im), rank ^ (1 << a) ^ (1 << b))
         elif k == "swap_multi":
             re, im = _swap_multi(op["bits"], op["rbits"], rank, local_bits, re, im, run)
+        elif k == "permute":
+            re, im = _permute(op["bits"], op["rbits"], re, im)
         else:
             raise AssertionError(k)
     return re, im
@@ -258,3 +274,28 @@ def test_plan_handle_needs_no_gpu():
         # gates run = gates given minus swaps (relabels)
         run = sum(len(o["gates"]) if o["kind"] == "fused" else 1 for o in ops)
         assert run == sum(not isinstance(g, cc.Swap) for g in gates)
+
+
+def test_readout_permutation_passes_replay_bit_exact():
+    # 16 qubits on one rank: the read-out undoes the qubit map with permutation passes (the staged
+    # pass's size); replayed with the oracle's gates and numpy, the result is the oracle's.
+    import sys
+
+    sys.path.insert(0, ROOT)
+    from lyth_b200 import circuit as cc
+    from lyth_b200.statevector import Plan
+    from oracle import oracle as orc
+    from tests.test_gpu_statevector import as_tuples
+
+    q = 16
+    gates = cc.layered(q, 3, cc.Rng(cc.BENCH_SEED))
+    re0, im0 = orc.random_state(700, q)
+    want_r, want_i = orc.run_gates(as_tuples(gates), re0, im0)
+    with Plan(q, 0, 1) as p:
+        p.apply(gates)
+        p.finish()
+        ops = p.ops()
+    assert any(o["kind"] == "permute" for o in ops)
+    re, im = replay(ops, 0, q, re0.copy(), im0.copy())
+    assert np.array_equal(re.view(np.uint32), want_r.view(np.uint32))
+    assert np.array_equal(im.view(np.uint32), want_i.view(np.uint32))
