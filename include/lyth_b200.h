@@ -551,6 +551,10 @@ int lyth_sv_set_swap_batch(lyth_sv *sv, int max_qubits);
  * flags; the default when every rank could map every peer), 0 = NCCL send / recv. Collective:
  * every rank sets the same value at the same point. lyth_sv_transport reports the one in use. */
 int lyth_sv_set_transport(lyth_sv *sv, int copy_engine);
+/* The exchanges' pipeline chunk in amplitudes per component (a power of two from 1024 up to the
+ * allocated 2^28, or the shard if smaller; the default is the largest). Collective. Smaller
+ * chunks cut every exchange into more pipelined pieces (used by the tests to drive many). */
+int lyth_sv_set_chunk(lyth_sv *sv, uint64_t elements);
 int lyth_sv_transport(const lyth_sv *sv);
 int lyth_sv_set_timing(lyth_sv *sv, int on);
 int lyth_sv_timing(lyth_sv *sv, int cls, uint64_t *count, double *ms);

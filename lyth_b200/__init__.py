@@ -120,6 +120,7 @@ _sig("lyth_sv_set_remap", _i32, [_vp, _i32])
 _sig("lyth_sv_set_swap_batch", _i32, [_vp, _i32])
 _sig("lyth_sv_set_transport", _i32, [_vp, _i32])
 _sig("lyth_sv_transport", _i32, [_vp])
+_sig("lyth_sv_set_chunk", _i32, [_vp, _u64])
 _sig("lyth_sv_plan_create", _i32, [C.POINTER(_vp), _u32, _i32, _i32])
 _sig("lyth_sv_plan_count", _u64, [_vp])
 _sig("lyth_sv_plan_op", _i32, [_vp, _u64, C.POINTER(SvOp)])

@@ -600,6 +600,14 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
     // elements per partner per chunk: a chunk buffer holds P slices
     uint64_t C = sv->chunk >> (k == 1 ? 0 : k);
     if (C > sub) C = sub;
+    // Over the copy engines a swap-in is cut into at least 8 chunks (of >= 2^24 amplitudes), so
+    // the first pack and the last unpack, the parts the pipeline cannot hide, stay short; copy-
+    // engine pulls keep their bandwidth at that size.
+    if (sv->ce) {
+        uint64_t c8 = sub >> 3;
+        if (c8 < (1ull << 24)) c8 = 1ull << 24;
+        if (C > c8) C = c8;
+    }
     const uint64_t nchunks = sub / C;
     const unsigned gx_cap = sv->ce ? (unsigned)device_sms() * 2u : (unsigned)device_sms() / 2u;
     unsigned gx = stream_grid(C / 4 + 1, 1024);
@@ -1234,6 +1242,20 @@ int lyth_sv_set_transport(lyth_sv *sv, int copy_engine) {
 }
 
 int lyth_sv_transport(const lyth_sv *sv) { return sv && sv->ce ? 1 : 0; }
+
+int lyth_sv_set_chunk(lyth_sv *sv, uint64_t elements) {
+    if (!sv) return LYTH_E_INVALID;
+    const uint64_t cap = sv->local_len < kChunk ? sv->local_len : kChunk;
+    if (elements < 1024 || (elements & (elements - 1)) || elements > cap) return LYTH_E_UNSUPPORTED;
+    if (!sv->plan) {
+        DeviceGuard guard(sv);
+        int st = status_of(cudaStreamSynchronize(sv->comm_stream));
+        if (!st) st = status_of(cudaStreamSynchronize(sv->stream));
+        if (st) return st;
+    }
+    sv->chunk = elements;
+    return LYTH_OK;
+}
 
 int lyth_sv_set_swap_batch(lyth_sv *sv, int max_qubits) {
     if (!sv) return LYTH_E_INVALID;

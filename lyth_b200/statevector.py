@@ -116,6 +116,10 @@ class StateVector:
         NCCL (False). Collective: every rank sets the same value at the same point."""
         check(lib.lyth_sv_set_transport(self._h, int(copy_engine)), "set_transport")
 
+    def set_chunk(self, elements: int) -> None:
+        """Exchange pipeline chunk, amplitudes per component (power of two >= 1024). Collective."""
+        check(lib.lyth_sv_set_chunk(self._h, elements), "set_chunk")
+
     @property
     def transport(self) -> str:
         return "copy_engine" if lib.lyth_sv_transport(self._h) else "nccl"

@@ -17,7 +17,7 @@ def _ngpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _worker(rank, nranks, q, case, nid, out_dir, remap=True, batch=6, ce=True):
+def _worker(rank, nranks, q, case, nid, out_dir, remap=True, batch=6, ce=True, chunk=None):
     import sys
 
     sys.path.insert(0, ROOT)
@@ -36,6 +36,8 @@ def _worker(rank, nranks, q, case, nid, out_dir, remap=True, batch=6, ce=True):
         sv.set_remap(remap)
         sv.set_swap_batch(batch)
         sv.set_transport(ce)
+        if chunk:
+            sv.set_chunk(chunk)
         transport = sv.transport
         sv.set_local(np.ascontiguousarray(re0[lo:hi]), np.ascontiguousarray(im0[lo:hi]))
         sv.apply(gates)
@@ -72,12 +74,12 @@ def case_gates(case, q):
     return "rank-bit gates", q, g
 
 
-def _run_ranks(nranks, q, case, remap, batch, tmp_path, ce=True):
+def _run_ranks(nranks, q, case, remap, batch, tmp_path, ce=True, chunk=None):
     import lyth_b200 as lb
 
     nid = lb.unique_id()
     ctx = torch.multiprocessing.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, nranks, q, case, nid, str(tmp_path), remap, batch, ce))
+    procs = [ctx.Process(target=_worker, args=(r, nranks, q, case, nid, str(tmp_path), remap, batch, ce, chunk))
              for r in range(nranks)]
     for p in procs:
         p.start()
@@ -100,6 +102,15 @@ def test_two_ranks_bit_exact(case, remap, tmp_path):
 
 
 @pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("ce", [True, False])
+@pytest.mark.parametrize("case", [0, 2])
+def test_two_ranks_many_chunks(case, ce, tmp_path):
+    # 1024-amplitude chunks: every swap-in and exchange runs as a long pipeline, so both send and
+    # receive slots are reused many times within one exchange (flags, events, slot waits)
+    _run_ranks(2, 18, case, True, 6, tmp_path, ce=ce, chunk=1024)
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("case", [0, 2])
 def test_two_ranks_nccl_transport(case, tmp_path):
     _run_ranks(2, 18, case, True, 6, tmp_path, ce=False)
@@ -111,6 +122,12 @@ def test_two_ranks_nccl_transport(case, tmp_path):
 def test_four_ranks_bit_exact(case, batch, tmp_path):
     # two rank bits: batch 6 takes the batched (all-to-all among 4 ranks) swap-ins
     _run_ranks(4, 19, case, True, batch, tmp_path)
+
+
+@pytest.mark.skipif(_ngpus() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("batch", [1, 6])
+def test_four_ranks_many_chunks(batch, tmp_path):
+    _run_ranks(4, 19, 0, True, batch, tmp_path, chunk=1024)
 
 
 @pytest.mark.skipif(_ngpus() < 4, reason="needs 4 GPUs")
