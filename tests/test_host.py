@@ -150,3 +150,48 @@ def test_fused_layout_selftest():
     st = lb.lib.lyth_b200_fused_layout_selftest(20_260_930, 4000, C.byref(planned), C.byref(boxes))
     assert st == 0, f"layout check {st} failed"
     assert planned.value == 4000 and boxes.value > 500
+
+
+def test_plan_handle_settings_are_validated_on_the_host():
+    # Plan handles take the engine's settings with the engine's checks and no device.
+    import lyth_b200 as lb
+    from lyth_b200.statevector import Plan
+
+    with Plan(20, 0, 2) as p:
+        for bad in (0, 7):
+            with pytest.raises(lb.LythError):
+                p.set_fusion(bad)
+            with pytest.raises(lb.LythError):
+                p.set_swap_batch(bad)
+        assert lb.lib.lyth_sv_set_chunk(p._h, 1000) == lb.E_UNSUPPORTED   # not a power of two
+        assert lb.lib.lyth_sv_set_chunk(p._h, 512) == lb.E_UNSUPPORTED    # below 1024
+        assert lb.lib.lyth_sv_set_chunk(p._h, 1 << 20) == lb.E_UNSUPPORTED  # beyond the shard
+        assert lb.lib.lyth_sv_set_chunk(p._h, 1 << 12) == lb.OK
+        # no peers are mapped on a plan handle: the copy-engine transport is refused
+        assert lb.lib.lyth_sv_set_transport(p._h, 1) == lb.E_UNSUPPORTED
+        assert lb.lib.lyth_sv_set_transport(p._h, 0) == lb.OK
+        assert lb.lib.lyth_sv_transport(p._h) == 0
+    with pytest.raises(lb.LythError):
+        Plan(20, 2, 2)   # rank out of range
+    with pytest.raises(lb.LythError):
+        Plan(20, 0, 3)   # not a power of two
+    with pytest.raises(lb.LythError):
+        Plan(2, 0, 4)    # fewer than two local qubits
+
+
+def test_plan_counters_do_not_depend_on_the_chunk():
+    # Bytes sent and exchanges are properties of the schedule, not of its pipelining.
+    from lyth_b200 import circuit as cc
+    from lyth_b200.statevector import Plan
+
+    gates = cc.layered(20, 2, cc.Rng(cc.BENCH_SEED))
+    stats = []
+    for chunk in (None, 1 << 12):
+        with Plan(20, 1, 4) as p:
+            if chunk:
+                import lyth_b200 as lb
+                assert lb.lib.lyth_sv_set_chunk(p._h, chunk) == lb.OK
+            p.apply(gates)
+            p.finish()
+            stats.append(p.stats())
+    assert stats[0] == stats[1] and stats[0]["exchanges"] > 0
