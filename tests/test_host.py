@@ -195,3 +195,33 @@ def test_plan_counters_do_not_depend_on_the_chunk():
             p.finish()
             stats.append(p.stats())
     assert stats[0] == stats[1] and stats[0]["exchanges"] > 0
+
+
+@pytest.mark.parametrize("k", [2, 3, 4, 5, 6])
+def test_engine_fusion_groups_match_lyth_circuit_fuse(k):
+    # lyth-circuit's fuse (lib.rs:72-100, restated in circuit.fuse) against the engine's own groups,
+    # read from a plan handle: on circuits without SWAPs (the engine relabels those instead of
+    # fusing them) and with no group above the engine's 48-gate cap, the groups are the same gates
+    # on the same qubits, in the same order.
+    from lyth_b200 import circuit as cc
+    from lyth_b200.statevector import Plan
+
+    rng = cc.Rng(20_260_930)
+    circuits = [(12, cc.ghz(12)), (10, cc.qft(10, rng)), (10, cc.random(10, 20, rng)), (14, cc.random(14, 12, rng))]
+    for q, gates in circuits:
+        gates = [g for g in gates if not isinstance(g, cc.Swap)]
+        want = cc.fuse(gates, k)
+        if any(len(grp.gates) > 48 for grp in want):
+            continue
+        with Plan(q, 0, 1) as p:
+            p.set_fusion(k)
+            p.apply(gates)
+            ops = p.ops()
+        got = []
+        for o in ops:
+            if o["kind"] == "fused":
+                got.append(sorted({b for t, c, _ in o["gates"] for b in (t, c) if b >= 0}, reverse=True))
+            else:
+                assert o["kind"] in ("u", "cu"), o["kind"]
+                got.append(sorted({o["a"]} | ({o["b"]} if o["kind"] == "cu" else set()), reverse=True))
+        assert got == [grp.qubits for grp in want], (q, k)
