@@ -60,7 +60,7 @@ def test_circuits_bit_exact(cuda, case):
 
 @pytest.mark.parametrize("case", [1, 2, 4])
 def test_fused_equals_unfused_at_every_k(cuda, case):
-    # ADR-0030 Q1: a fused circuit is the unfused circuit, bit for bit, for k = 1..5.
+    # ADR-0030 Q1: a fused circuit is the unfused circuit, bit for bit, for k = 1..6.
     name, q, gates = suite()[case]
     re0, im0 = orc.random_state(200 + case, q)
     ur, ui, ust = run_engine(q, gates, re0, im0, fuse=1)
