@@ -834,6 +834,7 @@ int fused_take_device_error() {
     return LYTH_OK;
 }
 
+// LYTH_FUSED_STAGING=0 sends every group to the register pass (an A/B switch: both are bit-exact).
 static bool staging_enabled() {
     static int on = -1;
     if (on < 0) {
