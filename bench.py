@@ -18,6 +18,9 @@ One JSON line on rank 0:
                shard from pinned host memory, applies the layer, and reads the shard back.
   * cpu_baseline  the host evaluator port (oracle/) on a bounded sample, rank 0, N = 1.
   * per_kernel HBM GB/s of every other kernel class at its BASELINE config (rank 0, N = 1).
+  * sharded_streams  at N > 1: saxpy over 2^33 elements split into one contiguous range per rank
+               (independent units, no collective), aggregate GB/s over the max of the ranks'
+               device times.
 
 ``--impl reference`` times the reference's algorithm on the host cores instead (the oracle
 port: the reference is Rust and cannot be built in this image) and prints the same line.
@@ -71,6 +74,7 @@ def args_():
     ap.add_argument("--skip-kernels", action="store_true", help="omit the per-kernel table")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-streams", action="store_true", help="omit the sharded-stream line at N > 1")
     ap.add_argument("--cpu-qubits", type=int, default=25)
     ap.add_argument("--fuse", type=int, default=None, help="max qubits per fused pass (1..6; default: the engine's)")
     ap.add_argument("--swap-batch", type=int, default=None,
@@ -440,6 +444,52 @@ def run_case(name: str, reps: int) -> None:
     print(json.dumps({"case": name, "reps": reps, kind: amount}))
 
 
+# --------------------------------------------------------------------------- sharded streams
+def sharded_streams(dist: Dist, peak: float, log2n: int = 33, reps: int = 5) -> dict:
+    """saxpy over 2^log2n elements, one contiguous range per rank (lyth_b200.stream_range): the
+    large streams shard as independent units with no collective on the data path. Device time of
+    `reps` launches per rank, max over ranks; every rank takes the same collective steps whatever
+    happens locally, so a local failure is reported instead of hanging the others."""
+    import torch
+
+    import lyth_b200 as lb
+
+    n = 1 << log2n
+    off, cnt = lb.stream_range(n, dist.rank, dist.world)
+    ok, ms, x, y = 1.0, 0.0, None, None
+    try:
+        x = torch.empty(cnt, dtype=torch.float32, device="cuda").uniform_(-1.0, 1.0)
+        y = torch.empty(cnt, dtype=torch.float32, device="cuda").uniform_(-1.0, 1.0)
+        for _ in range(3):
+            lb.saxpy(2.5, x, y)
+        torch.cuda.synchronize()
+    except Exception:
+        ok = 0.0
+    dist.barrier()
+    if ok:
+        try:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                lb.saxpy(2.5, x, y)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+        except Exception:
+            ok = 0.0
+    dist.barrier()
+    ms = dist.max(ms)
+    failed = dist.sum(1.0 - ok)
+    del x, y
+    torch.cuda.empty_cache()
+    if failed:
+        return {"error": f"{int(failed)} rank(s) could not run their range"}
+    gbs = 12.0 * n / (ms * 1e-3) / 1e9
+    return {"kernel": "saxpy", "elements": n, "elements_per_rank": cnt, "ms": round(ms, 4),
+            "GB_s_aggregate": round(gbs, 1), "frac_hbm_per_gpu": round(gbs / dist.world / peak, 4),
+            "collective": "none", "l2": "inputs larger than L2"}
+
+
 # --------------------------------------------------------------------------- our arm
 def ours(a, dist: Dist) -> None:
     import numpy as np
@@ -565,6 +615,8 @@ def ours(a, dist: Dist) -> None:
     sv.close()
     torch.cuda.empty_cache()
 
+    streams = sharded_streams(dist, pk["hbm_gbs"]) if dist.world > 1 and not a.skip_streams else None
+
     cpu = None
     kernels = None
     if dist.rank == 0 and dist.world == 1:
@@ -598,6 +650,8 @@ def ours(a, dist: Dist) -> None:
                                     "kind": "port", "sample": cpu["sample"]}
         if kernels:
             line["per_kernel"] = kernels
+        if streams:
+            line["sharded_streams"] = streams
         print(json.dumps(line), flush=True)
 
 

@@ -175,6 +175,19 @@ def _f32t():
 
 
 # ----------------------------------------------------------------------------- streams
+def stream_range(n: int, rank: int, world: int, align: int = 1024) -> tuple[int, int]:
+    """This rank's contiguous range (offset, count) of an n-element stream split over `world`
+    ranks: independent units, no collective (the streams are elementwise). Boundaries fall on
+    multiples of `align` elements (16-byte aligned slices keep the vector paths); the ranges
+    cover [0, n) exactly once, the last rank taking the remainder."""
+    if world < 1 or not 0 <= rank < world or n < 0 or align < 1:
+        raise ValueError("bad range request")
+    per = (n // world) // align * align
+    off = rank * per
+    cnt = per if rank < world - 1 else n - off
+    return off, cnt
+
+
 def saxpy(a: float, x, y, stream=None) -> None:
     """examples/saxpy.lyth: y = fma(a, x, y), in place on y."""
     check(lib.lyth_b200_saxpy(y.numel(), a, _ptr(x, _f32t(), "x"), _ptr(y, _f32t(), "y"), _stream(stream)), "saxpy")

@@ -299,3 +299,53 @@ def test_readout_permutation_passes_replay_bit_exact():
     re, im = replay(ops, 0, q, re0.copy(), im0.copy())
     assert np.array_equal(re.view(np.uint32), want_r.view(np.uint32))
     assert np.array_equal(im.view(np.uint32), want_i.view(np.uint32))
+
+
+def _range_worker(rank, world, port, out_dir):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    import torch.distributed as dist
+
+    import lyth_b200 as lb
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        rows = []
+        for n in (0, 1, 1000, 1 << 20, (1 << 20) + 3, 1 << 33):
+            off, cnt = lb.stream_range(n, rank, world)
+            got = [None] * world
+            dist.all_gather_object(got, (off, cnt))
+            rows.append((n, got))
+    finally:
+        dist.destroy_process_group()
+    import json
+
+    with open(os.path.join(out_dir, f"range{rank}.json"), "w") as f:
+        json.dump(rows, f)
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_stream_ranges_cover_once(world, tmp_path):
+    # Large streams shard as contiguous ranges, one per rank, with no collective on the data
+    # path: every rank derives the same partition, which covers [0, n) once, 16-byte aligned.
+    import json
+
+    port = _free_port()
+    ctx = torch.multiprocessing.get_context("spawn")
+    procs = [ctx.Process(target=_range_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for r, p in enumerate(procs):
+        assert p.exitcode == 0, r
+    tables = [json.load(open(tmp_path / f"range{r}.json")) for r in range(world)]
+    for rows in tables[1:]:
+        assert rows == tables[0]  # the same partition everywhere
+    for n, got in tables[0]:
+        pos = 0
+        for off, cnt in got:
+            assert off == pos and cnt >= 0 and off % 1024 == 0
+            pos += cnt
+        assert pos == n
