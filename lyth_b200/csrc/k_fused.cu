@@ -297,17 +297,23 @@ static FusedGroup arrange_levels(const FusedGroup &g, bool split) {
 //    bytes or more per lane half. Register levels are the group's other bits, filled up to five
 //    with the lowest free bits ("batch" levels: independent tuples side by side). Warp bits are
 //    the next free bits.
-//  * one persistent CTA per SM, 16 warps in two groups of 8 that take alternate tiles. A tile's
-//    contiguous runs (>= 512 B) are copied into a 3-stage ring of shared memory with 1-D bulk
-//    copies (cp.async.bulk, no multicast) completing on an mbarrier; each warp reads its 32
+//  * one persistent CTA per SM, 16 warps in two groups of 8 that take alternate tiles. A tile is
+//    copied into a 3-stage ring of shared memory, completing on an mbarrier: as 1-D bulk copies
+//    of its contiguous runs (cp.async.bulk) when the runs are >= 2 KiB, else as one to eight
+//    rank-5 tensor-map boxes (cp.async.bulk.tensor.5d, one box dimension per range of
+//    consecutive tile bits; many short runs cost one request each, a box one request for all),
+//    never with multicast. Each warp reads its 32
 //    amplitudes per lane from shared memory and releases the stage, and warp 0 of the group,
 //    once its whole group has read the stage, issues the tile three ahead into it. The gates
 //    then run in registers and the results go to global memory directly (coalesced streaming
 //    stores). Up to three tiles (192 KiB) are in flight per SM whatever the warps are doing,
 //    and no warp is set aside for copies (16 warps x 128 registers fill the register file).
-//  * with a group bit on lane bit 4, the runs whose copy of that bit is 1 sit 16 words further
-//    along modulo 32 (a 32-word pad after every two runs, that bit the lowest run-index bit),
-//    so the two lane halves read disjoint banks.
+//  * with a group bit on lane bit 4, the two lane halves read disjoint banks: as runs, those
+//    whose copy of that bit is 1 sit 16 words further along modulo 32 (a 32-word pad after every
+//    two runs, that bit the lowest run-index bit); as boxes, that bit is the box dimension right
+//    after address bits 0..3, 16 words.
+//  * with no gates and each tile bit stored at its image under a permutation of the group's bits,
+//    the same pass permutes the state in place (launch_permute: every tile maps onto itself).
 //  * gates on register levels run the packed chains above; a gate on a lane bit fetches both
 //    values of each pair from the two lanes by indexed shuffles and computes this lane's row.
 //    The arithmetic per amplitude is the same chain in the same order, so the result is
