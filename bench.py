@@ -53,6 +53,22 @@ FUSED_PASS_DRAM_BYTES_PER_AMP = 15.787
 L2_BYTES = 126 * 1024 * 1024
 
 
+def circuit_module():
+    """lyth_b200/circuit.py (the host side of lyth-circuit: gates, Rng, circuits) loaded by path,
+    without importing the lyth_b200 package: the reference arm must map no library of this
+    repository except the oracle's."""
+    import importlib.util
+
+    name = "lyth_circuit_host"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, "lyth_b200", "circuit.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -75,7 +91,11 @@ def args_():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-streams", action="store_true", help="omit the sharded-stream line at N > 1")
-    ap.add_argument("--cpu-qubits", type=int, default=25)
+    ap.add_argument("--cpu-qubits", type=int, default=30, help="host state size of the cpu_baseline sample")
+    ap.add_argument("--ref-qubits", type=int, default=30, help="host state size of the reference arm's steps")
+    ap.add_argument("--ref-gates", type=int, default=1, help="gates per reference-arm step")
+    ap.add_argument("--parity-qubits", type=int, default=22)
+    ap.add_argument("--skip-parity", action="store_true")
     ap.add_argument("--fuse", type=int, default=None, help="max qubits per fused pass (1..6; default: the engine's)")
     ap.add_argument("--swap-batch", type=int, default=None,
                     help="most rank-bit qubits per swap-in (1..6; default: the engine's)")
@@ -199,6 +219,15 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
         return float(t.item())
 
+    def min(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MIN)
+        return float(t.item())
+
     def bcast_bytes(self, b: bytes | None) -> bytes:
         if not self.pg:
             return b
@@ -213,64 +242,132 @@ class Dist:
 
 
 # --------------------------------------------------------------------------- CPU baseline
-def cpu_sample(qubits: int, budget_s: float = 15.0) -> dict:
-    """The oracle port applying the layered circuit's gates on a 2^qubits state, all host cores,
-    for about budget_s; gates/s scaled to the 33-qubit state (work is linear in the state)."""
+def host_state(qubits: int, seed: int = 3):
+    """A seeded random state for the host samples: re, im ~ U[-1, 1) from two SplitMix64 streams
+    (the oracle's generator), scaled in place to unit norm (f64 sum over chunks). Two arrays of
+    2^qubits f32 and nothing else, so a 30-qubit sample holds 8 GiB."""
     import numpy as np
 
-    from lyth_b200 import circuit as cc
     from oracle import oracle as orc
 
-    gates = cc.layered(qubits, 2, cc.Rng(cc.BENCH_SEED))
-    re, im = orc.random_state(3, qubits)
-    done, t0 = 0, time.perf_counter()
-    for g in gates:
-        if isinstance(g, cc.U):
-            orc.gate_q(1 << g.q, cc.f32s(g.m), re, im, inplace=True)
-        elif isinstance(g, cc.CU):
-            wc, wt = orc.widths_ct(g.c, g.t)
-            orc.cu_q(wc, wt, cc.f32s(g.m), re, im, inplace=True)
-        else:
-            wc, wt = orc.widths_ct(g.a, g.b)
-            orc.swap_q(wc, wt, re, im, inplace=True)
+    n = 1 << qubits
+    re, im = orc.uniform(seed, n), orc.uniform(seed + 1, n)
+    norm2, step = 0.0, 1 << 24
+    for a in (re, im):
+        for i in range(0, n, step):
+            c = a[i:i + step].astype(np.float64)
+            norm2 += float(np.dot(c, c))
+    f = np.float32(1.0 / np.sqrt(norm2))
+    re *= f
+    im *= f
+    return re, im
+
+
+def apply_host_gate(cc, orc, g, re, im):
+    """One gate of the circuit with the host evaluator port, unfused, in place (lyth-circuit's
+    execute on the host: gate_q / cu_q / swap_q over the whole state)."""
+    if isinstance(g, cc.U):
+        orc.gate_q(1 << g.q, cc.f32s(g.m), re, im, inplace=True)
+    elif isinstance(g, cc.CU):
+        wc, wt = orc.widths_ct(g.c, g.t)
+        orc.cu_q(wc, wt, cc.f32s(g.m), re, im, inplace=True)
+    else:
+        wc, wt = orc.widths_ct(g.a, g.b)
+        orc.swap_q(wc, wt, re, im, inplace=True)
+
+
+class HostSample:
+    """The host evaluator port applying the benchmark circuit's gates on a 2^qubits state, all host
+    cores. Each `run(ngates)` applies the next gates of the circuit in order and returns the seconds
+    it took; work per gate is one pass over the state, so gates/s at 33 qubits is gates/s at this
+    size x 2^(qubits - 33)."""
+
+    def __init__(self, qubits: int, qubits_config: int = 33):
+        cc = circuit_module()
+        from oracle import oracle as orc
+
+        self.cc, self.orc, self.q, self.qc = cc, orc, qubits, qubits_config
+        # the layered circuit at the sample's size: the 33-qubit layer's gate mix (H on every qubit,
+        # CU(phase) on adjacent pairs, SWAP on a random pairing) in circuit order
+        self.gates = cc.layered(qubits, 2, cc.Rng(cc.BENCH_SEED))
+        self.re, self.im = host_state(qubits)
+        self.pos = 0
+
+    def run(self, ngates: int) -> float:
+        t0 = time.perf_counter()
+        for _ in range(ngates):
+            g = self.gates[self.pos % len(self.gates)]
+            apply_host_gate(self.cc, self.orc, g, self.re, self.im)
+            self.pos += 1
+        return time.perf_counter() - t0
+
+    def scale(self) -> float:
+        return float(2.0 ** (self.q - self.qc))
+
+    def cores(self) -> int:
+        return self.orc.threads()
+
+    def describe(self, ngates: int) -> str:
+        return (f"{ngates} gate(s) per step of the layered circuit (H, CU(phase), SWAP in circuit order) applied "
+                f"by the host evaluator port (oracle/lythref.c, unfused, in place) to a {self.q}-qubit state "
+                f"(2^{self.q} amplitudes) on {self.cores()} host threads; gates/s scaled to {self.qc} qubits by "
+                f"2^{self.q - self.qc} (each gate is one pass over the state, so its work is linear in the state)")
+
+
+def cpu_sample(qubits: int, budget_s: float = 15.0) -> dict:
+    """The host evaluator port on a bounded sample (about budget_s of host time) of the benchmark
+    circuit's gates on a 2^qubits state, all host cores; gates/s scaled to 33 qubits."""
+    hs = HostSample(qubits)
+    done, dt = 0, 0.0
+    while dt < budget_s:
+        dt += hs.run(1)
         done += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
-    dt = time.perf_counter() - t0
     gps = done / dt
-    del np
     return {"gates": done, "seconds": dt, "gates_per_s_at_sample": gps,
-            "gates_per_s_at_33": gps / float(1 << (33 - qubits)), "cores": orc.threads(),
-            "sample": f"{done} gates of the layered circuit on a {qubits}-qubit state (oracle port, unfused, "
-                      f"in place), scaled to 33 qubits by 2^-{33 - qubits} (each gate is one pass over the state)"}
+            "gates_per_s_at_33": gps * hs.scale(), "cores": hs.cores(),
+            "sample": f"{done} gates in {dt:.1f} s: " + hs.describe(1)}
 
 
 def reference_arm(a, dist: Dist) -> None:
-    """--impl reference: the reference's algorithm on the host cores (the oracle port; the Rust
-    reference cannot be built here). Rank 0 only; the other ranks exit without work."""
+    """--impl reference: the reference's algorithm on the host cores -- its host evaluator, as the
+    oracle port (the Rust reference cannot be built in this image) -- on this arm's config. Rank 0
+    only; the other ranks exit without work. One step = a bounded sample of the 33-qubit layered
+    circuit: `--ref-gates` gates applied to a `--ref-qubits` state (default 30 qubits, the BASELINE
+    single-GPU size, 8 GiB of host memory), gates/s scaled to 33 qubits. No library of this
+    repository is loaded except the oracle's (the circuit generator is read by path)."""
     if dist.rank != 0:
         return
-    steps = []
+    hs = HostSample(a.ref_qubits)
     for _ in range(a.warmup):
-        cpu_sample(a.cpu_qubits, budget_s=2.0)
-    for _ in range(a.steps):
-        steps.append(cpu_sample(a.cpu_qubits, budget_s=8.0))
-    v = sum(s["gates"] for s in steps) / sum(s["seconds"] for s in steps) / float(1 << (33 - a.cpu_qubits))
-    cores = steps[0]["cores"]
+        hs.run(1)
+    secs = [hs.run(a.ref_gates) for _ in range(a.steps)]
+    t = sum(secs)
+    v = a.ref_gates * a.steps / t * hs.scale()
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "gates/s", "n_gpus": a.gpus,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 * 81 / v if v else None,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 * t / a.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: SplitMix64-seeded normalised random state, layered circuit seed 20260930",
-        "config": {"workload": "statevector layered circuit, 33 qubits, 81 gates per layer (one step = one layer)",
-                   "qubits": 33, "gates_per_step": 81},
-        "cpu_baseline": {"value": v, "unit": "gates/s", "cores": cores, "kind": "port",
-                         "sample": steps[0]["sample"]},
+        "data": "synthetic: SplitMix64-seeded random state scaled to unit norm; layered circuit seed 20260930",
+        "config": config_of(33, 81, a.gpus),
+        "step": f"{a.ref_gates} gate(s) of the 33-qubit layer on a {a.ref_qubits}-qubit host state "
+                f"(ms_per_step is that sample's host time)",
+        "cpu_baseline": {"value": v, "unit": "gates/s", "cores": hs.cores(), "kind": "port",
+                         "sample": hs.describe(a.ref_gates)},
         "e2e": {"value": v, "unit": "gates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "QuantumDrizzy/LYTH is Rust (no cargo/rustc in this image); its host evaluator is timed "
                 "through this repository's C restatement of it (oracle/lythref.c)",
     }
     print(json.dumps(line), flush=True)
+
+
+def config_of(q: int, per: int, world: int) -> dict:
+    import math
+
+    return {"workload": f"statevector layered circuit, {q} qubits, {per} gates per layer "
+                        "(H on every qubit, CU(phase) on adjacent pairs, SWAP on a random pairing), one step = one layer",
+            "qubits": q, "gates_per_step": per, "global_qubits": int(math.log2(world)) if world > 1 else 0,
+            "parallelism": f"sharded on the high {int(math.log2(world))} qubits" if world > 1 else "1 GPU, in place",
+            "l2": f"inputs larger than L2: the state is {8 * (1 << q) / 2**30:.0f} GiB"}
 
 
 # --------------------------------------------------------------------------- per-kernel table
@@ -448,20 +545,29 @@ def run_case(name: str, reps: int) -> None:
 def sharded_streams(dist: Dist, peak: float, log2n: int = 33, reps: int = 5) -> dict:
     """saxpy over 2^log2n elements, one contiguous range per rank (lyth_b200.stream_range): the
     large streams shard as independent units with no collective on the data path. Device time of
-    `reps` launches per rank, max over ranks; every rank takes the same collective steps whatever
-    happens locally, so a local failure is reported instead of hanging the others."""
+    `reps` launches per rank, max over ranks. Afterwards every rank checks its range: 4096 sampled
+    elements of y (and the range's first and last) against fma(2.5, x, y0) applied once per launch
+    on the host (the evaluator's saxpy), from saved copies of x and y0, and the ranges must tile [0, n) exactly. Every rank
+    takes the same collective steps whatever happens locally, so a local failure is reported
+    instead of hanging the others."""
+    import numpy as np
     import torch
 
     import lyth_b200 as lb
 
     n = 1 << log2n
     off, cnt = lb.stream_range(n, dist.rank, dist.world)
-    ok, ms, x, y = 1.0, 0.0, None, None
+    ok, ms, x, y, launches = 1.0, 0.0, None, None, 0
+    idx = None
     try:
         x = torch.empty(cnt, dtype=torch.float32, device="cuda").uniform_(-1.0, 1.0)
         y = torch.empty(cnt, dtype=torch.float32, device="cuda").uniform_(-1.0, 1.0)
+        g = np.random.default_rng(dist.rank)
+        idx = torch.from_numpy(np.unique(np.concatenate([[0, cnt - 1], g.integers(0, cnt, 4096)]))).cuda()
+        xs, y0s = x[idx].cpu().numpy(), y[idx].cpu().numpy()
         for _ in range(3):
             lb.saxpy(2.5, x, y)
+            launches += 1
         torch.cuda.synchronize()
     except Exception:
         ok = 0.0
@@ -472,22 +578,90 @@ def sharded_streams(dist: Dist, peak: float, log2n: int = 33, reps: int = 5) -> 
             e0.record()
             for _ in range(reps):
                 lb.saxpy(2.5, x, y)
+                launches += 1
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / reps
+            from oracle import oracle as orc
+
+            want = y0s.copy()
+            for _ in range(launches):
+                want = orc.saxpy(2.5, xs, want)
+            got = y[idx].cpu().numpy()
+            if not np.array_equal(got.view(np.uint32), want.view(np.uint32)):
+                ok = 0.0
         except Exception:
             ok = 0.0
     dist.barrier()
     ms = dist.max(ms)
     failed = dist.sum(1.0 - ok)
+    covered = dist.sum(float(cnt))
+    # contiguity: rank r's range must start where rank r-1's ended
+    ends = [None] * dist.world
+    if dist.pg:
+        dist.pg.all_gather_object(ends, (off, cnt))
+    else:
+        ends = [(off, cnt)]
+    tiles = all(ends[i][0] + ends[i][1] == ends[i + 1][0] for i in range(len(ends) - 1)) and ends[0][0] == 0
     del x, y
     torch.cuda.empty_cache()
     if failed:
-        return {"error": f"{int(failed)} rank(s) could not run their range"}
+        return {"error": f"{int(failed)} rank(s) could not run or verify their range"}
+    if int(covered) != n or not tiles:
+        return {"error": f"the ranges do not tile [0, {n}): {ends}"}
     gbs = 12.0 * n / (ms * 1e-3) / 1e9
     return {"kernel": "saxpy", "elements": n, "elements_per_rank": cnt, "ms": round(ms, 4),
             "GB_s_aggregate": round(gbs, 1), "frac_hbm_per_gpu": round(gbs / dist.world / peak, 4),
-            "collective": "none", "l2": "inputs larger than L2"}
+            "collective": "none", "l2": "inputs larger than L2",
+            "verified": "ranges tile [0, n); 4098 sampled elements per rank bit-exact vs fma on the host"}
+
+
+# --------------------------------------------------------------------------- parity before timing
+def sharded_parity(a, dist: Dist) -> dict:
+    """Bit-exactness on the same N ranks, before anything is timed: a `--parity-qubits` (default 22)
+    state sharded over the N ranks exactly as the timed run shards its state, two layers of the
+    layered circuit through the engine (fused staged passes, swap-ins of rank-bit qubits, SWAPs as
+    relabels, read-out undoing the qubit map), and every rank's shard compared bit for bit with the
+    host evaluator applying the same gates unfused in order to the same input
+    (crates/lyth-circuit/tests/fusion.rs:53-92). Every rank takes the same collective steps
+    whatever happens locally; `ok` is the minimum over ranks."""
+    import numpy as np
+
+    import lyth_b200 as lb
+    from lyth_b200 import circuit as cc
+    from oracle import oracle as orc
+
+    q = a.parity_qubits
+    ok, detail, gates, st = 1.0, "", [], {}
+    nid = lb.unique_id() if (dist.world > 1 and dist.rank == 0) else None
+    nid = dist.bcast_bytes(nid)
+    try:
+        gates = cc.layered(q, 2, cc.Rng(cc.BENCH_SEED + 1))
+        re0, im0 = orc.random_state(cc.BENCH_SEED + 1, q)
+        orc.set_threads(max(1, (os.cpu_count() or 1) // dist.world))
+        wr, wi = orc.run_gates(cc.as_tuples(gates), re0.copy(), im0.copy(), inplace=True)
+        with lb.StateVector(q, device=dist.local, rank=dist.rank, nranks=dist.world, nccl_id=nid) as sv:
+            n = sv.local_len
+            lo = dist.rank * n
+            sv.set_local(np.ascontiguousarray(re0[lo:lo + n]), np.ascontiguousarray(im0[lo:lo + n]))
+            sv.apply(gates)
+            sv.sync()
+            gr, gi = np.empty(n, np.float32), np.empty(n, np.float32)
+            sv.get_local(gr, gi)
+            st = sv.stats()
+        bad = int(np.count_nonzero(gr.view(np.uint32) != wr[lo:lo + n].view(np.uint32)))
+        bad += int(np.count_nonzero(gi.view(np.uint32) != wi[lo:lo + n].view(np.uint32)))
+        if bad:
+            ok, detail = 0.0, f"rank {dist.rank}: {bad} words differ"
+    except Exception as e:  # reported, not raised: the other ranks still take the same steps
+        ok, detail, st = 0.0, f"rank {dist.rank}: {type(e).__name__}: {str(e)[:120]}", {}
+    ok = dist.min(ok)
+    out = {"ok": bool(ok), "qubits": q, "ranks": dist.world, "layers": 2, "gates": len(gates),
+           "compare": "every rank's shard, bit for bit, against the host evaluator (unfused, in order)",
+           "engine_passes": st.get("passes"), "engine_exchanges": st.get("exchanges")}
+    if detail:
+        out["detail"] = detail
+    return out
 
 
 # --------------------------------------------------------------------------- our arm
@@ -501,6 +675,12 @@ def ours(a, dist: Dist) -> None:
 
     pk, pk_kind = peaks()
     q = a.qubits
+    parity = None if a.skip_parity else sharded_parity(a, dist)
+    if parity is not None and not parity["ok"]:
+        if dist.rank == 0:
+            print(json.dumps({"metric": METRIC, "value": None, "unit": "gates/s", "n_gpus": dist.world,
+                              "error": "parity check failed: no value is reported", "parity": parity}), flush=True)
+        return
     nid = lb.unique_id() if (dist.world > 1 and dist.rank == 0) else None
     nid = dist.bcast_bytes(nid)
     sv = lb.StateVector(q, device=dist.local, rank=dist.rank, nranks=dist.world, nccl_id=nid)
@@ -631,19 +811,14 @@ def ours(a, dist: Dist) -> None:
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: SplitMix64-seeded normalised random complex64 state (split re/im f32); "
                     "layered circuit from circuits::Rng seed 20260930",
-            "config": {"workload": f"statevector layered circuit, {q} qubits, {per} gates per layer "
-                                   "(H on every qubit, CU(phase) on adjacent pairs, SWAP on a random pairing), "
-                                   "one step = one layer",
-                       "qubits": q, "gates_per_step": per, "global_qubits": q - (sv.local_len.bit_length() - 1),
-                       "parallelism": f"sharded on the high {int(np.log2(dist.world))} qubits" if dist.world > 1
-                       else "1 GPU, in place",
-                       "l2": f"inputs larger than L2: the state is {8 * (1 << q) / 2**30:.0f} GiB"},
+            "config": config_of(q, per, dist.world),
             "roofline": roofline,
             "e2e": e2e,
             "gpu_launches": int(launches),
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"]},
             "engine": {"passes": st["passes"], "exchanges": st["exchanges"], "bytes_sent": st["bytes_sent"]},
+            "parity": parity,
         }
         if cpu:
             line["cpu_baseline"] = {"value": cpu["gates_per_s_at_33"], "unit": "gates/s", "cores": cpu["cores"],

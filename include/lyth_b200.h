@@ -436,6 +436,13 @@ int lyth_b200_matmul_bf16(uint32_t m, uint32_t n, uint32_t k, const uint16_t *a,
 /* LYTH_E_TIMEOUT when a bounded device-side wait of any kernel in this library ran out since the
  * last call (the flag is then cleared), else LYTH_OK. Synchronises with the current device. */
 int lyth_b200_device_error(void);
+/* Bounded-wait self-test (no counterpart in the reference, which has no device-side waits): one
+ * thread waits on something that never completes -- which = 0: an mbarrier phase, the wait of the
+ * TMA-fed kernels; which = 1: a device flag, the wait of the multi-GPU transport -- through the
+ * same wait functions, with a limit of limit_us microseconds (1 .. 2,000,000) instead of 2 s. The
+ * wait gives up and the kernel returns; lyth_b200_device_error then reports LYTH_E_TIMEOUT once.
+ * LYTH_E_INVALID for another `which` or limit. */
+int lyth_b200_wait_selftest(int which, uint32_t limit_us, cudaStream_t stream);
 
 /* gate_proj GEMV (fixtures/kernel/gate_proj_int4.json, fixtures/poly/gate-proj-int4-nf4.json:
  * cost contracts only; the reference has no kernel). y[r] = sum_k dequant(W)[r, k] * x[k].
@@ -448,7 +455,9 @@ int lyth_b200_device_error(void);
 #define LYTH_GEMV_NF4 1
 int lyth_b200_gemv_q4(int fmt, uint32_t rows, uint32_t k, uint32_t group, const uint8_t *w,
                       const uint16_t *scales, const uint16_t *x, uint16_t *y, cudaStream_t stream);
-/* The dequantised matrix (rows x k f32), through the same unpack the GEMV uses: bit-exact. */
+/* The dequantised matrix (rows x k f32, 16-byte aligned; k and group multiples of 8), decoded
+ * by the same device function the GEMV's kernels decode W with (decode_word, k_gemv.cu): INT4
+ * q * scale, exact; NF4 code * scale, one rounding. Bit-exact against the format's definition. */
 int lyth_b200_gemv_dequant(int fmt, uint32_t rows, uint32_t k, uint32_t group, const uint8_t *w,
                            const uint16_t *scales, float *out, cudaStream_t stream);
 /* The 16 NF4 levels (QLoRA's normal-float construction, computed on the host at load). */

@@ -126,6 +126,7 @@ _sig("lyth_sv_plan_count", _u64, [_vp])
 _sig("lyth_sv_plan_op", _i32, [_vp, _u64, C.POINTER(SvOp)])
 _sig("lyth_sv_plan_clear", _i32, [_vp])
 _sig("lyth_b200_device_error", _i32, [])
+_sig("lyth_b200_wait_selftest", _i32, [_i32, _u32, _vp])
 _sig("lyth_b200_fused_layout_selftest", _i32, [_u64, _u32, C.POINTER(_u32), C.POINTER(_u32)])
 
 

@@ -180,3 +180,17 @@ def layered(n: int, layers: int, rng: Rng):
 
 
 BENCH_SEED = 20260930
+
+
+def as_tuples(gates):
+    """The gates as (kind, q0, q1, m8) tuples -- kind 0 = U on q0, 1 = CU(c = q0, t = q1),
+    2 = SWAP(q0, q1) -- the form the host evaluator's ``run_gates`` takes."""
+    out = []
+    for g in gates:
+        if isinstance(g, U):
+            out.append((0, g.q, 0, f32s(g.m)))
+        elif isinstance(g, CU):
+            out.append((1, g.c, g.t, f32s(g.m)))
+        else:
+            out.append((2, g.a, g.b, [0.0] * 8))
+    return out

@@ -264,8 +264,13 @@ extern "C" int lyth_b200_matmul_bf16(uint32_t m, uint32_t n, uint32_t k, const u
 }
 
 extern "C" int lyth_b200_device_error(void) {
+    // every flag is read (and cleared) whichever reports first
     const int fused = fused_take_device_error();
+    const int gemv = gemv_take_device_error();
+    const int probe = probe_take_device_error();
     if (fused != LYTH_OK) return fused;
+    if (gemv != LYTH_OK) return gemv;
+    if (probe != LYTH_OK) return probe;
     int v = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
     if (e != cudaSuccess) return status_of(e);

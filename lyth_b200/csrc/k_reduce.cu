@@ -12,7 +12,10 @@
 // memory (DSMEM) and folds the eight in block order; a last single-block pass folds the
 // cluster results in cluster order. The combine order is therefore fixed and documented, and
 // the host oracle reproduces it exactly.
+#include <cuda.h>
+
 #include <cooperative_groups.h>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -225,10 +228,32 @@ namespace lyth {
 constexpr uint32_t kNoAllocClusters = 16384;
 static __device__ __align__(256) float g_noalloc_clusters[kNoAllocClusters];
 
-// The array's device address, looked up once per device with that device current (a host-side
-// use of the symbol's name is not a device address).
+// The array's device address, looked up with the device current (a host-side use of the
+// symbol's name is not a device address) on the first call in each CUDA context: it is cached per
+// device together with the context it was found in, and looked up again when the device's current
+// context is another one (after a cudaDeviceReset, say). A mutex guards the cache, so host threads
+// may call concurrently.
+typedef CUresult (*PFN_ctx_get_current)(CUcontext *);
+
+static CUcontext current_context() {
+    static PFN_ctx_get_current fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_ctx_get_current>(p);
+    });
+    CUcontext c = nullptr;
+    if (fn) fn(&c);
+    return c;
+}
+
 static float *noalloc_scratch(int *status) {
+    static std::mutex mu;
     static float *ptr_of[64] = {nullptr};
+    static CUcontext ctx_of[64] = {nullptr};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) {
@@ -239,7 +264,11 @@ static float *noalloc_scratch(int *status) {
         *status = LYTH_E_UNSUPPORTED;
         return nullptr;
     }
-    if (!ptr_of[dev]) {
+    // No context current on this thread yet (null) also means "look it up": the lookup makes
+    // the device's primary context current.
+    const CUcontext ctx = current_context();
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptr_of[dev] || !ctx || ctx_of[dev] != ctx) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_clusters);
         if (e != cudaSuccess) {
@@ -247,6 +276,7 @@ static float *noalloc_scratch(int *status) {
             return nullptr;
         }
         ptr_of[dev] = static_cast<float *>(p);
+        ctx_of[dev] = current_context();
     }
     *status = LYTH_OK;
     return ptr_of[dev];

@@ -24,10 +24,11 @@ LYTH_D uint64_t global_ns() {
     return t;
 }
 
-// Wait for the phase of parity `parity` to complete; on the limit set *err and return false.
-LYTH_D bool mbar_wait(uint32_t bar, uint32_t parity, int *err) {
+// Wait for the phase of parity `parity` to complete, giving up after `polls` polls or `ns` of
+// global-timer time; on the limit set *err and return false.
+LYTH_D bool mbar_wait_limited(uint32_t bar, uint32_t parity, int *err, uint32_t polls, uint64_t ns) {
     uint64_t t0 = 0;
-    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+    for (uint32_t i = 0; i < polls; ++i) {
         uint32_t ok;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -40,12 +41,33 @@ LYTH_D bool mbar_wait(uint32_t bar, uint32_t parity, int *err) {
         if ((i & 255u) == 0) {
             const uint64_t t = global_ns();
             if (i == 0) t0 = t;
-            else if (t - t0 > kWaitNs) break;
+            else if (t - t0 > ns) break;
         }
     }
     atomicExch(err, 1);
     return false;
 }
+// The kernels' wait: 2^24 polls or 2 s.
+LYTH_D bool mbar_wait(uint32_t bar, uint32_t parity, int *err) {
+    return mbar_wait_limited(bar, parity, err, kWaitPolls, kWaitNs);
+}
+
+// Wait until a 64-bit flag in global memory (this GPU's or a peer's, system scope) reaches
+// `target`, polling with acquire loads; on `ns` of global-timer time set *err and return false.
+LYTH_D bool flag_wait_bounded(const uint64_t *flag, uint64_t target, uint64_t ns, int *err) {
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        uint64_t v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+        if (v >= target) return true;
+        if (global_ns() - t0 > ns) {
+            atomicExch(err, 1);
+            return false;
+        }
+        __nanosleep(200);
+    }
+}
+
 LYTH_D void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }

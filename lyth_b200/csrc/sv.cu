@@ -33,6 +33,7 @@
 #include <vector>
 
 #include "fused.cuh"
+#include "mbar.cuh"
 
 namespace lyth {
 
@@ -207,20 +208,7 @@ struct FlagSet {
 __global__ void flag_wait_kernel(const __grid_constant__ FlagSet fs, uint64_t target) {
     const uint32_t t = threadIdx.x;
     if (t >= fs.n) return;
-    uint64_t t0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    for (;;) {
-        uint64_t v;
-        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(fs.flag[t]) : "memory");
-        if (v >= target) return;
-        uint64_t now;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-        if (now - t0 > 2000000000ull) {
-            atomicExch(&g_sv_error, 1);
-            return;
-        }
-        __nanosleep(200);
-    }
+    flag_wait_bounded(fs.flag[t], target, kWaitNs, &g_sv_error);
 }
 
 }  // namespace lyth
@@ -1228,8 +1216,10 @@ int lyth_sv_set_transport(lyth_sv *sv, int copy_engine) {
     if (copy_engine && sv->peer_flags.empty()) return LYTH_E_UNSUPPORTED;
     if (!sv->plan) {
         DeviceGuard guard(sv);
-        // drain the current transport before switching: partners must have pulled every chunk
+        // drain the current transport before switching: partners must have pulled every chunk,
+        // and this rank's own pulls on the copy stream must have landed
         int st = status_of(cudaStreamSynchronize(sv->comm_stream));
+        if (!st && sv->copy_stream) st = status_of(cudaStreamSynchronize(sv->copy_stream));
         if (!st) st = status_of(cudaStreamSynchronize(sv->stream));
         if (st) return st;
         if (sv->ce && !copy_engine)
@@ -1250,6 +1240,7 @@ int lyth_sv_set_chunk(lyth_sv *sv, uint64_t elements) {
     if (!sv->plan) {
         DeviceGuard guard(sv);
         int st = status_of(cudaStreamSynchronize(sv->comm_stream));
+        if (!st && sv->copy_stream) st = status_of(cudaStreamSynchronize(sv->copy_stream));
         if (!st) st = status_of(cudaStreamSynchronize(sv->stream));
         if (st) return st;
     }

@@ -300,12 +300,18 @@ def set_threads(n: int) -> None:
 
 
 # ---------------------------------------------------------------- circuits (unfused, in order)
-def run_gates(gates, re, im):
+def run_gates(gates, re, im, inplace=False):
     """Apply (kind, q0, q1, m8) gates in order, the unfused way lyth-circuit's execute does:
     kind 0 = gate_q on width 2^q0; 1 = cu_q with widths_ct(q0, q1); 2 = swap_q likewise.
-    Returns new (re, im); the inputs are not modified."""
-    re = _f32(re).copy()
-    im = _f32(im).copy()
+    Returns new (re, im); the inputs are not modified unless `inplace` (then they must be
+    contiguous f32 arrays, and are returned)."""
+    if inplace:
+        if not (isinstance(re, np.ndarray) and re.dtype == np.float32 and re.flags.c_contiguous
+                and isinstance(im, np.ndarray) and im.dtype == np.float32 and im.flags.c_contiguous):
+            raise ValueError("run_gates(inplace=True) needs contiguous float32 arrays")
+    else:
+        re = _f32(re).copy()
+        im = _f32(im).copy()
     for kind, q0, q1, m8 in gates:
         if kind == 0:
             re, im = gate_q(1 << q0, m8, re, im, inplace=True)

@@ -29,8 +29,10 @@ def to_dev(w, scales, x, rows, k, group, cuda):
 
 
 @pytest.mark.parametrize("fmt", [lb.GEMV_INT4, lb.GEMV_NF4])
-def test_dequant_bit_exact(cuda, fmt):
-    rows, k, group = 64, 1024, 64
+@pytest.mark.parametrize("rows,k,group", [(64, 1024, 64), (14336, 4096, 64), (3, 24, 8)])
+def test_dequant_bit_exact(cuda, fmt, rows, k, group):
+    # lyth_b200_gemv_dequant decodes W with the GEMV kernels' own decode (decode_word): a change
+    # to the hot decode (nibble order, the PRMT selectors, the INT4 offset) breaks this test.
     w, scales, x = problem(rows, k, group)
     wd, sd, _ = to_dev(w, scales, x, rows, k, group, cuda)
     out = torch.empty(rows * k, device=cuda)
@@ -40,7 +42,7 @@ def test_dequant_bit_exact(cuda, fmt):
 
 
 @pytest.mark.parametrize("fmt", [lb.GEMV_INT4, lb.GEMV_NF4])
-@pytest.mark.parametrize("rows,k,group", [(64, 1024, 64), (14336, 4096, 64), (1000, 2048, 128)])
+@pytest.mark.parametrize("rows,k,group", [(64, 1024, 64), (14336, 4096, 64), (1000, 2048, 128), (37, 3072, 1024)])
 def test_gemv_within_tolerance(cuda, fmt, rows, k, group):
     w, scales, x = problem(rows, k, group)
     wd, sd, xd = to_dev(w, scales, x, rows, k, group, cuda)
@@ -49,4 +51,21 @@ def test_gemv_within_tolerance(cuda, fmt, rows, k, group):
     got = y.cpu().numpy().astype(np.float64)
     ref = orc.gemv_f64(fmt, rows, k, group, w, scales, x)
     rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+    assert rel <= 1e-3, rel
+
+
+@pytest.mark.parametrize("fmt", [lb.GEMV_INT4, lb.GEMV_NF4])
+def test_gemv_is_the_dequantised_product(cuda, fmt):
+    # y against the f64 product of the DEVICE's dequantised matrix (the values the kernel's
+    # decode produces) with x: the same 1e-3 bar, so the GEMV multiplies what the dequant shows.
+    rows, k, group = 14336, 4096, 64
+    w, scales, x = problem(rows, k, group, seed=61)
+    wd, sd, xd = to_dev(w, scales, x, rows, k, group, cuda)
+    deq = torch.empty(rows * k, device=cuda)
+    lb.gemv_dequant(fmt, wd, sd, deq, group=group)
+    y = torch.empty(rows, dtype=torch.float16, device=cuda)
+    lb.gemv_q4(fmt, wd, sd, xd, y, group=group)
+    ref = deq.view(rows, k).double() @ xd.double()
+    got = y.double()
+    rel = float(torch.linalg.norm(got - ref) / torch.linalg.norm(ref))
     assert rel <= 1e-3, rel

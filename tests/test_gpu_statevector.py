@@ -11,16 +11,7 @@ from tests.conftest import bits
 pytestmark = pytest.mark.gpu
 
 
-def as_tuples(gates):
-    out = []
-    for g in gates:
-        if isinstance(g, cc.U):
-            out.append((0, g.q, 0, cc.f32s(g.m)))
-        elif isinstance(g, cc.CU):
-            out.append((1, g.c, g.t, cc.f32s(g.m)))
-        else:
-            out.append((2, g.a, g.b, [0.0] * 8))
-    return out
+as_tuples = cc.as_tuples
 
 
 def run_engine(q, gates, re0, im0, fuse=6):

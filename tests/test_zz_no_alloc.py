@@ -50,3 +50,29 @@ def test_sizes_past_the_fixed_scratch_are_refused(cuda):
     assert rc == lb.E_UNSUPPORTED
     torch.cuda.synchronize()
     assert out.item() == 7.0  # nothing ran
+
+
+def test_exact_fill_zero_and_a_small_call_after_a_large_one(cuda):
+    # n = the limit fills all 16384 slots; n = 0 is the identity; a small n right after the
+    # limit must not read any slot the large call left behind.
+    stream = torch.cuda.current_stream().cuda_stream
+    big = torch.from_numpy(orc.uniform(93, 1 << 20)).to(cuda).repeat(MAX_N >> 20)  # 1 GiB
+    for n, src in [(MAX_N, big), (0, big), (1000, big), (3, big)]:
+        x = src[:n] if n else src[:1][:0]
+        want = lb.reduce(lb.SUM, x)
+        got = torch.full((1,), float("nan"), device=cuda)
+        rc = _fn(lb.SUM, n, src.data_ptr(), None, got.data_ptr(), stream)
+        assert rc == lb.OK
+        torch.cuda.synchronize()
+        assert got.cpu().numpy().view(np.uint32)[0] == want.cpu().numpy().view(np.uint32)[0], n
+    del big
+    torch.cuda.empty_cache()
+
+
+def test_max_with_y_is_refused_and_runs_nothing(cuda):
+    x = torch.ones(64, device=cuda)
+    out = torch.full((1,), 7.0, device=cuda)
+    for op in (lb.MAX, lb.MIN):
+        assert noalloc(op, x, x, out) == lb.E_UNSUPPORTED
+    torch.cuda.synchronize()
+    assert out.item() == 7.0
