@@ -541,8 +541,10 @@ uint64_t lyth_sv_launches(const lyth_sv *sv);
 /* 4 = a rank-bit qubit swapped into a local bit (pack, transfer and unpack of half the shard). */
 #define LYTH_SV_T_SWAP 4
 /* Fusion (lyth-circuit fuse, lib.rs:72-100; docs/ADR-0030): consecutive local gates touching at
- * most `max_qubits` (1..6) bits run as one pass with the same chains in circuit order, bit-exact
- * with the unfused passes. 1 = one pass per gate. The default is 6. */
+ * most `max_qubits` (1..13) bits run as one pass with the same chains in circuit order, bit-exact
+ * with the unfused passes. A group must also fit one pass at the shard's size: states of 2^14
+ * amplitudes and more take the tile pass (at most 8 of a group's bits above bit 4), smaller ones
+ * the register pass (at most 6 bits). 1 = one pass per gate. The default is 13. */
 int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits);
 /* A gate on a qubit that currently lives on a rank bit: on = 1 (default) first swaps it with the
  * local qubit used furthest ahead in the gate list (half the shard crosses NVLink each way) and
@@ -576,7 +578,7 @@ int lyth_sv_reset_timing(lyth_sv *sv);
  * lyth_sv_set_remap and lyth_sv_stats work on it; set_local / init_* only reset the qubit map;
  * lyth_sv_get_local records the permutation steps that undo the map and copies nothing (re and
  * im may be NULL). Replaying the steps on every rank's shard gives the engine's result. */
-#define LYTH_SV_FUSE_MAX_QUBITS 6
+#define LYTH_SV_FUSE_MAX_QUBITS 13
 #define LYTH_SV_FUSE_MAX_GATES 48
 #define LYTH_SV_OP_U 0           /* U on local bit a */
 #define LYTH_SV_OP_CU 1          /* CU, control local bit a, target local bit b */

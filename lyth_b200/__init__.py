@@ -66,7 +66,7 @@ class SvOp(C.Structure):
     """``lyth_sv_op``: one step a plan handle recorded (include/lyth_b200.h)."""
 
     _fields_ = [("kind", C.c_int32), ("a", C.c_int32), ("b", C.c_int32), ("c", C.c_int32),
-                ("m", _f32 * 8), ("k", C.c_int32), ("bits", _u32 * 6), ("rbits", _u32 * 6), ("ngates", _u32),
+                ("m", _f32 * 8), ("k", C.c_int32), ("bits", _u32 * 13), ("rbits", _u32 * 13), ("ngates", _u32),
                 ("gt", C.c_int8 * 48), ("gc", C.c_int8 * 48), ("gm", (_f32 * 8) * 48)]
 
 

@@ -285,514 +285,539 @@ static FusedGroup arrange_levels(const FusedGroup &g, bool split) {
     return o;
 }
 
-// ------------------------------------------------------------------ the staged pass
-// For states of 2^14 amplitudes and more. The register pass above loads a whole tuple, computes,
-// and stores, so at most its resident warps' loads are in flight: it streams well below HBM
-// speed, and a group on the low address bits makes every warp load touch 32 lines. The staged
-// pass moves the state through shared memory in tiles instead:
+// ------------------------------------------------------------------ the tile pass
+// For states of 2^14 amplitudes and more. The register pass above loads a whole tuple, computes
+// and stores, so at most its resident warps' loads are in flight, and it holds at most 6 qubits.
+// The tile pass moves the state through shared memory in tiles and applies a group of up to 13
+// qubits per pass:
 //
-//  * a tile is 2^13 amplitudes whose indices differ in 13 "tile bits": 5 lane bits, 5 register
-//    levels and 3 warp bits. Lane bits are address bits 0..4, except that when all six group
-//    bits are >= 5 the highest one takes lane bit 4: every warp access is then 64 contiguous
-//    bytes or more per lane half. Register levels are the group's other bits, filled up to five
-//    with the lowest free bits ("batch" levels: independent tuples side by side). Warp bits are
-//    the next free bits.
-//  * one persistent CTA per SM, 16 warps in two groups of 8 that take alternate tiles. A tile is
-//    copied into a 3-stage ring of shared memory, completing on an mbarrier: as 1-D bulk copies
-//    of its contiguous runs (cp.async.bulk) when the runs are >= 2 KiB, else as one to eight
-//    rank-5 tensor-map boxes (cp.async.bulk.tensor.5d, one box dimension per range of
-//    consecutive tile bits; many short runs cost one request each, a box one request for all),
-//    never with multicast. Each warp reads its 32
-//    amplitudes per lane from shared memory and releases the stage, and warp 0 of the group,
-//    once its whole group has read the stage, issues the tile three ahead into it. The gates
-//    then run in registers and the results go to global memory directly (coalesced streaming
-//    stores). Up to three tiles (192 KiB) are in flight per SM whatever the warps are doing,
-//    and no warp is set aside for copies (16 warps x 128 registers fill the register file).
-//  * with a group bit on lane bit 4, the two lane halves read disjoint banks: as runs, those
-//    whose copy of that bit is 1 sit 16 words further along modulo 32 (a 32-word pad after every
-//    two runs, that bit the lowest run-index bit); as boxes, that bit is the box dimension right
-//    after address bits 0..3, 16 words.
-//  * with no gates and each tile bit stored at its image under a permutation of the group's bits,
-//    the same pass permutes the state in place (launch_permute: every tile maps onto itself).
-//  * gates on register levels run the packed chains above; a gate on a lane bit fetches both
-//    values of each pair from the two lanes by indexed shuffles and computes this lane's row.
-//    The arithmetic per amplitude is the same chain in the same order, so the result is
-//    bit-identical.
-constexpr int kStTileBits = 13;
-constexpr int kStTile = 1 << kStTileBits;            // amplitudes per tile
-constexpr int kStRegs = 5;                           // register levels: 32 amplitudes per lane
-constexpr int kStWarpBits = kStTileBits - 5 - kStRegs;
-constexpr int kStGroupWarps = 1 << kStWarpBits;      // consumer warps per tile
-constexpr int kStGroups = 2;                         // consumer groups, alternate tiles
-constexpr int kStStages = 3;
-constexpr int kStConsumers = kStGroups * kStGroupWarps;
-constexpr int kStThreads = kStConsumers * 32;      // no separate producer warp
-constexpr int kStMaxRuns = 64;
-constexpr int kStCompWords = kStTile + 32 * (kStMaxRuns / 2);  // one component of a stage, padded
-constexpr size_t kStBufBytes = (size_t)kStStages * 2 * kStCompWords * sizeof(float);
-constexpr size_t kStSmem = kStBufBytes + (kStGroups + 1) * kStStages * sizeof(uint64_t) +
-                          2 * kStGroups * kStStages * sizeof(uint32_t);
-constexpr uint32_t kStMinBits = 14;                  // local bits from which the staged pass runs
+//  * a tile is 2^13 amplitudes whose indices differ in 13 "tile bits": address bits 0..4 (128
+//    contiguous bytes of each component) and eight more -- the group's bits above bit 4 (at most
+//    eight) filled up with the lowest free bits. A group's whole gate list therefore runs on data
+//    in shared memory: one HBM pass per group, whatever its size.
+//  * one persistent CTA per SM, 16 warps in two groups of 8 that take alternate tiles from a
+//    3-stage ring (64 KiB a stage: re and im). A tile arrives as one to sixteen rank-5 tensor-map
+//    boxes per component (cp.async.bulk.tensor.5d, completion on an mbarrier; dimension 0 = address
+//    bits 0..4, one further dimension per range of consecutive tile bits, iterated boxes beyond
+//    four ranges; no multicast), stored with the 128-byte swizzle: in every 1 KiB of shared memory
+//    the 16-byte chunk index of a word is XOR'ed with its 128-byte row index.
+//  * the group's gates run in segments: a segment's gates target at most five "register levels" --
+//    address bits 0 and 1 (the four words of one 16-byte chunk) and up to three more tile bits.
+//    Per segment a thread reads its 32 amplitudes with eight 128-bit shared loads per component,
+//    applies the segment's gates in registers (the packed chains of the register pass: pairs
+//    along address bit 0, fma.rn.f32x2 on every other level), writes them back in place, and the
+//    group synchronises before the next segment reads with its own layout. The eight tile bits
+//    that are not register levels are the thread's lane and warp bits; lanes 0..2 take bits whose
+//    swizzled chunks differ, so every quarter-warp's 128-bit access covers all 32 banks. A control
+//    on a lane or warp bit is a predicate: all of a thread's amplitudes share its value.
+//  * after the last segment every thread fences its shared-memory writes for the async proxy, the
+//    group synchronises, and warp 0 of the group stores the tile back with the same boxes
+//    (cp.async.bulk.tensor store, bulk group), waits until the store has read the stage, and
+//    issues the tile three ahead into it.
+//  * with no gates and each tile bit written at its image under a permutation of tile bits, the
+//    same kernel permutes the state in place (every tile maps onto itself): the read-out's
+//    permutation passes.
+//  * every wait is bounded (mbar.cuh); a group decides together (bar.red.and) whether its tile
+//    arrived, so no warp is left at a group barrier; before the block leaves, its stores have
+//    completed and every armed load has landed (bounded).
+//
+// The arithmetic per amplitude is the unfused passes' chain in circuit order, so the result is
+// bit-identical to them whatever the segments.
+constexpr int kTpTileBits = 13;
+constexpr int kTpTile = 1 << kTpTileBits;            // amplitudes per tile
+constexpr int kTpRegs = 5;                           // register levels: 32 amplitudes per thread
+constexpr int kTpLaneBits = 5;
+constexpr int kTpWarpBits = kTpTileBits - kTpLaneBits - kTpRegs;  // 3
+constexpr int kTpGroupWarps = 1 << kTpWarpBits;      // 8 warps per tile
+constexpr int kTpGroups = 2;                         // consumer groups, alternate tiles
+constexpr int kTpStages = 3;
+constexpr int kTpThreads = kTpGroups * kTpGroupWarps * 32;
+constexpr int kTpHighBits = kTpTileBits - 5;         // group bits above bit 4 a tile holds
+constexpr int kTpMaxBoxes = 16;
+constexpr uint32_t kTpMinBits = 14;                  // local bits from which the tile pass runs
+constexpr uint32_t kTpCompBytes = kTpTile * (uint32_t)sizeof(float);
+constexpr uint32_t kTpStageBytes = 2 * kTpCompBytes;
+constexpr int kTpBars = kTpStages * kTpGroups;
+constexpr size_t kTpSmem = 1024 + (size_t)kTpStages * kTpStageBytes + kTpBars * sizeof(uint64_t) +
+                           2 * kTpBars * sizeof(uint32_t);
 
-// A gate of the staged pass. case_: target register level t and control register level c
-// (or -1) as t * 8 + c + 1; 64 + c + 1 for a target on lane bit `lt`. lc: a control on a lane
-// bit, or -1.
-struct StagedGate {
+// A segment: shared-memory word images (swizzled word offsets) of the thread's lane bits, warp
+// bits and register levels 2..4 (levels 0 and 1 are address bits 0 and 1: words +1, +2), and its
+// gates [g0, g1).
+struct TpSeg {
+    uint32_t lane_img[kTpLaneBits], warp_img[kTpWarpBits], reg_img[3];
+    uint16_t g0, g1;
+};
+// A gate of the tile pass: case_ = T * 8 + C + 1 (target register level T, control register level
+// C or -1); cl = a control on lane bit cl (0..4) or warp bit cl - 5 (5..7), else -1.
+struct TpGate {
     int16_t case_;
-    int8_t lt, lc;
+    int8_t cl, pad;
     float m[8];
 };
-
-struct StagedPlan {
-    uint32_t tile_bits[kStTileBits];  // the tile's address bits, ascending (for the tile base)
-    uint32_t run_bits;                // a run is address bits 0..run_bits-1: 2^run_bits amplitudes
-    uint32_t nruns;
-    uint32_t lane_w[5], reg_w[kStRegs], warp_w[kStWarpBits];  // shared-memory word weights
-    uint32_t lane_addr[5], reg_addr[kStRegs], warp_addr[kStWarpBits];
-    // Where each lane / register / warp bit's value is stored: the bit itself, or for a
-    // permutation pass its image (a permutation of tile bits keeps every tile in place).
-    uint32_t dlane_addr[5], dreg_addr[kStRegs], dwarp_addr[kStWarpBits];
-    uint32_t run_word[kStMaxRuns];  // shared-memory word of run r
-    // Box copies (tma = 1): dimension k of the tensor maps covers address bits
-    // [dim_lo[k], dim_lo[k] + dim_len[k]) and its box the lowest dim_box[k] of them; nbox boxes
-    // per component, box b at word b * box_words with the address bits box_off[b] set.
-    uint32_t tma;
+struct TpPlan {
+    uint32_t tile_bits[kTpTileBits];  // ascending
     uint32_t dim_lo[5], dim_len[5], dim_box[5];
     uint32_t nbox, box_words;
-    uint64_t box_off[8];
-    uint64_t run_off[kStMaxRuns];   // element offset of run r within a tile
+    uint64_t box_off[kTpMaxBoxes];
     uint64_t ntiles;
-    uint32_t ngates;
-    StagedGate gates[kFuseMaxGates];
+    uint32_t nseg, ngates;
+    uint32_t permute;                                                   // a permutation pass
+    uint32_t wlane_img[kTpLaneBits], wwarp_img[kTpWarpBits], wreg_img[kTpRegs];  // its write images
+    TpSeg segs[kFuseMaxGates];
+    TpGate gates[kFuseMaxGates];
 };
 
 __device__ int g_fused_error;
 
-LYTH_D uint64_t st_tile_base(const StagedPlan &P, uint64_t tile) {
+LYTH_D uint64_t tp_tile_base(const TpPlan &P, uint64_t tile) {
     uint64_t b = tile;
 #pragma unroll
-    for (int k = 0; k < kStTileBits; k++) b = insert_bit(b, P.tile_bits[k], 0);
+    for (int k = 0; k < kTpTileBits; k++) b = insert_bit(b, P.tile_bits[k], 0);
     return b;
 }
-
-// A gate on a lane bit: lane `lo` holds the pair's p0 and lane `hi` its p1 (lo = this lane with
-// the bit clear, hi = with it set); r = this lane's row coefficients in row-0 form. CL as in
-// split_gate. Pairs a register control excludes neither shuffle nor compute.
-template <int KL, int CL>
-LYTH_D void lane_gate(const U8 &r, int lo, int hi, bool on, float2 (&X)[1 << (KL - 1)], float2 (&Y)[1 << (KL - 1)]) {
-#pragma unroll
-    for (int i = 0; i < (1 << (KL - 1)); i++) {
-        if (CL >= 1 && !(i & (1 << (CL - 1)))) continue;
-        if (CL == 0) {
-            const float p0r = __shfl_sync(0xffffffffu, X[i].y, lo), p0i = __shfl_sync(0xffffffffu, Y[i].y, lo);
-            const float p1r = __shfl_sync(0xffffffffu, X[i].y, hi), p1i = __shfl_sync(0xffffffffu, Y[i].y, hi);
-            float a, b;
-            row0(r, p0r, p0i, p1r, p1i, a, b);
-            if (on) { X[i].y = a; Y[i].y = b; }
-        } else {
-            float2 p0r, p0i, p1r, p1i;
-            p0r.x = __shfl_sync(0xffffffffu, X[i].x, lo); p0r.y = __shfl_sync(0xffffffffu, X[i].y, lo);
-            p0i.x = __shfl_sync(0xffffffffu, Y[i].x, lo); p0i.y = __shfl_sync(0xffffffffu, Y[i].y, lo);
-            p1r.x = __shfl_sync(0xffffffffu, X[i].x, hi); p1r.y = __shfl_sync(0xffffffffu, X[i].y, hi);
-            p1i.x = __shfl_sync(0xffffffffu, Y[i].x, hi); p1i.y = __shfl_sync(0xffffffffu, Y[i].y, hi);
-            float2 a, b;
-            row0_2(r, p0r, p0i, p1r, p1i, a, b);
-            if (on) { X[i] = a; Y[i] = b; }
-        }
-    }
+LYTH_D float4 lds128(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a) : "memory");
+    return v;
+}
+LYTH_D void sts128(uint32_t a, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
+}
+LYTH_D void sts32(uint32_t a, float v) { asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory"); }
+LYTH_D void group_sync(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"(kTpGroupWarps * 32) : "memory"); }
+// Every thread of the group passes `p`; all get the AND (a barrier: all of them must arrive).
+LYTH_D bool group_all(int id, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred a, b;\n\t"
+        "setp.ne.u32 a, %1, 0;\n\t"
+        "bar.red.and.pred b, %2, %3, a;\n\t"
+        "selp.u32 %0, 1, 0, b;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)p), "r"(id), "n"(kTpGroupWarps * 32)
+        : "memory");
+    return r != 0;
 }
 
-#define LYTH_ST_REG(T, C) \
-    case (T) * 8 + (C) + 1: gate_case<kStRegs, T, C>(m, X, Y); break;
-#define LYTH_ST_REG_T(T) \
-    LYTH_ST_REG(T, -1) LYTH_ST_C0(T) LYTH_ST_C1(T) LYTH_ST_C2(T) LYTH_ST_C3(T) LYTH_ST_C4(T)
-#define LYTH_ST_C0(T) LYTH_ST_IF(T, 0)
-#define LYTH_ST_C1(T) LYTH_ST_IF(T, 1)
-#define LYTH_ST_C2(T) LYTH_ST_IF(T, 2)
-#define LYTH_ST_C3(T) LYTH_ST_IF(T, 3)
-#define LYTH_ST_C4(T) LYTH_ST_IF(T, 4)
-// (T, C) with C == T never occurs; its label maps to no work
-#define LYTH_ST_IF(T, C) \
-    case (T) * 8 + (C) + 1: if constexpr ((T) != (C)) gate_case<kStRegs, T, ((T) != (C) ? (C) : -1)>(m, X, Y); break;
-#define LYTH_ST_LANE(C) \
-    case 64 + (C) + 1: lane_gate<kStRegs, C>(r, lo, hi, on, X, Y); break;
-
-// Issue tile `t`'s bulk copies into stage `stage` (the whole warp: lane 0 arms the barrier with
-// the tile's byte count, every lane issues its share of the runs).
-LYTH_D void st_issue(const StagedPlan &P, const CUtensorMap *tre, const CUtensorMap *tim, uint64_t t, float *sre,
-                     float *sim, uint32_t bar, const float *re, const float *im, int lane) {
-    if (lane == 0) mbar_expect_tx(bar, 2u * kStTile * (uint32_t)sizeof(float));
+// Box coordinates of box b of the tile whose first amplitude is `base`.
+LYTH_D void tp_coords(const TpPlan &P, uint64_t base, uint32_t b, int (&c)[5]) {
+    const uint64_t a = base + P.box_off[b];
+#pragma unroll
+    for (int k = 0; k < 5; k++) c[k] = (int)((a >> P.dim_lo[k]) & ((1ull << P.dim_len[k]) - 1));
+}
+// Warp-wide: load tile t into the stage at (sre, sre + kTpCompBytes), completing on `bar`.
+LYTH_D void tp_load(const TpPlan &P, const CUtensorMap *tre, const CUtensorMap *tim, uint64_t t, uint32_t sre,
+                    uint32_t bar, int lane) {
+    if (lane == 0) mbar_expect_tx(bar, kTpStageBytes);
     __syncwarp();
-    const uint64_t base = st_tile_base(P, t);
-    if (P.tma) {
-        if ((uint32_t)lane < P.nbox) {
-            const uint64_t a = base + P.box_off[lane];
-            int c[5];
-#pragma unroll
-            for (int k = 0; k < 5; k++) c[k] = (int)((a >> P.dim_lo[k]) & ((1ull << P.dim_len[k]) - 1));
-            const uint32_t w = (uint32_t)lane * P.box_words;
-            tensor_load_5d(smem_u32(sre + w), tre, c[0], c[1], c[2], c[3], c[4], bar);
-            tensor_load_5d(smem_u32(sim + w), tim, c[0], c[1], c[2], c[3], c[4], bar);
-        }
-        return;
-    }
-    const uint32_t run_bytes = (1u << P.run_bits) * (uint32_t)sizeof(float);
-    for (uint32_t r = lane; r < P.nruns; r += 32) {
-        const uint64_t g = base + P.run_off[r];
-        bulk_load(smem_u32(sre + P.run_word[r]), re + g, run_bytes, bar);
-        bulk_load(smem_u32(sim + P.run_word[r]), im + g, run_bytes, bar);
+    if ((uint32_t)lane < P.nbox) {
+        int c[5];
+        tp_coords(P, tp_tile_base(P, t), (uint32_t)lane, c);
+        const uint32_t w = (uint32_t)lane * P.box_words * (uint32_t)sizeof(float);
+        tensor_load_5d(sre + w, tre, c[0], c[1], c[2], c[3], c[4], bar);
+        tensor_load_5d(sre + kTpCompBytes + w, tim, c[0], c[1], c[2], c[3], c[4], bar);
     }
 }
+// Warp-wide: store the stage back to tile t (one bulk group per lane, committed).
+LYTH_D void tp_store(const TpPlan &P, const CUtensorMap *tre, const CUtensorMap *tim, uint64_t t, uint32_t sre,
+                     int lane) {
+    if ((uint32_t)lane < P.nbox) {
+        int c[5];
+        tp_coords(P, tp_tile_base(P, t), (uint32_t)lane, c);
+        const uint32_t w = (uint32_t)lane * P.box_words * (uint32_t)sizeof(float);
+        tensor_store_5d(tre, c[0], c[1], c[2], c[3], c[4], sre + w);
+        tensor_store_5d(tim, c[0], c[1], c[2], c[3], c[4], sre + kTpCompBytes + w);
+    }
+    bulk_commit();
+}
 
-__global__ void __launch_bounds__(kStThreads, 1)
-    staged_fused_kernel(const __grid_constant__ StagedPlan P, const __grid_constant__ CUtensorMap tre,
-                        const __grid_constant__ CUtensorMap tim, float *re, float *im) {
-    constexpr int NP = 1 << (kStRegs - 1);  // float2 pairs per lane
-    extern __shared__ __align__(128) uint8_t st_smem[];
-    float *buf = reinterpret_cast<float *>(st_smem);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(st_smem + kStBufBytes);
-    // Tiles of this CTA: t_j = blockIdx.x + j * gridDim.x. Tile j lives in stage j % 3 and is
-    // consumed by group j % 2; warp 0 of that group issues tile j + 3 into the same stage once
-    // all its warps have read tile j (the stage's `empty` barrier). A tile's arrival is signalled
-    // on the barrier of its (stage, group): a group consumes the uses of its barriers in order,
-    // so it never waits more than one phase ahead of one it has seen complete, however far the
-    // two groups drift apart.
-    auto full = [&](uint64_t j) { return smem_u32(bars + (j % kStStages) * kStGroups + (j % kStGroups)); };
-    auto full_parity = [&](uint64_t j) { return (uint32_t)(j / (kStStages * kStGroups)) & 1u; };
-    auto empty = [&](uint32_t s) { return smem_u32(bars + kStGroups * kStStages + s); };
-    auto sre_of = [&](uint32_t s) { return buf + (size_t)s * 2 * kStCompWords; };
+#define LYTH_TP_REG(T, C) \
+    case (T) * 8 + (C) + 1: gate_case<kTpRegs, T, C>(m, X, Y); break;
+#define LYTH_TP_REG_T(T) \
+    LYTH_TP_REG(T, -1) LYTH_TP_IF(T, 0) LYTH_TP_IF(T, 1) LYTH_TP_IF(T, 2) LYTH_TP_IF(T, 3) LYTH_TP_IF(T, 4)
+// (T, C) with C == T never occurs; its label maps to no work
+#define LYTH_TP_IF(T, C) \
+    case (T) * 8 + (C) + 1: if constexpr ((T) != (C)) gate_case<kTpRegs, T, ((T) != (C) ? (C) : -1)>(m, X, Y); break;
+
+template <bool PERMUTE>
+__global__ void __launch_bounds__(kTpThreads, 1)
+    tile_pass_kernel(const __grid_constant__ TpPlan P, const __grid_constant__ CUtensorMap tre,
+                     const __grid_constant__ CUtensorMap tim) {
+    constexpr int NP = 1 << (kTpRegs - 1);  // float2 pairs per thread
+    extern __shared__ uint8_t tp_raw[];
+    const uint32_t raw = smem_u32(tp_raw);
+    const uint32_t ring = (raw + 1023u) & ~1023u;  // 1 KiB aligned: the 128-byte swizzle's period
+    uint64_t *bars = reinterpret_cast<uint64_t *>(tp_raw + (ring - raw) + (size_t)kTpStages * kTpStageBytes);
+    uint32_t *n_armed = reinterpret_cast<uint32_t *>(bars + kTpBars);
+    uint32_t *n_used = n_armed + kTpBars;
+    // Tiles of this CTA: t_j = blockIdx.x + j * gridDim.x, in stage j % 3, taken by group j % 2.
+    // A tile's arrival is signalled on the barrier of its (stage, group): a group consumes the
+    // uses of its barriers in order, so it never waits more than one phase ahead.
+    auto bar_of = [&](uint64_t j) { return (uint32_t)((j % kTpStages) * kTpGroups + (j % kTpGroups)); };
+    auto full = [&](uint64_t j) { return smem_u32(bars + bar_of(j)); };
+    auto full_parity = [&](uint64_t j) { return (uint32_t)(j / kTpBars) & 1u; };
+    auto stage = [&](uint64_t j) { return ring + (uint32_t)(j % kTpStages) * kTpStageBytes; };
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int grp = warp / kStGroupWarps, wid = warp % kStGroupWarps;
+    const int grp = warp / kTpGroupWarps, wid = warp % kTpGroupWarps;
+    const int bar_id = 1 + grp;
     const uint64_t ntiles = P.ntiles > blockIdx.x ? (P.ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-    // Uses of each full barrier armed and consumed, for the wind-down: every use up to the last
-    // has completed except possibly the last armed one, so its parity is unambiguous.
-    constexpr int NB = kStStages * kStGroups;
-    uint32_t *n_armed = reinterpret_cast<uint32_t *>(bars + (kStGroups + 1) * kStStages);
-    uint32_t *n_used = n_armed + NB;
-    auto bar_of = [&](uint64_t j) { return (uint32_t)((j % kStStages) * kStGroups + (j % kStGroups)); };
     if (warp == 0) {
         if (lane == 0) {
-            for (int b = 0; b < NB; b++) {
+            for (int b = 0; b < kTpBars; b++) {
                 mbar_init(smem_u32(bars + b), 1);
                 n_armed[b] = 0;
                 n_used[b] = 0;
             }
-            for (int s = 0; s < kStStages; s++) mbar_init(empty(s), kStGroupWarps);
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
         __syncwarp();
-        for (uint32_t j = 0; j < (uint32_t)kStStages && j < ntiles; j++) {
-            st_issue(P, &tre, &tim, blockIdx.x + (uint64_t)j * gridDim.x, sre_of(j), sre_of(j) + kStCompWords, full(j),
-                     re, im, lane);
+        for (uint32_t j = 0; j < (uint32_t)kTpStages && j < ntiles; j++) {
+            tp_load(P, &tre, &tim, blockIdx.x + (uint64_t)j * gridDim.x, stage(j), full(j), lane);
             if (lane == 0) n_armed[bar_of(j)]++;
         }
     }
     __syncthreads();
 
-    uint32_t lane_s = 0, warp_s = 0;
-    uint64_t lane_g = 0, warp_g = 0;
-#pragma unroll
-    for (int b = 0; b < 5; b++)
-        if ((lane >> b) & 1) { lane_s += P.lane_w[b]; lane_g += 1ull << P.dlane_addr[b]; }
-#pragma unroll
-    for (int b = 0; b < kStWarpBits; b++)
-        if ((wid >> b) & 1) { warp_s += P.warp_w[b]; warp_g += 1ull << P.dwarp_addr[b]; }
-    for (uint64_t j = grp; j < ntiles; j += kStGroups) {
+    for (uint64_t j = grp; j < ntiles; j += kTpGroups) {
         const uint64_t t = blockIdx.x + j * gridDim.x;
-        const uint32_t stage = (uint32_t)(j % kStStages), phase = (uint32_t)(j / kStStages) & 1u;
         const bool ok = mbar_wait(full(j), full_parity(j), &g_fused_error);
-        if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform: the gates below shuffle
+        if (!group_all(bar_id, ok)) break;  // the whole group leaves together
         if (wid == 0 && lane == 0) n_used[bar_of(j)]++;
-        const float *sre = sre_of(stage);
-        const float *sim = sre + kStCompWords;
-        uint32_t ss[kStRegs];
+        const uint32_t sre = stage(j), sim = sre + kTpCompBytes;
+        for (uint32_t s = 0; s < P.nseg; s++) {
+            const TpSeg &sg = P.segs[s];
+            uint32_t base = 0;
 #pragma unroll
-        for (int l = 0; l < kStRegs; l++) {
-            ss[l] = P.reg_w[l];
-            asm volatile("" : "+r"(ss[l]));
-        }
-        float2 X[NP], Y[NP];
+            for (int b = 0; b < kTpLaneBits; b++)
+                if ((lane >> b) & 1) base ^= sg.lane_img[b];
 #pragma unroll
-        for (int i = 0; i < NP; i++) {
-            uint32_t o = lane_s + warp_s;
+            for (int b = 0; b < kTpWarpBits; b++)
+                if ((wid >> b) & 1) base ^= sg.warp_img[b];
+            uint32_t ri[3];
 #pragma unroll
-            for (int l = 1; l < kStRegs; l++)
-                if (i & (1 << (l - 1))) o += ss[l];
-            X[i] = make_float2(sre[o], sre[o + ss[0]]);
-            Y[i] = make_float2(sim[o], sim[o + ss[0]]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty(stage));  // release: the reads above are ordered before
-        if (wid == 0 && j + kStStages < ntiles) {
-            // refill: wait until the whole group has read this stage, then issue tile j + 3
-            const bool free_ok = mbar_wait(empty(stage), phase, &g_fused_error);
-            if (!__all_sync(0xffffffffu, free_ok)) break;
-            st_issue(P, &tre, &tim, t + (uint64_t)kStStages * gridDim.x, sre_of(stage), sre_of(stage) + kStCompWords,
-                     full(j + kStStages), re, im, lane);
-            if (lane == 0) n_armed[bar_of(j + kStStages)]++;
-        }
-
-        for (uint32_t g = 0; g < P.ngates; g++) {
-            const StagedGate &sg = P.gates[g];
-            const U8 m{sg.m[0], sg.m[1], sg.m[2], sg.m[3], sg.m[4], sg.m[5], sg.m[6], sg.m[7]};
-            const bool on = sg.lc < 0 || ((lane >> sg.lc) & 1);
-            if (sg.case_ < 64) {
-                if (!on) continue;
-                switch (sg.case_) {
-                    LYTH_ST_REG_T(0) LYTH_ST_REG_T(1) LYTH_ST_REG_T(2) LYTH_ST_REG_T(3) LYTH_ST_REG_T(4)
-                    default: break;
-                }
+            for (int l = 0; l < 3; l++) {
+                ri[l] = sg.reg_img[l];
+                asm volatile("" : "+r"(ri[l]));
+            }
+            // word of chunk q (register levels 2..4 = the bits of q), as a byte offset
+            auto addr = [&](int q) {
+                uint32_t a = base;
+#pragma unroll
+                for (int l = 0; l < 3; l++)
+                    if ((q >> l) & 1) a ^= ri[l];
+                return a * (uint32_t)sizeof(float);
+            };
+            float2 X[NP], Y[NP];
+#pragma unroll
+            for (int q = 0; q < NP / 2; q++) {
+                const uint32_t a = addr(q);
+                const float4 vr = lds128(sre + a), vi = lds128(sim + a);
+                X[2 * q] = make_float2(vr.x, vr.y);
+                X[2 * q + 1] = make_float2(vr.z, vr.w);
+                Y[2 * q] = make_float2(vi.x, vi.y);
+                Y[2 * q + 1] = make_float2(vi.z, vi.w);
+            }
+            if constexpr (PERMUTE) {
+                // every thread has read before any writes: the images are other threads' words
+                group_sync(bar_id);
+                uint32_t wbase = 0;
+#pragma unroll
+                for (int b = 0; b < kTpLaneBits; b++)
+                    if ((lane >> b) & 1) wbase ^= P.wlane_img[b];
+#pragma unroll
+                for (int b = 0; b < kTpWarpBits; b++)
+                    if ((wid >> b) & 1) wbase ^= P.wwarp_img[b];
+#pragma unroll
+                for (int q = 0; q < NP / 2; q++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        uint32_t a = wbase;
+                        if (e & 1) a ^= P.wreg_img[0];
+                        if (e & 2) a ^= P.wreg_img[1];
+#pragma unroll
+                        for (int l = 0; l < 3; l++)
+                            if ((q >> l) & 1) a ^= P.wreg_img[2 + l];
+                        const float2 x = X[2 * q + (e >> 1)], y = Y[2 * q + (e >> 1)];
+                        sts32(sre + a * (uint32_t)sizeof(float), (e & 1) ? x.y : x.x);
+                        sts32(sim + a * (uint32_t)sizeof(float), (e & 1) ? y.y : y.x);
+                    }
             } else {
-                const int h = (lane >> sg.lt) & 1;
-                const int lo = lane & ~(1 << sg.lt), hi = lane | (1 << sg.lt);
-                const U8 r{h ? m.cr : m.ar, h ? m.ci : m.ai, h ? m.dr : m.br, h ? m.di : m.bi, 0.f, 0.f, 0.f, 0.f};
-                switch (sg.case_) {
-                    LYTH_ST_LANE(-1) LYTH_ST_LANE(0) LYTH_ST_LANE(1) LYTH_ST_LANE(2) LYTH_ST_LANE(3) LYTH_ST_LANE(4)
-                    default: break;
+                for (uint32_t g = sg.g0; g < sg.g1; g++) {
+                    const TpGate &tg = P.gates[g];
+                    const bool on = tg.cl < 0 || (tg.cl < kTpLaneBits ? ((lane >> tg.cl) & 1)
+                                                                      : ((wid >> (tg.cl - kTpLaneBits)) & 1));
+                    if (!on) continue;
+                    const U8 m{tg.m[0], tg.m[1], tg.m[2], tg.m[3], tg.m[4], tg.m[5], tg.m[6], tg.m[7]};
+                    switch (tg.case_) {
+                        LYTH_TP_REG_T(0) LYTH_TP_REG_T(1) LYTH_TP_REG_T(2) LYTH_TP_REG_T(3) LYTH_TP_REG_T(4)
+                        default: break;
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < NP / 2; q++) {
+                    const uint32_t a = addr(q);
+                    sts128(sre + a, make_float4(X[2 * q].x, X[2 * q].y, X[2 * q + 1].x, X[2 * q + 1].y));
+                    sts128(sim + a, make_float4(Y[2 * q].x, Y[2 * q].y, Y[2 * q + 1].x, Y[2 * q + 1].y));
                 }
             }
+            if (s + 1 < P.nseg) group_sync(bar_id);
         }
-
-        uint64_t gs[kStRegs];
-#pragma unroll
-        for (int l = 0; l < kStRegs; l++) {
-            gs[l] = 1ull << P.dreg_addr[l];
-            asm volatile("" : "+l"(gs[l]));
-        }
-        const uint64_t base = st_tile_base(P, t) + lane_g + warp_g;
-#pragma unroll
-        for (int i = 0; i < NP; i++) {
-            uint64_t a = base;
-#pragma unroll
-            for (int l = 1; l < kStRegs; l++)
-                if (i & (1 << (l - 1))) a += gs[l];
-            __stcs(re + a, X[i].x);
-            __stcs(re + a + gs[0], X[i].y);
-            __stcs(im + a, Y[i].x);
-            __stcs(im + a + gs[0], Y[i].y);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the store
+        group_sync(bar_id);
+        if (wid == 0) {
+            tp_store(P, &tre, &tim, t, sre, lane);
+            bulk_wait_read0();  // the store has read the stage: it may be refilled
+            __syncwarp();
+            if (j + kTpStages < ntiles) {
+                tp_load(P, &tre, &tim, t + (uint64_t)kTpStages * gridDim.x, sre, full(j + kTpStages), lane);
+                if (lane == 0) n_armed[bar_of(j + kTpStages)]++;
+            }
         }
     }
+    if (wid == 0) bulk_wait0();  // this warp's stores have completed
     // Every armed tile has landed before the block may leave. Normally each was consumed; after
     // a timed-out wait, one use per barrier may be outstanding (bounded wait for it).
     __syncthreads();
     if (threadIdx.x == 0)
-        for (int b = 0; b < NB; b++)
+        for (int b = 0; b < kTpBars; b++)
             if (n_armed[b] != n_used[b]) mbar_wait(smem_u32(bars + b), (n_armed[b] - 1u) & 1u, &g_fused_error);
 }
-#undef LYTH_ST_REG
-#undef LYTH_ST_REG_T
-#undef LYTH_ST_C0
-#undef LYTH_ST_C1
-#undef LYTH_ST_C2
-#undef LYTH_ST_C3
-#undef LYTH_ST_C4
-#undef LYTH_ST_IF
-#undef LYTH_ST_LANE
+#undef LYTH_TP_REG
+#undef LYTH_TP_REG_T
+#undef LYTH_TP_IF
 
-// The staged layout of a group over L local bits (false: the register pass runs instead).
-// Box layout of the tile bits (tensor-map copies): dimension 0 = address bits 0..3 (with a lane
-// group bit) or the contiguous tile bits from 0, then the lane group bit (so the two lane halves
-// sit 16 words apart), then each further range of consecutive tile bits; beyond five dimensions
-// the smallest ranges are iterated as separate boxes (at most 8). Fills weight[] (word weight of
-// each tile bit) and the plan's dim / box fields; false when the tile does not fit the form.
-static bool layout_boxes(const bool *tile, int star, uint32_t L, uint32_t *weight, StagedPlan &P) {
-    struct Dim { uint32_t lo, box; };
-    Dim d[kStTileBits];
-    int nd = 0;
-    bool placed[64] = {false};
-    uint32_t b0 = 0;
-    if (star >= 0) b0 = 4;
-    else while (b0 < 8 && tile[b0]) b0++;
-    for (uint32_t b = 0; b < b0; b++) if (!tile[b]) return false;
-    d[nd++] = {0, b0};
-    for (uint32_t b = 0; b < b0; b++) placed[b] = true;
-    if (star >= 0) { d[nd++] = {(uint32_t)star, 1}; placed[star] = true; }
-    for (uint32_t b = 0; b < 64; b++) {
-        if (!tile[b] || placed[b]) continue;
+// ---- host planning
+// The swizzled word of a logical word bit w: the 128-byte swizzle XORs word bits 2..4 (the 16-byte
+// chunk) with bits 5..7 (the row within 1 KiB). XOR-ing images of disjoint bits gives the word.
+static uint32_t tp_img(uint32_t w) { return (1u << w) ^ ((w >= 5 && w < 8) ? (1u << (w - 3)) : 0u); }
+
+// The tile of a group (its bits `gbits`) over L local bits: tile bits, tensor-map dimensions and
+// boxes, and each tile bit's logical word position wpos[] (bits 0..4 = address bits 0..4, then the
+// boxes' dimensions, then the iterated bits). False when the group does not fit a tile.
+static bool tp_layout(const uint32_t *gbits, int k, uint32_t L, TpPlan &P, int *wpos) {
+    if (L < kTpMinBits || L > 48) return false;
+    bool tile[64] = {false};
+    int cnt = 5, nhigh = 0;
+    for (int b = 0; b < 5; b++) tile[b] = true;
+    for (int l = 0; l < k; l++) {
+        const uint32_t b = gbits[l];
+        if (b >= L) return false;
+        if (!tile[b]) { tile[b] = true; cnt++; nhigh++; }
+    }
+    if (nhigh > kTpHighBits) return false;
+    for (uint32_t b = 5; b < L && cnt < kTpTileBits; b++)
+        if (!tile[b]) { tile[b] = true; cnt++; }
+    if (cnt != kTpTileBits) return false;
+    struct Range { uint32_t lo, len; };
+    Range rg[kTpHighBits];
+    int nr = 0;
+    for (uint32_t b = 5; b < L;) {
+        if (!tile[b]) { b++; continue; }
         uint32_t e = b;
-        while (e < 64 && tile[e] && !placed[e] && e - b < 8) e++;
-        d[nd++] = {b, e - b};
-        for (uint32_t x = b; x < e; x++) placed[x] = true;
+        while (e < L && tile[e]) e++;
+        rg[nr++] = {b, e - b};
+        b = e;
     }
-    uint32_t iter[3];
-    int ni = 0;
-    while (nd > 5) {  // iterate the smallest range (ties: the highest), never dimension 0 or the star
+    bool iter[kTpHighBits] = {false};
+    for (int kept = nr; kept > 4; kept--) {  // iterate the smallest range (ties: the highest)
         int pick = -1;
-        for (int k = (star >= 0 ? 2 : 1); k < nd; k++)
-            if (pick < 0 || d[k].box < d[pick].box || (d[k].box == d[pick].box && d[k].lo > d[pick].lo)) pick = k;
-        if (ni + (int)d[pick].box > 3) return false;
-        for (uint32_t i = 0; i < d[pick].box; i++) iter[ni++] = d[pick].lo + i;
-        for (int k = pick; k + 1 < nd; k++) d[k] = d[k + 1];
-        nd--;
+        for (int i = 0; i < nr; i++)
+            if (!iter[i] && (pick < 0 || rg[i].len < rg[pick].len || (rg[i].len == rg[pick].len && rg[i].lo > rg[pick].lo)))
+                pick = i;
+        iter[pick] = true;
     }
-    // coverage: from each dimension's first bit to the next dimension's first bit in address order
-    for (int k = 0; k < nd; k++) {
-        uint32_t hi = L;
+    memset(P.dim_lo, 0, sizeof P.dim_lo);
+    memset(P.dim_len, 0, sizeof P.dim_len);
+    memset(P.dim_box, 0, sizeof P.dim_box);
+    int nd = 1;
+    P.dim_box[0] = 5;
+    for (int i = 0; i < nr; i++)
+        if (!iter[i]) { P.dim_lo[nd] = rg[i].lo; P.dim_box[nd] = rg[i].len; nd++; }
+    for (int d = 0; d < nd; d++) {
+        uint32_t next = L;
         for (int q = 0; q < nd; q++)
-            if (d[q].lo > d[k].lo && d[q].lo < hi) hi = d[q].lo;
-        if (hi - d[k].lo < d[k].box || hi - d[k].lo > 31) return false;
-        P.dim_lo[k] = d[k].lo;
-        P.dim_len[k] = hi - d[k].lo;
-        P.dim_box[k] = d[k].box;
+            if (P.dim_lo[q] > P.dim_lo[d] && P.dim_lo[q] < next) next = P.dim_lo[q];
+        P.dim_len[d] = next - P.dim_lo[d];
+        if (P.dim_len[d] > 31 || P.dim_len[d] < P.dim_box[d]) return false;
     }
-    if (d[0].box < 2) return false;  // the inner box must span >= 16 bytes
-    for (int k = nd; k < 5; k++) { P.dim_lo[k] = 0; P.dim_len[k] = 0; P.dim_box[k] = 0; }
-    uint32_t w = 1;
-    for (int k = 0; k < nd; k++)
-        for (uint32_t i = 0; i < d[k].box; i++) { weight[d[k].lo + i] = w; w <<= 1; }
-    P.box_words = w;
-    P.nbox = 1u << ni;
-    for (int i = 0; i < ni; i++) weight[iter[i]] = w << i;
+    int w = 0;
+    for (uint32_t b = 0; b < 5; b++) wpos[b] = w++;
+    for (int d = 1; d < nd; d++)
+        for (uint32_t i = 0; i < P.dim_box[d]; i++) wpos[P.dim_lo[d] + i] = w++;
+    P.box_words = 1u << w;
+    uint32_t it[kTpHighBits];
+    int nit = 0;
+    for (int i = 0; i < nr; i++)
+        if (iter[i])
+            for (uint32_t x = 0; x < rg[i].len; x++) { it[nit] = rg[i].lo + x; wpos[it[nit]] = w++; nit++; }
+    if (w != kTpTileBits || P.box_words < 256 || (1 << nit) > kTpMaxBoxes) return false;
+    P.nbox = 1u << nit;
     for (uint32_t bx = 0; bx < P.nbox; bx++) {
         uint64_t off = 0;
-        for (int i = 0; i < ni; i++)
-            if ((bx >> i) & 1) off += 1ull << iter[i];
+        for (int i = 0; i < nit; i++)
+            if ((bx >> i) & 1) off += 1ull << it[i];
         P.box_off[bx] = off;
     }
-    P.tma = 1;
-    return true;
-}
-
-// boxes: 0 = runs only, 1 = boxes where runs would be short (< 2 KiB), 2 = boxes where they fit.
-static bool plan_staged(const FusedGroup &g, uint32_t L, int boxes, StagedPlan &P) {
-    if (L < kStMinBits || g.k < 1 || g.k > kFuseMaxQubits) return false;
-    const int k = g.k;
-    int use[kFuseMaxQubits] = {0};
-    for (uint32_t i = 0; i < g.ngates; i++) {
-        use[g.gates[i].t]++;
-        if (g.gates[i].c >= 0) use[g.gates[i].c]++;
-    }
-    bool group[64] = {false};
-    for (int l = 0; l < k; l++) group[g.bits[l]] = true;
-    int code[kFuseMaxQubits];  // group level -> kernel level (0..4 register, 5 + b lane bit b)
-    for (int l = 0; l < k; l++) code[l] = g.bits[l] < 5 ? 5 + (int)g.bits[l] : -1;
-    // a sixth group bit >= 5 goes to lane bit 4: the highest one (it splits the fewest runs)
-    int nhi = 0, top_l = -1;
-    for (int l = 0; l < k; l++)
-        if (g.bits[l] >= 5) {
-            nhi++;
-            if (top_l < 0 || g.bits[l] > g.bits[top_l]) top_l = l;
-        }
-    const int nstar = nhi > kStRegs ? 1 : 0;
-    uint32_t lane_addr[5] = {0, 1, 2, 3, 4};
-    bool star[64] = {false};
-    if (nstar) {
-        lane_addr[4] = g.bits[top_l];
-        code[top_l] = 5 + 4;
-        star[g.bits[top_l]] = true;
-    }
-    bool used[64] = {false};
-    for (int b = 0; b < 5; b++) used[lane_addr[b]] = true;
-    auto next_free = [&]() -> uint32_t {
-        for (uint32_t b = 0; b < 64; b++)
-            if (!used[b] && !group[b]) { used[b] = true; return b; }
-        return 64;
-    };
-    // register levels: level 0 a batch bit when there is one (no gate touches it, so every gate
-    // runs on packed pairs), else the group bit used least
-    int regs_l[kStRegs], nreg = 0;
-    for (int l = 0; l < k; l++)
-        if (code[l] < 0) regs_l[nreg++] = l;
-    uint32_t reg_addr[kStRegs];
-    int r = 0;
-    if (nreg < kStRegs) {
-        reg_addr[r++] = next_free();
-    } else {
-        int best = 0;
-        for (int i = 1; i < nreg; i++)
-            if (use[regs_l[i]] < use[regs_l[best]]) best = i;
-        const int t = regs_l[0]; regs_l[0] = regs_l[best]; regs_l[best] = t;
-    }
-    for (int i = 0; i < nreg; i++) {
-        code[regs_l[i]] = r;
-        reg_addr[r++] = g.bits[regs_l[i]];
-        used[g.bits[regs_l[i]]] = true;
-    }
-    while (r < kStRegs) reg_addr[r++] = next_free();
-    uint32_t warp_addr[kStWarpBits];
-    for (int b = 0; b < kStWarpBits; b++) warp_addr[b] = next_free();
-
-    uint32_t all[kStTileBits];
     int n = 0;
-    for (int b = 0; b < 5; b++) all[n++] = lane_addr[b];
-    for (int b = 0; b < kStRegs; b++) all[n++] = reg_addr[b];
-    for (int b = 0; b < kStWarpBits; b++) all[n++] = warp_addr[b];
-    for (int i = 0; i < n; i++)
-        if (all[i] >= L) return false;
-    for (int i = 1; i < n; i++)
-        for (int j = i; j > 0 && all[j - 1] > all[j]; j--) { const uint32_t t = all[j]; all[j] = all[j - 1]; all[j - 1] = t; }
-    for (int i = 1; i < n; i++)
-        if (all[i] == all[i - 1]) return false;
-    bool tile[64] = {false};
-    for (int i = 0; i < n; i++) tile[all[i]] = true;
-    memset(&P, 0, sizeof P);
-    for (int i = 0; i < n; i++) P.tile_bits[i] = all[i];
-    uint32_t weight[64] = {0};  // shared-memory word weight of each tile bit
-    // Runs of >= 2 KiB copy fastest as plain bulk copies; shorter ones (a tile of many small
-    // runs) as tensor-map boxes, one or a few per component.
-    uint32_t m_runs = 0;
-    while (m_runs < 64 && tile[m_runs] && !star[m_runs]) m_runs++;
-    if (boxes == 1 && m_runs >= 9) boxes = 0;
-    if (!(boxes && layout_boxes(tile, nstar ? (int)lane_addr[4] : -1, L, weight, P))) {
-        // runs: address bits 0..m-1, all tile bits and none the lane group bit
-        P.tma = 0;
-        uint32_t m = 0;
-        while (m < 64 && tile[m] && !star[m]) m++;
-        // run-index bits: the lane group bit first, then the other tile bits above the run
-        uint32_t ridx[kStTileBits];
-        int nr = 0;
-        if (nstar) ridx[nr++] = lane_addr[4];
-        for (int i = 0; i < n; i++)
-            if (all[i] >= m && !star[all[i]]) ridx[nr++] = all[i];
-        if (m < 7 || (1 << nr) > kStMaxRuns || (uint32_t)nr + m != (uint32_t)kStTileBits) return false;
-        const uint32_t RL = 1u << m;
-        const uint32_t gstride = nstar ? 2 * RL + 32u : RL, jstride = RL + 16u;
-        for (uint32_t b = 0; b < m; b++) weight[b] = 1u << b;
-        for (int q = 0; q < nr; q++)
-            weight[ridx[q]] = q < nstar ? jstride : (1u << (q - nstar)) * gstride;
-        P.run_bits = m;
-        P.nruns = 1u << nr;
-        uint32_t top = 0;
-        for (uint32_t run = 0; run < P.nruns; run++) {
-            uint64_t off = 0;
-            uint32_t w = 0;
-            for (int q = 0; q < nr; q++)
-                if ((run >> q) & 1) { off += 1ull << ridx[q]; w += weight[ridx[q]]; }
-            P.run_off[run] = off;
-            P.run_word[run] = w;
-            if (w + RL > top) top = w + RL;
-        }
-        if (top > (uint32_t)kStCompWords) return false;
-    }
-    for (int b = 0; b < 5; b++) { P.lane_addr[b] = lane_addr[b]; P.lane_w[b] = weight[lane_addr[b]]; }
-    for (int b = 0; b < 5; b++) P.dlane_addr[b] = lane_addr[b];
-    for (int b = 0; b < kStRegs; b++) P.dreg_addr[b] = reg_addr[b];
-    for (int b = 0; b < kStWarpBits; b++) P.dwarp_addr[b] = warp_addr[b];
-    for (int b = 0; b < kStRegs; b++) { P.reg_addr[b] = reg_addr[b]; P.reg_w[b] = weight[reg_addr[b]]; }
-    for (int b = 0; b < kStWarpBits; b++) { P.warp_addr[b] = warp_addr[b]; P.warp_w[b] = weight[warp_addr[b]]; }
-    P.ntiles = 1ull << (L - kStTileBits);
-    P.ngates = g.ngates;
-    for (uint32_t i = 0; i < g.ngates; i++) {
-        const FusedGate &fg = g.gates[i];
-        StagedGate &sg = P.gates[i];
-        const int t = code[fg.t], c = fg.c >= 0 ? code[fg.c] : -1;
-        const int creg = c >= 0 && c < kStRegs ? c : -1;
-        sg.lc = (int8_t)(c >= kStRegs ? c - 5 : -1);
-        if (t < kStRegs) {
-            sg.case_ = (int16_t)(t * 8 + creg + 1);
-            sg.lt = -1;
-        } else {
-            sg.case_ = (int16_t)(64 + creg + 1);
-            sg.lt = (int8_t)(t - 5);
-        }
-        memcpy(sg.m, fg.m, sizeof sg.m);
-    }
+    for (uint32_t b = 0; b < L && n < kTpTileBits; b++)
+        if (tile[b]) P.tile_bits[n++] = b;
+    P.ntiles = 1ull << (L - kTpTileBits);
     return true;
 }
 
-// The two tensor maps of a box plan (re and im over 2^L f32 amplitudes). Unused dimensions have
-// extent 1.
-static bool encode_boxes(const StagedPlan &P, uint32_t L, float *re, float *im, CUtensorMap &tre, CUtensorMap &tim) {
+// Whether register levels (address bits, by their word positions) leave every quarter-warp's
+// 128-bit access conflict-free: for each chunk bit i, word bit 2+i or 5+i must be left to a lane.
+static bool tp_regs_ok(const uint32_t *regs, int n, const int *wpos) {
+    bool has[kTpTileBits] = {false};
+    for (int i = 0; i < n; i++) has[wpos[regs[i]]] = true;
+    for (int i = 0; i < 3; i++)
+        if (has[2 + i] && has[5 + i]) return false;
+    return true;
+}
+
+// Thread mapping of a segment whose extra register levels are R (tile address bits, not 0 or 1):
+// levels = [0, 1, R..., pads], lanes 0..2 = one of word bits 2+i / 5+i each, then the rest.
+struct TpMap {
+    uint32_t reg[kTpRegs], lane[kTpLaneBits], warp[kTpWarpBits];
+};
+static bool tp_map(const TpPlan &P, const int *wpos, const uint32_t *R, int nR, TpMap &M) {
+    uint32_t regs[kTpRegs] = {0, 1};
+    int n = 2;
+    for (int i = 0; i < nR; i++) regs[n++] = R[i];
+    auto in = [&](uint32_t b, const uint32_t *v, int m) {
+        for (int i = 0; i < m; i++)
+            if (v[i] == b) return true;
+        return false;
+    };
+    // pads: tile bits at word positions 8..12 (they bear on no chunk bit), lowest first
+    for (int wp = 8; wp < kTpTileBits && n < kTpRegs; wp++)
+        for (int t = 0; t < kTpTileBits; t++) {
+            const uint32_t b = P.tile_bits[t];
+            if (wpos[b] == wp && !in(b, regs, n)) { regs[n++] = b; break; }
+        }
+    if (n != kTpRegs || !tp_regs_ok(regs + 2, kTpRegs - 2, wpos)) return false;
+    uint32_t by_w[kTpTileBits];
+    for (int t = 0; t < kTpTileBits; t++) by_w[wpos[P.tile_bits[t]]] = P.tile_bits[t];
+    uint32_t used[kTpTileBits];
+    int nu = 0;
+    for (int i = 0; i < kTpRegs; i++) used[nu++] = regs[i];
+    for (int i = 0; i < 3; i++) {
+        uint32_t b = by_w[2 + i];
+        if (in(b, regs, kTpRegs)) b = by_w[5 + i];
+        if (in(b, used, nu)) return false;
+        M.lane[i] = b;
+        used[nu++] = b;
+    }
+    int li = 3, wi = 0;
+    for (int wp = 0; wp < kTpTileBits; wp++) {
+        const uint32_t b = by_w[wp];
+        if (in(b, used, nu)) continue;
+        if (li < kTpLaneBits) M.lane[li++] = b;
+        else M.warp[wi++] = b;
+        used[nu++] = b;
+    }
+    if (li != kTpLaneBits || wi != kTpWarpBits) return false;
+    for (int i = 0; i < kTpRegs; i++) M.reg[i] = regs[i];
+    return true;
+}
+
+static void tp_fill_seg(const TpMap &M, const int *wpos, TpSeg &S) {
+    for (int b = 0; b < kTpLaneBits; b++) S.lane_img[b] = tp_img((uint32_t)wpos[M.lane[b]]);
+    for (int b = 0; b < kTpWarpBits; b++) S.warp_img[b] = tp_img((uint32_t)wpos[M.warp[b]]);
+    for (int l = 0; l < 3; l++) S.reg_img[l] = tp_img((uint32_t)wpos[M.reg[2 + l]]);
+}
+
+// The tile-pass plan of a fused group over L local bits: layout, then segments (greedy in gate
+// order: a gate whose target is not yet a register level adds it while there is room and the
+// levels stay conflict-free; else the segment closes).
+static bool plan_tile(const FusedGroup &g, uint32_t L, TpPlan &P) {
+    if (g.k < 1 || g.k > kFuseMaxQubits || g.ngates > (uint32_t)kFuseMaxGates) return false;
+    memset(&P, 0, sizeof P);
+    int wpos[64];
+    for (int i = 0; i < 64; i++) wpos[i] = -1;
+    if (!tp_layout(g.bits, g.k, L, P, wpos)) return false;
+    uint32_t R[3];
+    int nR = 0;
+    uint32_t g0 = 0;
+    auto close = [&](uint32_t g1) -> bool {
+        TpMap M;
+        if (!tp_map(P, wpos, R, nR, M)) return false;
+        TpSeg &S = P.segs[P.nseg++];
+        tp_fill_seg(M, wpos, S);
+        S.g0 = (uint16_t)g0;
+        S.g1 = (uint16_t)g1;
+        for (uint32_t i = g0; i < g1; i++) {
+            const FusedGate &fg = g.gates[i];
+            TpGate &tg = P.gates[i];
+            const uint32_t tb = g.bits[fg.t];
+            int T = -1, C = -1;
+            tg.cl = -1;
+            for (int l = 0; l < kTpRegs; l++) if (M.reg[l] == tb) T = l;
+            if (T < 0) return false;
+            if (fg.c >= 0) {
+                const uint32_t cb = g.bits[fg.c];
+                for (int l = 0; l < kTpRegs; l++) if (M.reg[l] == cb) C = l;
+                if (C < 0) {
+                    for (int b = 0; b < kTpLaneBits; b++) if (M.lane[b] == cb) tg.cl = (int8_t)b;
+                    for (int b = 0; b < kTpWarpBits; b++) if (M.warp[b] == cb) tg.cl = (int8_t)(kTpLaneBits + b);
+                    if (tg.cl < 0) return false;
+                }
+            }
+            tg.case_ = (int16_t)(T * 8 + C + 1);
+            tg.pad = 0;
+            memcpy(tg.m, fg.m, sizeof tg.m);
+        }
+        return true;
+    };
+    for (uint32_t i = 0; i < g.ngates; i++) {
+        const uint32_t t = g.bits[g.gates[i].t];
+        bool have = t < 2;
+        for (int r = 0; r < nR; r++) have = have || R[r] == t;
+        if (have) continue;
+        if (nR < 3) {
+            R[nR] = t;
+            if (tp_regs_ok(R, nR + 1, wpos)) { nR++; continue; }
+        }
+        if (!close(i)) return false;
+        g0 = i;
+        R[0] = t;
+        nR = 1;
+    }
+    if (!close(g.ngates)) return false;
+    P.ngates = g.ngates;
+    return true;
+}
+
+// A permutation pass over the tile holding `src`: one segment with no gates, each tile bit written
+// at its image (src[j] -> dst[j], the other tile bits in place).
+static bool plan_tile_permute(const uint32_t *src, const uint32_t *dst, int k, uint32_t L, TpPlan &P) {
+    memset(&P, 0, sizeof P);
+    int wpos[64];
+    for (int i = 0; i < 64; i++) wpos[i] = -1;
+    if (k < 1 || k > kTpTileBits || !tp_layout(src, k, L, P, wpos)) return false;
+    TpMap M;
+    if (!tp_map(P, wpos, nullptr, 0, M)) return false;
+    auto image = [&](uint32_t a) {
+        for (int j = 0; j < k; j++)
+            if (src[j] == a) return dst[j];
+        return a;
+    };
+    for (int j = 0; j < k; j++)
+        if (wpos[dst[j]] < 0) return false;  // an image outside the tile
+    TpSeg &S = P.segs[P.nseg++];
+    tp_fill_seg(M, wpos, S);
+    S.g0 = S.g1 = 0;
+    for (int b = 0; b < kTpLaneBits; b++) P.wlane_img[b] = tp_img((uint32_t)wpos[image(M.lane[b])]);
+    for (int b = 0; b < kTpWarpBits; b++) P.wwarp_img[b] = tp_img((uint32_t)wpos[image(M.warp[b])]);
+    for (int l = 0; l < kTpRegs; l++) P.wreg_img[l] = tp_img((uint32_t)wpos[image(M.reg[l])]);
+    P.permute = 1;
+    return true;
+}
+
+// The two tensor maps of a tile plan (re and im over 2^L f32 amplitudes), 128-byte swizzle.
+// Unused dimensions have extent 1.
+static bool encode_tile_maps(const TpPlan &P, uint32_t L, float *re, float *im, CUtensorMap &tre, CUtensorMap &tim) {
     PFN_encode_tiled enc = tensor_map_encoder();
     if (!enc) return false;
     cuuint64_t dims[5], strides[4];
@@ -805,26 +830,31 @@ static bool encode_boxes(const StagedPlan &P, uint32_t L, float *re, float *im, 
     }
     auto one = [&](CUtensorMap &map, float *base) {
         return enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     };
     return one(tre, re) && one(tim, im);
 }
 
-static int launch_staged(const StagedPlan &P, const CUtensorMap &tre, const CUtensorMap &tim, float *re, float *im,
-                         cudaStream_t s) {
-    static bool attr_done[64] = {false};
+static int launch_tile(const TpPlan &P, uint32_t L, float *re, float *im, cudaStream_t s) {
+    CUtensorMap tre, tim;
+    memset(&tre, 0, sizeof tre);
+    memset(&tim, 0, sizeof tim);
+    if (!encode_tile_maps(P, L, re, im, tre, tim)) return LYTH_E_UNSUPPORTED;
+    static bool attr_done[2][64] = {{false}};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return LYTH_E_INVALID;
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(staged_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStSmem);
+    const int pm = P.permute ? 1 : 0;
+    if (dev >= 0 && dev < 64 && !attr_done[pm][dev]) {
+        const cudaError_t e = pm ? cudaFuncSetAttribute(tile_pass_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTpSmem)
+                                 : cudaFuncSetAttribute(tile_pass_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTpSmem);
         if (e != cudaSuccess) return status_of(e);
-        attr_done[dev] = true;
+        attr_done[pm][dev] = true;
     }
     const uint64_t sms = (uint64_t)device_sms();
     const unsigned grid = (unsigned)(P.ntiles < sms ? P.ntiles : sms);
-    staged_fused_kernel<<<grid, kStThreads, kStSmem, s>>>(P, tre, tim, re, im);
+    if (pm) tile_pass_kernel<true><<<grid, kTpThreads, kTpSmem, s>>>(P, tre, tim);
+    else tile_pass_kernel<false><<<grid, kTpThreads, kTpSmem, s>>>(P, tre, tim);
     return last_launch_status();
 }
 
@@ -840,7 +870,8 @@ int fused_take_device_error() {
     return LYTH_OK;
 }
 
-// LYTH_FUSED_STAGING=0 sends every group to the register pass (an A/B switch: both are bit-exact).
+// LYTH_FUSED_STAGING=0 sends every group to the register pass (an A/B switch: both are bit-exact;
+// groups then hold at most 6 qubits).
 static bool staging_enabled() {
     static int on = -1;
     if (on < 0) {
@@ -850,18 +881,32 @@ static bool staging_enabled() {
     return on == 1;
 }
 
+static bool tile_path(uint64_t len, uint32_t &L) {
+    if (!staging_enabled() || !len || (len & (len - 1))) return false;
+    L = 0;
+    while ((1ull << L) < len) L++;
+    return L >= kTpMinBits;
+}
+
+bool fused_fits(uint64_t len, const uint32_t *bits, int k) {
+    if (k < 1 || k > kFuseMaxQubits) return false;
+    uint32_t L = 0;
+    if (!tile_path(len, L)) return k <= kFuseRegisterQubits;
+    int nhigh = 0;
+    for (int l = 0; l < k; l++) nhigh += bits[l] >= 5;
+    return nhigh <= kTpHighBits;
+}
+
 int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaStream_t s) {
-    if (staging_enabled() && len && !(len & (len - 1)) && !(((uintptr_t)re | (uintptr_t)im) & 15)) {
-        uint32_t L = 0;
-        while ((1ull << L) < len) L++;
-        StagedPlan P;
-        CUtensorMap tre, tim;
-        memset(&tre, 0, sizeof tre);
-        memset(&tim, 0, sizeof tim);
-        bool ok = plan_staged(g, L, 1, P);
-        if (ok && P.tma && !encode_boxes(P, L, re, im, tre, tim)) ok = plan_staged(g, L, 0, P);  // runs instead
-        if (ok) return launch_staged(P, tre, tim, re, im, s);
+    uint32_t L = 0;
+    if (tile_path(len, L) && !(((uintptr_t)re | (uintptr_t)im) & 15)) {
+        TpPlan P;
+        if (plan_tile(g, L, P)) {
+            const int st = launch_tile(P, L, re, im, s);
+            if (st != LYTH_E_UNSUPPORTED) return st;
+        }
     }
+    if (g.k > kFuseRegisterQubits) return LYTH_E_UNSUPPORTED;
     const bool split = g.k >= 5;
     const FusedGroup o = arrange_levels(g, split);
     const uint64_t threads = split ? (len >> g.k) * 2 : (len >> g.k);
@@ -879,57 +924,36 @@ int launch_fused(uint64_t len, const FusedGroup &g, float *re, float *im, cudaSt
 }
 
 // A permutation pass: the amplitude at index i moves to the index whose bit dst[j] is bit src[j]
-// of i (j < k <= 6; dst a permutation of src; other bits unchanged). The staged pass with no gates
-// and each tile bit stored at its image: the permuted bits are tile bits, so every tile maps onto
+// of i (j < k; dst a permutation of src; other bits unchanged). The tile pass with no gates and
+// each tile bit written at its image: the permuted bits are tile bits, so every tile maps onto
 // itself and the pass runs in place. LYTH_E_UNSUPPORTED when the state is too small for tiles.
 bool permute_supported(uint64_t len, const uint32_t *src, int k) {
-    if (k < 1 || k > kFuseMaxQubits || !len || (len & (len - 1))) return false;
     uint32_t L = 0;
-    while ((1ull << L) < len) L++;
-    FusedGroup g{};
-    g.k = k;
-    for (int j = 0; j < k; j++) g.bits[j] = src[j];
-    StagedPlan P;
-    return plan_staged(g, L, 0, P);
+    if (k < 1 || k > kPermuteMaxBits || !tile_path(len, L)) return false;
+    TpPlan P;
+    return plan_tile_permute(src, src, k, L, P);
 }
 
 int launch_permute(uint64_t len, const uint32_t *src, const uint32_t *dst, int k, float *re, float *im,
                    cudaStream_t s) {
-    if (k < 1 || k > kFuseMaxQubits || !len || (len & (len - 1)) || (((uintptr_t)re | (uintptr_t)im) & 15))
-        return LYTH_E_UNSUPPORTED;
     uint32_t L = 0;
-    while ((1ull << L) < len) L++;
-    FusedGroup g{};
-    g.k = k;
-    for (int j = 0; j < k; j++) g.bits[j] = src[j];
-    g.ngates = 0;
-    StagedPlan P;
-    CUtensorMap tre, tim;
-    memset(&tre, 0, sizeof tre);
-    memset(&tim, 0, sizeof tim);
-    bool ok = plan_staged(g, L, 1, P);
-    if (ok && P.tma && !encode_boxes(P, L, re, im, tre, tim)) ok = plan_staged(g, L, 0, P);
-    if (!ok) return LYTH_E_UNSUPPORTED;
-    auto image = [&](uint32_t a) {
-        for (int j = 0; j < k; j++)
-            if (src[j] == a) return dst[j];
-        return a;
-    };
-    for (int b = 0; b < 5; b++) P.dlane_addr[b] = image(P.lane_addr[b]);
-    for (int b = 0; b < kStRegs; b++) P.dreg_addr[b] = image(P.reg_addr[b]);
-    for (int b = 0; b < kStWarpBits; b++) P.dwarp_addr[b] = image(P.warp_addr[b]);
-    return launch_staged(P, tre, tim, re, im, s);
+    if (k < 1 || k > kPermuteMaxBits || !tile_path(len, L) || (((uintptr_t)re | (uintptr_t)im) & 15))
+        return LYTH_E_UNSUPPORTED;
+    TpPlan P;
+    if (!plan_tile_permute(src, dst, k, L, P)) return LYTH_E_UNSUPPORTED;
+    return launch_tile(P, L, re, im, s);
 }
 
 }  // namespace lyth
 
 // ------------------------------------------------------------------ host-only layout self-test
-// The staged pass is correct only if its planner's maps agree: for random groups it checks that
-// every tile element has exactly one shared-memory word, that the copies (runs or tensor-map
-// boxes, with the box coordinates rebuilt from the tile base) and the warps' reads agree on it,
-// that the tensor-map dimensions partition the index space with 16-byte-aligned box origins,
-// that no warp read hits a bank twice, and that every gate's target / control land on the
-// group's bits. No device is touched.
+// The tile pass is correct only if its planner's maps agree. For random groups (and permutations)
+// it checks: the boxes' words cover the tile exactly once with the word positions the plan uses,
+// the tensor-map coordinates rebuild each box origin (inner coordinate 0: 16-byte aligned), every
+// segment's 128-bit accesses cover each word of the tile exactly once and reach all 32 banks in
+// every quarter-warp (with the swizzle), each gate's target is a register level of its segment and
+// its control where the gate says, and a permutation's writes send each word to its image. No
+// device is touched.
 namespace lyth {
 namespace {
 struct SplitMix {
@@ -943,93 +967,154 @@ struct SplitMix {
     uint32_t below(uint32_t n) { return (uint32_t)(next() % n); }
 };
 
-int check_layout(const FusedGroup &g, uint32_t L, const StagedPlan &P, SplitMix &rng) {
-    std::vector<int64_t> word2off(kStCompWords, -1);
-    if (P.tma) {
-        if (P.box_words * P.nbox != (uint32_t)kStTile) return -10;
-        std::vector<int> cover(L, 0);
-        for (int d = 0; d < 5; d++) {
-            if (!P.dim_len[d]) continue;
-            if (d > 0 && P.dim_lo[d] < 2) return -11;  // global strides must be multiples of 16 B
-            for (uint32_t x = 0; x < P.dim_len[d]; x++) {
-                if (P.dim_lo[d] + x >= L) return -12;
-                cover[P.dim_lo[d] + x]++;
-            }
-        }
-        for (uint32_t x = 0; x < L; x++)
-            if (cover[x] != 1) return -13;
-        for (uint32_t b = 0; b < P.nbox; b++)
-            for (uint32_t e = 0; e < P.box_words; e++) {
-                uint32_t rest = e;
-                uint64_t a = P.box_off[b];
-                for (int d = 0; d < 5; d++) {
-                    if (!P.dim_len[d]) continue;
-                    a += (uint64_t)(rest & ((1u << P.dim_box[d]) - 1)) << P.dim_lo[d];
-                    rest >>= P.dim_box[d];
-                }
-                const uint32_t w = b * P.box_words + e;
-                if (word2off[w] != -1) return -14;
-                word2off[w] = (int64_t)a;
-            }
-        uint64_t base = rng.next() % P.ntiles;
-        for (int t = 0; t < kStTileBits; t++) base = insert_bit(base, P.tile_bits[t], 0);
-        for (uint32_t b = 0; b < P.nbox; b++) {
-            const uint64_t a = base + P.box_off[b];
-            uint64_t back = 0;
+// The swizzled word of a logical word.
+uint32_t phys_word(uint32_t w) { return w ^ (((w >> 5) & 7u) << 2); }
+
+int check_tile(const uint32_t *gbits, int k, const FusedGroup *g, const uint32_t *dst, uint32_t L, const TpPlan &P,
+               SplitMix &rng) {
+    // logical word -> address offset, from the boxes (dimension order, iterated boxes on top)
+    std::vector<int64_t> off_of(kTpTile, -1);
+    if (P.box_words * P.nbox != (uint32_t)kTpTile) return -10;
+    for (uint32_t b = 0; b < P.nbox; b++)
+        for (uint32_t e = 0; e < P.box_words; e++) {
+            uint32_t rest = e;
+            uint64_t a = P.box_off[b];
             for (int d = 0; d < 5; d++) {
                 if (!P.dim_len[d]) continue;
-                const uint64_t c = (a >> P.dim_lo[d]) & ((1ull << P.dim_len[d]) - 1);
-                if (c & ((1ull << P.dim_box[d]) - 1)) return -15;  // box origin off its alignment
-                back += c << P.dim_lo[d];
+                a += (uint64_t)(rest & ((1u << P.dim_box[d]) - 1)) << P.dim_lo[d];
+                rest >>= P.dim_box[d];
             }
-            if (back != a) return -16;
+            const uint32_t w = b * P.box_words + e;
+            if (off_of[w] != -1) return -11;
+            off_of[w] = (int64_t)a;
         }
-    } else {
-        for (uint32_t r = 0; r < P.nruns; r++)
-            for (uint32_t o = 0; o < (1u << P.run_bits); o++) {
-                const uint32_t w = P.run_word[r] + o;
-                if (w >= (uint32_t)kStCompWords || word2off[w] != -1) return -17;
-                word2off[w] = (int64_t)(P.run_off[r] + o);
-            }
+    // the offsets are exactly the tile's index space; dims partition [0, L); strides 16-byte aligned
+    std::vector<int> cover(L, 0);
+    for (int d = 0; d < 5; d++) {
+        if (!P.dim_len[d]) continue;
+        if (d > 0 && P.dim_lo[d] < 2) return -12;
+        for (uint32_t x = 0; x < P.dim_len[d]; x++) {
+            if (P.dim_lo[d] + x >= L) return -13;
+            cover[P.dim_lo[d] + x]++;
+        }
     }
-    std::vector<uint8_t> hit(kStTile, 0);
-    for (int wp = 0; wp < kStGroupWarps; wp++)
-        for (int i = 0; i < (1 << kStRegs); i++) {
-            uint32_t banks = 0;
-            for (int lane = 0; lane < 32; lane++) {
-                uint32_t w = 0;
-                uint64_t a = 0;
-                for (int b = 0; b < 5; b++)
-                    if ((lane >> b) & 1) { w += P.lane_w[b]; a += 1ull << P.lane_addr[b]; }
-                for (int b = 0; b < kStWarpBits; b++)
-                    if ((wp >> b) & 1) { w += P.warp_w[b]; a += 1ull << P.warp_addr[b]; }
-                for (int b = 0; b < kStRegs; b++)
-                    if ((i >> b) & 1) { w += P.reg_w[b]; a += 1ull << P.reg_addr[b]; }
-                if (w >= (uint32_t)kStCompWords || word2off[w] != (int64_t)a) return -18;
-                uint32_t idx = 0;  // the element's position among the tile bits
-                for (int t = 0; t < kStTileBits; t++)
-                    if ((a >> P.tile_bits[t]) & 1) idx |= 1u << t;
-                if (hit[idx]++) return -19;
-                banks |= 1u << (w % 32);
+    for (uint32_t x = 0; x < L; x++)
+        if (cover[x] != 1) return -14;
+    std::vector<uint8_t> seen(kTpTile, 0);
+    for (uint32_t w = 0; w < (uint32_t)kTpTile; w++) {
+        uint32_t idx = 0;
+        for (int t = 0; t < kTpTileBits; t++)
+            if ((off_of[w] >> P.tile_bits[t]) & 1) idx |= 1u << t;
+        uint64_t back = 0;
+        for (int t = 0; t < kTpTileBits; t++)
+            if ((idx >> t) & 1) back |= 1ull << P.tile_bits[t];
+        if (back != (uint64_t)off_of[w] || seen[idx]++) return -15;
+    }
+    uint64_t base = rng.next() % P.ntiles;
+    for (int t = 0; t < kTpTileBits; t++) base = insert_bit(base, P.tile_bits[t], 0);
+    for (uint32_t b = 0; b < P.nbox; b++) {
+        const uint64_t a = base + P.box_off[b];
+        uint64_t back = 0;
+        for (int d = 0; d < 5; d++) {
+            if (!P.dim_len[d]) continue;
+            const uint64_t c = (a >> P.dim_lo[d]) & ((1ull << P.dim_len[d]) - 1);
+            if (c & ((1ull << P.dim_box[d]) - 1)) return -16;  // a box origin off its box
+            back += c << P.dim_lo[d];
+        }
+        if (back != a) return -17;
+    }
+    // physical word -> address offset
+    std::vector<int64_t> off_phys(kTpTile, -1);
+    for (uint32_t w = 0; w < (uint32_t)kTpTile; w++) off_phys[phys_word(w)] = off_of[w];
+    // address bit -> its word image, recovered from the logical words
+    auto img_of_bit = [&](uint32_t bit) -> uint32_t {
+        for (uint32_t w = 0; w < (uint32_t)kTpTile; w++)
+            if (off_of[w] == (int64_t)(1ull << bit)) return phys_word(w);
+        return 0xffffffffu;
+    };
+    for (uint32_t s = 0; s < P.nseg; s++) {
+        const TpSeg &S = P.segs[s];
+        std::vector<uint8_t> hit(kTpTile, 0);
+        for (int wp = 0; wp < kTpGroupWarps; wp++)
+            for (int q = 0; q < 8; q++) {
+                uint32_t chunks[4] = {0, 0, 0, 0};
+                for (int lane = 0; lane < 32; lane++) {
+                    uint32_t a = 0;
+                    for (int b = 0; b < kTpLaneBits; b++) if ((lane >> b) & 1) a ^= S.lane_img[b];
+                    for (int b = 0; b < kTpWarpBits; b++) if ((wp >> b) & 1) a ^= S.warp_img[b];
+                    for (int l = 0; l < 3; l++) if ((q >> l) & 1) a ^= S.reg_img[l];
+                    if (a & 3u || a >= (uint32_t)kTpTile) return -18;
+                    for (int e = 0; e < 4; e++) {
+                        if (hit[a + e]++) return -19;
+                        // element e of the chunk holds address bits 0, 1 = e
+                        if ((off_phys[a + e] & 3) != e) return -20;
+                    }
+                    chunks[lane >> 3] |= 1u << ((a >> 2) & 7u);
+                }
+                for (int h = 0; h < 4; h++)
+                    if (chunks[h] != 0xffu) return -21;  // a quarter-warp reaches 8 distinct chunks
             }
-            if (banks != 0xffffffffu) return -20;
+        for (uint32_t i = S.g0; i < S.g1; i++) {
+            if (!g) return -22;
+            const TpGate &tg = P.gates[i];
+            const int T = tg.case_ / 8, C = tg.case_ % 8 - 1;
+            auto reg_bit = [&](int l) -> int64_t {
+                if (l == 0) return 0;
+                if (l == 1) return 1;
+                for (uint32_t bit = 0; bit < L; bit++)
+                    if (img_of_bit(bit) == S.reg_img[l - 2]) return bit;
+                return -1;
+            };
+            if (reg_bit(T) != (int64_t)g->bits[g->gates[i].t]) return -23;
+            int64_t cb = -1;
+            if (C >= 0) cb = reg_bit(C);
+            if (tg.cl >= 0) {
+                if (C >= 0) return -24;
+                const uint32_t im = tg.cl < kTpLaneBits ? S.lane_img[tg.cl] : S.warp_img[tg.cl - kTpLaneBits];
+                for (uint32_t bit = 0; bit < L; bit++)
+                    if (img_of_bit(bit) == im) cb = bit;
+            }
+            if (cb != (g->gates[i].c >= 0 ? (int64_t)g->bits[g->gates[i].c] : -1)) return -25;
         }
-    for (uint32_t gi = 0; gi < g.ngates; gi++) {
-        const StagedGate &sg = P.gates[gi];
-        int64_t tb, cb = -1;
-        if (sg.case_ < 64) {
-            tb = P.reg_addr[sg.case_ / 8];
-            if (sg.case_ % 8 > 0) cb = P.reg_addr[sg.case_ % 8 - 1];
-        } else {
-            tb = P.lane_addr[sg.lt];
-            if (sg.case_ > 64) cb = P.reg_addr[sg.case_ - 65];
+    }
+    if (g) {
+        uint32_t covered = 0;
+        for (uint32_t s = 0; s < P.nseg; s++) {
+            if (P.segs[s].g0 != covered) return -26;
+            covered = P.segs[s].g1;
         }
-        if (sg.lc >= 0) {
-            if (cb >= 0) return -21;
-            cb = P.lane_addr[sg.lc];
-        }
-        if (tb != (int64_t)g.bits[g.gates[gi].t]) return -22;
-        if (cb != (g.gates[gi].c >= 0 ? (int64_t)g.bits[g.gates[gi].c] : -1)) return -23;
+        if (covered != g->ngates) return -27;
+    }
+    if (P.permute) {
+        std::vector<uint8_t> hit(kTpTile, 0);
+        auto image = [&](uint64_t a) {
+            uint64_t o = 0;
+            for (uint32_t bit = 0; bit < L; bit++) {
+                if (!((a >> bit) & 1)) continue;
+                uint32_t to = bit;
+                for (int j = 0; j < k; j++)
+                    if (gbits[j] == bit) to = dst[j];
+                o |= 1ull << to;
+            }
+            return o;
+        };
+        const TpSeg &S = P.segs[0];
+        for (int wp = 0; wp < kTpGroupWarps; wp++)
+            for (int lane = 0; lane < 32; lane++)
+                for (int q = 0; q < 8; q++)
+                    for (int e = 0; e < 4; e++) {
+                        uint32_t r = (uint32_t)e, wr = 0;
+                        for (int b = 0; b < kTpLaneBits; b++)
+                            if ((lane >> b) & 1) { r ^= S.lane_img[b]; wr ^= P.wlane_img[b]; }
+                        for (int b = 0; b < kTpWarpBits; b++)
+                            if ((wp >> b) & 1) { r ^= S.warp_img[b]; wr ^= P.wwarp_img[b]; }
+                        for (int l = 0; l < 3; l++)
+                            if ((q >> l) & 1) { r ^= S.reg_img[l]; wr ^= P.wreg_img[2 + l]; }
+                        if (e & 1) wr ^= P.wreg_img[0];
+                        if (e & 2) wr ^= P.wreg_img[1];
+                        if (wr >= (uint32_t)kTpTile || hit[wr]++) return -28;
+                        if (off_phys[wr] != (int64_t)image((uint64_t)off_phys[r])) return -29;
+                    }
     }
     return LYTH_OK;
 }
@@ -1043,29 +1128,43 @@ extern "C" int lyth_b200_fused_layout_selftest(uint64_t seed, uint32_t groups, u
     SplitMix rng{seed};
     uint32_t n_planned = 0, n_boxes = 0;
     for (uint32_t it = 0; it < groups; it++) {
-        const uint32_t L = kStMinBits + rng.below(34 - kStMinBits);
+        const uint32_t L = kTpMinBits + rng.below(34 - kTpMinBits);
+        // at most 8 bits above bit 4, at most 13 in all; a third of the groups on the low bits
+        const uint32_t span = (it % 3 == 0) ? (L < 16 ? L : 16) : L;
         FusedGroup g{};
         g.k = 1 + (int32_t)rng.below(kFuseMaxQubits);
-        // a third of the groups on the low bits, where lanes hold group bits
-        const uint32_t span = (it % 3 == 0) ? 12 : L;
-        uint32_t used = 0;
-        for (int l = 0; l < g.k;) {
+        uint64_t used = 0;
+        int nhigh = 0, tries = 0;
+        for (int l = 0; l < g.k && tries < 1000; tries++) {
             const uint32_t b = rng.below(span);
-            if (b >= 32 || (used >> b) & 1) continue;
-            used |= 1u << b;
+            if ((used >> b) & 1) continue;
+            if (b >= 5 && nhigh == kTpHighBits) continue;
+            used |= 1ull << b;
+            nhigh += b >= 5;
             g.bits[l++] = b;
         }
-        g.ngates = 1 + rng.below(12);
+        int have = 0;
+        for (uint32_t b = 0; b < 64; b++) have += (used >> b) & 1;
+        g.k = have;
+        g.ngates = 1 + rng.below(kFuseMaxGates);
         for (uint32_t i = 0; i < g.ngates; i++) {
             g.gates[i].t = (int8_t)rng.below((uint32_t)g.k);
             g.gates[i].c = (int8_t)(g.k > 1 && rng.below(2) ? (g.gates[i].t + 1 + rng.below((uint32_t)g.k - 1)) % g.k : -1);
+            for (int e = 0; e < 8; e++) g.gates[i].m[e] = 0.0f;
         }
-        StagedPlan P;
-        if (!plan_staged(g, L, (int)(it % 3), P)) return LYTH_E_UNSUPPORTED;  // every such group must plan
+        TpPlan P;
+        if (!plan_tile(g, L, P)) return LYTH_E_UNSUPPORTED;  // every such group must plan
         n_planned++;
-        n_boxes += P.tma;
-        const int st = check_layout(g, L, P, rng);
+        n_boxes += P.nbox;
+        int st = check_tile(g.bits, g.k, &g, nullptr, L, P, rng);
         if (st) return st;
+        // a permutation of up to kPermuteMaxBits of the group's bits (a random cycle)
+        const int pk = 1 + (int)rng.below((uint32_t)(g.k < kPermuteMaxBits ? g.k : kPermuteMaxBits));
+        uint32_t src[kPermuteMaxBits], dst[kPermuteMaxBits];
+        for (int j = 0; j < pk; j++) src[j] = g.bits[j];
+        for (int j = 0; j < pk; j++) dst[j] = src[(j + 1) % pk];
+        if (!plan_tile_permute(src, dst, pk, L, P)) return LYTH_E_UNSUPPORTED;
+        if ((st = check_tile(src, pk, nullptr, dst, L, P, rng))) return st;
     }
     if (planned) *planned = n_planned;
     if (boxes) *boxes = n_boxes;

@@ -94,6 +94,21 @@ LYTH_D void tensor_load_5d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
         : "memory");
 }
 
+// Tiled tensor-map store of a rank-5 box from this CTA's shared memory (bulk group of the issuing
+// thread; commit and wait below).
+LYTH_D void tensor_store_5d(const CUtensorMap *map, int c0, int c1, int c2, int c3, int c4, uint32_t src) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4, %5}], [%6];" ::"l"(
+            (uint64_t)map),
+        "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(src)
+        : "memory");
+}
+LYTH_D void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// This thread's committed bulk stores have finished reading shared memory.
+LYTH_D void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// This thread's committed bulk stores have completed.
+LYTH_D void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ---- host: tensor maps through the driver entry point (no link-time libcuda).
 typedef CUresult (*PFN_encode_tiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                      const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,

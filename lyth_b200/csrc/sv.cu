@@ -488,7 +488,16 @@ int add_local(lyth_sv *sv, int c, uint32_t t, const U8 &m) {
     if (sv->fuse_k <= 1) return c < 0 ? local_u(sv, t, m) : local_cu(sv, (uint32_t)c, t, m);
     FusedGroup &g = sv->open;
     int extra = (level_of(g, t) < 0) + (c >= 0 && level_of(g, (uint32_t)c) < 0);
-    if (g.ngates > 0 && (g.k + extra > sv->fuse_k || g.ngates == (uint32_t)kFuseMaxGates)) {
+    bool fits = g.k + extra <= sv->fuse_k;
+    if (fits && extra) {  // the union must also run as one pass at this size (fused_fits)
+        uint32_t u[kFuseMaxQubits];
+        int n = 0;
+        for (int l = 0; l < g.k; l++) u[n++] = g.bits[l];
+        if (level_of(g, t) < 0) u[n++] = t;
+        if (c >= 0 && level_of(g, (uint32_t)c) < 0) u[n++] = (uint32_t)c;
+        fits = fused_fits(sv->local_len, u, n);
+    }
+    if (g.ngates > 0 && (!fits || g.ngates == (uint32_t)kFuseMaxGates)) {
         int st = flush_group(sv);
         if (st) return st;
     }
@@ -789,8 +798,8 @@ int normalize(lyth_sv *sv) {
     st = LYTH_OK;
     for (auto &cyc : cycles) {
         while (cyc.size() > 1 && !st) {
-            const size_t m = cyc.size() < (size_t)kFuseMaxQubits ? cyc.size() : (size_t)kFuseMaxQubits;
-            if (src.size() + m > (size_t)kFuseMaxQubits && (st = flush())) break;
+            const size_t m = cyc.size() < (size_t)kPermuteMaxBits ? cyc.size() : (size_t)kPermuteMaxBits;
+            if (src.size() + m > (size_t)kPermuteMaxBits && (st = flush())) break;
             // bits cyc[0..m) rotate: cyc[i] -> cyc[i + 1], cyc[m - 1] -> cyc[0]
             for (size_t i = 0; i < m; i++) {
                 src.push_back(cyc[i]);

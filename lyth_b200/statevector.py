@@ -99,7 +99,9 @@ class StateVector:
         check(lib.lyth_sv_set_timing(self._h, int(on)), "set_timing")
 
     def set_fusion(self, max_qubits: int) -> None:
-        """Fuse consecutive local gates touching at most max_qubits (1..6) bits; 1 = unfused."""
+        """Fuse consecutive local gates touching at most max_qubits (1..13) bits; 1 = unfused.
+        A group must also fit one pass: at most 8 bits above bit 4 (the tile pass, shards of 2^14
+        amplitudes and more), at most 6 bits (the register pass, smaller shards)."""
         check(lib.lyth_sv_set_fusion(self._h, max_qubits), "set_fusion")
 
     def set_remap(self, on: bool) -> None:

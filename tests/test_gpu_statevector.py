@@ -49,14 +49,15 @@ def test_circuits_bit_exact(cuda, case):
     assert st["passes"] <= len(gates) - swaps  # swaps are relabels; fused groups take one pass
 
 
-@pytest.mark.parametrize("case", [1, 2, 4])
+@pytest.mark.parametrize("case", [1, 2, 3, 4, 5])
 def test_fused_equals_unfused_at_every_k(cuda, case):
-    # ADR-0030 Q1: a fused circuit is the unfused circuit, bit for bit, for k = 1..6.
+    # ADR-0030 Q1: a fused circuit is the unfused circuit, bit for bit, for every group size: the
+    # register pass (k <= 6, states below 2^14) and the tile pass (k up to 13, 16 qubits and up).
     name, q, gates = suite()[case]
     re0, im0 = orc.random_state(200 + case, q)
     ur, ui, ust = run_engine(q, gates, re0, im0, fuse=1)
     passes = []
-    for k in range(2, 7):
+    for k in (2, 3, 4, 5, 6, 8, 10, 13):
         fr, fi, fst = run_engine(q, gates, re0, im0, fuse=k)
         assert np.array_equal(bits(fr), bits(ur)), (name, k)
         assert np.array_equal(bits(fi), bits(ui)), (name, k)
@@ -118,22 +119,25 @@ def on_bits(bits, n, rng):
     return g
 
 
-# The staged pass (2^14 amplitudes and more) places group bits below 5 on lanes (shuffle gates),
-# the rest in registers, and with six bits all >= 5 one of them on lane bit 4; controls on lane
-# bits and on register levels in every combination.
+# The tile pass (2^14 amplitudes and more): a group's bits are tile bits, its gates run in segments
+# of at most five register levels (address bits 0 and 1 always among them), controls on register
+# levels or as lane / warp predicates; up to 13 bits, at most 8 of them above bit 4, which makes
+# the tile's boxes (ranges of consecutive bits, iterated beyond four ranges).
 STAGED_BITS = [
     (0, 1, 2, 3, 4, 5), (10, 11, 12, 13, 14, 15), (5, 6, 7, 8, 9, 10), (1, 3, 7, 9, 12, 14),
     (0, 5, 6, 7, 8, 9), (2, 3, 4), (4, 13), (0,), (15,), (3, 4, 5, 6, 7),
+    (0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12), (5, 6, 7, 8, 9, 10, 11, 12), (1, 2, 5, 7, 9, 11, 13, 15),
+    (0, 2, 4, 6, 8, 10, 12, 14, 16, 18, 19), (3, 4, 6, 7, 17, 18, 19, 20, 21, 23),
 ]
 
 
 @pytest.mark.parametrize("bits_", STAGED_BITS, ids=[",".join(map(str, b)) for b in STAGED_BITS])
 def test_staged_groups_bit_exact(cuda, bits_):
-    q = 16
+    q = 16 if max(bits_) < 16 else 24
     gates = on_bits(bits_, 40, cc.Rng(hash(bits_) & 0xFFFF))
     re0, im0 = orc.random_state(500 + len(bits_), q)
     wr, wi = orc.run_gates(as_tuples(gates), re0, im0)
-    gr, gi, st = run_engine(q, gates, re0, im0)
+    gr, gi, st = run_engine(q, gates, re0, im0, fuse=13)
     assert np.array_equal(bits(gr), bits(wr)) and np.array_equal(bits(gi), bits(wi))
     assert st["passes"] == 1  # one fused group
 

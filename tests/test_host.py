@@ -140,8 +140,9 @@ def test_sv_create_refuses_bad_arguments_without_a_device():
 
 
 def test_fused_layout_selftest():
-    # The staged fused pass's planner, on the host: random groups over 14..33 local qubits, runs
-    # and tensor-map boxes, every map consistent and every warp read free of bank conflicts.
+    # The tile pass's planner, on the host: random groups (up to 13 bits, 8 above bit 4) and
+    # permutations over 14..33 local qubits: every map consistent, every quarter-warp access free
+    # of bank conflicts under the swizzle, every gate on its segment's register levels.
     import ctypes as C
 
     import lyth_b200 as lb
@@ -149,7 +150,7 @@ def test_fused_layout_selftest():
     planned, boxes = C.c_uint32(), C.c_uint32()
     st = lb.lib.lyth_b200_fused_layout_selftest(20_260_930, 4000, C.byref(planned), C.byref(boxes))
     assert st == 0, f"layout check {st} failed"
-    assert planned.value == 4000 and boxes.value > 500
+    assert planned.value == 4000 and boxes.value > 4000
 
 
 def test_plan_handle_settings_are_validated_on_the_host():
@@ -158,9 +159,10 @@ def test_plan_handle_settings_are_validated_on_the_host():
     from lyth_b200.statevector import Plan
 
     with Plan(20, 0, 2) as p:
-        for bad in (0, 7):
+        for bad in (0, 14):
             with pytest.raises(lb.LythError):
                 p.set_fusion(bad)
+        for bad in (0, 7):
             with pytest.raises(lb.LythError):
                 p.set_swap_batch(bad)
         assert lb.lib.lyth_sv_set_chunk(p._h, 1000) == lb.E_UNSUPPORTED   # not a power of two

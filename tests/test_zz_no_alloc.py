@@ -57,14 +57,15 @@ def test_exact_fill_zero_and_a_small_call_after_a_large_one(cuda):
     # limit must not read any slot the large call left behind.
     stream = torch.cuda.current_stream().cuda_stream
     big = torch.from_numpy(orc.uniform(93, 1 << 20)).to(cuda).repeat(MAX_N >> 20)  # 1 GiB
-    for n, src in [(MAX_N, big), (0, big), (1000, big), (3, big)]:
-        x = src[:n] if n else src[:1][:0]
-        want = lb.reduce(lb.SUM, x)
+    for n in (MAX_N, 0, 1000, 3):
+        # n = 0: the sum's identity, +0.0 (the workspace entry point refuses an empty tensor's
+        # null pointer, so the bits are compared with the identity directly)
+        want = lb.reduce(lb.SUM, big[:n]).cpu().numpy() if n else np.zeros(1, np.float32)
         got = torch.full((1,), float("nan"), device=cuda)
-        rc = _fn(lb.SUM, n, src.data_ptr(), None, got.data_ptr(), stream)
+        rc = _fn(lb.SUM, n, big.data_ptr(), None, got.data_ptr(), stream)
         assert rc == lb.OK
         torch.cuda.synchronize()
-        assert got.cpu().numpy().view(np.uint32)[0] == want.cpu().numpy().view(np.uint32)[0], n
+        assert got.cpu().numpy().view(np.uint32)[0] == want.view(np.uint32)[0], n
     del big
     torch.cuda.empty_cache()
 
