@@ -476,6 +476,113 @@ int lyth_b200_cu(uint64_t n, uint64_t wc, uint64_t wt, const float *m, const flo
 int lyth_b200_swap(uint64_t n, uint64_t wc, uint64_t wt, const float *re, const float *im, float *qr,
                    float *qi, cudaStream_t stream);
 
+/* ---- the back-end entry: a lowered kernel in, a kernel of this library (or a refusal) out.
+ * Replaces lyth_ptx::emit(&KernelIr, arch) -> Module (crates/lyth-ptx/src/lib.rs:65-253; refusals
+ * EmitError, :48-62) and Function::launch_shared with Arg slots in declaration order
+ * (crates/lyth-cuda/src/lib.rs:483-549). The descriptor is the part of lyth-lang's KernelIr
+ * (crates/lyth-lang/src/ir.rs:24-56) a back end reads: parameters in declaration order, the rank-2
+ * space, tile, coarsen, contraction, reduction, split views (ir.rs:58-81) and the lowered body
+ * (Op, ir.rs:463-503) with the registers each drained buffer takes. Registers are indices into
+ * `ops` (op i defines register i). */
+#define LYTH_TY_U32 0
+#define LYTH_TY_F32 1
+#define LYTH_TY_BUF_F32 2
+#define LYTH_TY_BUF_F16 3
+#define LYTH_TY_BUF_BF16 4
+#define LYTH_IR_LOAD 0   /* name = buffer or view; transposed = rank-2 access [j, i] */
+#define LYTH_IR_PARAM 1  /* name = scalar parameter */
+#define LYTH_IR_CONST 2  /* value */
+#define LYTH_IR_BIN 3    /* bin = LYTH_BIN_*, a, b */
+#define LYTH_IR_FMA 4    /* a * b + c, one rounding */
+#define LYTH_IR_NEG 5    /* a */
+#define LYTH_BIN_ADD 0
+#define LYTH_BIN_SUB 1
+#define LYTH_BIN_MUL 2
+#define LYTH_BIN_DIV 3
+#define LYTH_BIN_MAX 4
+#define LYTH_BIN_MIN 5
+typedef struct lyth_ir_param {
+    const char *name;
+    int32_t ty;                 /* LYTH_TY_* */
+} lyth_ir_param;
+typedef struct lyth_ir_view {   /* element k of `name` is view_index(width, part, k) of `base` */
+    const char *name, *base, *width;
+    uint32_t part;
+} lyth_ir_view;
+typedef struct lyth_ir_op {
+    int32_t kind, bin;
+    int32_t a, b, c;            /* operand registers */
+    double value;
+    const char *name;
+    uint32_t transposed;
+} lyth_ir_op;
+typedef struct lyth_ir_drain {
+    const char *buffer;         /* a buffer parameter or a view */
+    int32_t reg;
+    uint32_t transposed;
+} lyth_ir_drain;
+typedef struct lyth_ir {
+    const char *name, *machine;
+    uint32_t nparams;
+    const lyth_ir_param *params;
+    uint32_t rank;              /* 1, or 2 (a `space i, j`) */
+    uint32_t tile[2];           /* {0, 0}: no tile */
+    uint32_t coarsen[2];        /* {0, 0}: none */
+    uint32_t contract;          /* 1: `contract sum p` (a[i, p] * b[p, j] in the body) */
+    int32_t reduce_op;          /* -1: none; LYTH_SUM / LYTH_MAX / LYTH_MIN (0, 1, 2) */
+    int32_t reduce_reg;
+    const char *reduce_into;
+    uint32_t reduce_via_smem;   /* the declared path is reg -> smem -> dram */
+    uint32_t nviews;
+    const lyth_ir_view *views;
+    uint32_t nops;
+    const lyth_ir_op *ops;
+    uint32_t ndrains;
+    const lyth_ir_drain *drains;
+} lyth_ir;
+#define LYTH_CLASS_SAXPY 1
+#define LYTH_CLASS_AXPBY 2
+#define LYTH_CLASS_LERP 3
+#define LYTH_CLASS_HORNER 4
+#define LYTH_CLASS_COPY2D 5
+#define LYTH_CLASS_TRANSPOSE 6
+#define LYTH_CLASS_TRANSPOSE_TILED 7
+#define LYTH_CLASS_SUM 8
+#define LYTH_CLASS_DOT 9
+#define LYTH_CLASS_MAX 10
+#define LYTH_CLASS_MIN 11
+#define LYTH_CLASS_MATMUL_F32 12
+#define LYTH_CLASS_MATMUL_BF16 13
+#define LYTH_CLASS_HADAMARD_Q 14
+#define LYTH_CLASS_GATE_Q 15
+#define LYTH_CLASS_CU_Q 16
+#define LYTH_CLASS_SWAP_Q 17
+typedef struct lyth_kernel {
+    int32_t cls;                /* LYTH_CLASS_*, 0 when refused */
+    char entry[48];             /* the class's name */
+    uint32_t nparams;           /* the kernel's parameters, declaration order */
+    int32_t param_ty[32];
+    int32_t slot[16];           /* class argument j <- declaration slot slot[j] */
+    uint32_t retargeted;        /* 1: written for another machine the sm_100a file accepts */
+    char message[320];          /* why it was refused (EmitError's text), or a note */
+} lyth_kernel;
+typedef struct lyth_launch {    /* optional: NULL takes the kernel's own launch shape */
+    uint32_t grid;              /* reductions: the number of partials (default lyth_b200_reduce_grid(n)) */
+} lyth_launch;
+/* 0 and a kernel, or LYTH_E_UNSUPPORTED / LYTH_E_INVALID with out->message: no bound (EmitError
+ * NoBound), no drain (NoDrain), an unknown machine (UnknownTarget: sm_100a, sm_100 and the
+ * machines fixtures/machine/sm_100a.json accepts, sm_120), a reduction not staged through shared
+ * memory, a coarsened tile that does not contract, or a body no kernel of this library computes.
+ * Never a fallback: a refusal runs nothing. */
+int lyth_b200_select(const lyth_ir *ir, lyth_kernel *out);
+/* Launch a selected kernel. args[i] points to declaration slot i's value, as cuLaunchKernel's
+ * kernelParams: a uint32_t, a float, or a device pointer (CUdeviceptr) for a buffer. Returns 0,
+ * a CUDA error, or a LYTH refusal (split widths, shapes) before anything runs. */
+int lyth_b200_launch(const lyth_kernel *k, void *const *args, const lyth_launch *launch, cudaStream_t stream);
+/* Device scratch a launch of this kernel with these arguments needs: 0 for every class this
+ * library has (reductions write their partials to the caller's `into` buffer). */
+size_t lyth_b200_workspace_bytes(const lyth_kernel *k, void *const *args);
+
 /* Host-only self-test of the fused pass's tile layouts (no counterpart in the reference; no device
  * is touched): plans `groups` random gate groups over 14..33 local qubits and checks that the
  * copies into shared memory and the warps' reads agree on every amplitude, that tensor-map boxes
