@@ -83,26 +83,28 @@ LYTH_D uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 }
 
 // One 16-byte chunk (32 weights) against its 32 staged x values: INT4 returns sum f x (the caller
-// corrects), NF4 sum code[v] x. The even and odd weights accumulate separately (two lanes of one
-// packed fma) and are added at the end.
+// corrects), NF4 sum code[v] x. Four partial sums -- even and odd weights (the two lanes of one
+// packed fma) of words 0, 2 and of words 1, 3 (two independent fma chains) -- added at the end.
 template <int FMT>
 LYTH_D float chunk_dot(uint4 v, const float *xr, const float *lut) {
     const uint32_t words[4] = {v.x, v.y, v.z, v.w};
-    uint64_t acc = 0;  // (even, odd) = (+0, +0)
+    uint64_t acc[2] = {0, 0};  // words 0, 2 and 1, 3: (even, odd) weights each, from (+0, +0)
 #pragma unroll
     for (int q = 0; q < 4; q++) {
         float f[8];
         decode_word<FMT>(words[q], lut, f);
         const float4 xa = *reinterpret_cast<const float4 *>(xr + 8 * q);
         const float4 xb = *reinterpret_cast<const float4 *>(xr + 8 * q + 4);
-        acc = fma2(pk2(f[0], f[1]), pk2(xa.x, xa.y), acc);
-        acc = fma2(pk2(f[2], f[3]), pk2(xa.z, xa.w), acc);
-        acc = fma2(pk2(f[4], f[5]), pk2(xb.x, xb.y), acc);
-        acc = fma2(pk2(f[6], f[7]), pk2(xb.z, xb.w), acc);
+        uint64_t &a = acc[q & 1];
+        a = fma2(pk2(f[0], f[1]), pk2(xa.x, xa.y), a);
+        a = fma2(pk2(f[2], f[3]), pk2(xa.z, xa.w), a);
+        a = fma2(pk2(f[4], f[5]), pk2(xb.x, xb.y), a);
+        a = fma2(pk2(f[6], f[7]), pk2(xb.z, xb.w), a);
     }
-    float e, o;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(e), "=f"(o) : "l"(acc));
-    return __fadd_rn(e, o);
+    float e0, o0, e1, o1;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(e0), "=f"(o0) : "l"(acc[0]));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(e1), "=f"(o1) : "l"(acc[1]));
+    return __fadd_rn(__fadd_rn(e0, o0), __fadd_rn(e1, o1));
 }
 
 constexpr int kGemvRowStride = 36;  // floats per staged 32-value chunk (pad 4: conflict-free LDS.128)
@@ -150,6 +152,10 @@ LYTH_D void stage_x(uint32_t k, const uint16_t *x, float *xs, float *xsum, uint3
 template <int FMT, bool SHARED_W>
 LYTH_D float row_dot(uint32_t k, uint32_t group, const uint4 *w16, const uint16_t *srow, const float *xs,
                      const float *xsum, const float *lut, int lane) {
+    // the chunk's scale: chunk * 32 / group, a shift when the group is a power of two (a division
+    // by a run-time divisor costs a reciprocal and conversions per chunk otherwise)
+    const bool pow2 = (group & (group - 1)) == 0;
+    const uint32_t gshift = pow2 ? (uint32_t)__ffs(group >> 5) - 1u : 0u;
     const uint32_t steps = k >> 10;  // 32 chunks (one per lane) per warp-step
     float acc = 0.0f;
     for (uint32_t s0 = 0; s0 < steps; s0 += 4) {
@@ -166,7 +172,7 @@ LYTH_D float row_dot(uint32_t k, uint32_t group, const uint4 *w16, const uint16_
                                  : "=r"(v[u].x), "=r"(v[u].y), "=r"(v[u].z), "=r"(v[u].w)
                                  : "l"(w16 + chunk));
                 }
-                sc[u] = half_bits_to_float(srow[(chunk * 32) / group]);
+                sc[u] = half_bits_to_float(srow[pow2 ? (chunk >> gshift) : (chunk * 32) / group]);
             }
         }
 #pragma unroll
