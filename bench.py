@@ -10,8 +10,8 @@ One JSON line on rank 0:
                random normalised state resident in HBM; one step = one layer; strong scaling
                (33 qubits at every N, sharded on the high qubits). Device time (CUDA events on
                the engine's stream), max over ranks.
-  * roofline   the dominant kernel (the fused pass, staged_fused_kernel: one pass per group of
-               consecutive gates on <= 6 qubits): algorithmic bytes (16 B per amplitude: read
+  * roofline   the dominant kernel (the fused pass, tile_pass_kernel: one pass per group of
+               consecutive gates on <= 13 qubits): algorithmic bytes (16 B per amplitude: read
                and write re and im once) / its average device duration inside the timed region;
                traffic = DRAM bytes per launch from an ncu capture of the same kernel, scaled.
   * e2e        the same metric through the public API with host buffers: each step uploads the
@@ -44,12 +44,12 @@ if ROOT not in sys.path:
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0}
 METRIC = "33-qubit statevector gates/s (HBM GB/s per kernel alongside)"
-# DRAM bytes (read + write) per amplitude of one staged fused pass: the mean over the 21 launches
-# of two layers of the benchmark circuit at 2^28 amplitudes (a 4 GiB state, 32x L2), ncu
-# dram__bytes_read.sum + dram__bytes_write.sum (8.006 + 7.781); the algorithmic figure is 16.
+# DRAM bytes (read + write) per amplitude of one fused pass (tile_pass_kernel): the mean over the
+# 12 launches of two layers of the benchmark circuit at 2^28 amplitudes (a 4 GiB state, 32x L2),
+# ncu dram__bytes_read.sum + dram__bytes_write.sum (8.064 + 7.775); the algorithmic figure is 16.
 # Traffic grows with the amplitudes a launch processes, so a launch's traffic is this x its
 # amplitudes.
-FUSED_PASS_DRAM_BYTES_PER_AMP = 15.787
+FUSED_PASS_DRAM_BYTES_PER_AMP = 15.839
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -67,6 +67,17 @@ def circuit_module():
     sys.modules[name] = mod
     spec.loader.exec_module(mod)
     return mod
+
+
+def machine_file_peak():
+    """The dram bandwidth of fixtures/machine/sm_100a.json (lyth-machine/0.1, measured by
+    `python -m lyth_b200.probe machine`), or None."""
+    try:
+        with open(os.path.join(ROOT, "fixtures", "machine", "sm_100a.json")) as f:
+            m = json.load(f)
+        return next(lv["bandwidth_gbs"] for lv in m["levels"] if lv["name"] == "dram")
+    except Exception:
+        return None
 
 
 def peaks():
@@ -745,7 +756,7 @@ def ours(a, dist: Dist) -> None:
     roofline = {"bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4) if achieved else None, "traffic": None,
                 "peak_source": pk_kind,
-                "kernel": "staged_fused_kernel (fused pass: <= 6 qubits, in place, TMA-staged tiles)"
+                "kernel": "tile_pass_kernel (fused pass: <= 13 qubits, in place, TMA-staged 2^13-amplitude tiles)"
                 if dominant == "fused" else "gate_q_kernel (in-place 1-qubit pass)",
                 "algorithmic_bytes_per_launch": int(pass_bytes), "avg_launch_ms": round(d_avg, 4),
                 "launches_timed": d_n,
@@ -759,6 +770,10 @@ def ours(a, dist: Dist) -> None:
                             "GB_s_each_way": round(4.0 * sv.local_len / (tim["swap"][1] / tim["swap"][0] * 1e-3) / 1e9, 1)
                             if tim["swap"][0] else None,
                             "share_of_timed_region": round(tim["swap"][1] / ms, 4) if ms else None}}
+    mf = machine_file_peak()
+    if mf and achieved:
+        roofline["machine_file"] = {"peak": mf, "frac": round(achieved / mf, 4),
+                                    "source": "fixtures/machine/sm_100a.json dram bandwidth_gbs (triad pattern)"}
     if dominant == "fused" and FUSED_PASS_DRAM_BYTES_PER_AMP:
         roofline["traffic"] = int(FUSED_PASS_DRAM_BYTES_PER_AMP * sv.local_len)
 

@@ -2,7 +2,7 @@
 each body is what lyth-lang's lowering makes of the example's `at reg:` lines, fma formed
 exactly where ir.rs:2388-2429 forms one (a * b + c -> fma(a, b, c); lhs + t * d -> fma(t, d,
 lhs); a product of a negated parameter -> neg then mul), the file cited per kernel."""
-from lyth_b200.ir import Kernel
+from .ir import Kernel
 
 U, F, B, H = "u32", "f32", "f32[]", "bf16[]"
 

@@ -8,7 +8,7 @@ import torch
 import lyth_b200 as lb
 from lyth_b200 import circuit as cc
 from oracle import oracle as orc
-from tests import examples_ir as ex
+from lyth_b200 import examples as ex
 from tests.conftest import bits
 
 pytestmark = pytest.mark.gpu

@@ -6,7 +6,7 @@ import pytest
 
 import lyth_b200 as lb
 from lyth_b200 import ir
-from tests import examples_ir as ex
+from lyth_b200 import examples as ex
 
 
 @pytest.mark.parametrize("name", sorted(ex.IN_SCOPE))
