@@ -631,8 +631,19 @@ int lyth_sv_set_local(lyth_sv *sv, const float *re, const float *im);
 int lyth_sv_get_local(lyth_sv *sv, float *re, float *im);
 /* Apply `count` gates in order. Returns when the work is queued on lyth_sv_stream. */
 int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count);
-/* Wait for the handle's streams; LYTH_E_TIMEOUT if a pass gave up one of its bounded waits. */
+/* Wait for the handle's streams; LYTH_E_TIMEOUT if a pass gave up one of its bounded waits. With
+ * an NCCL communicator the wait polls the streams and ncclCommGetAsyncError and gives up at the
+ * handle's deadline (lyth_sv_set_deadline): an async error aborts the communicator
+ * (ncclCommAbort) and returns LYTH_E_NCCL; the deadline aborts it and returns LYTH_E_TIMEOUT. An
+ * aborted handle refuses further collective work with LYTH_E_NCCL; destroy it. */
 int lyth_sv_sync(lyth_sv *sv);
+/* The host-side deadline of the handle's NCCL waits, in milliseconds (>= 1; default 300000). No
+ * counterpart in the reference (no multi-GPU code). */
+int lyth_sv_set_deadline(lyth_sv *sv, double ms);
+/* Host-only check of the deadline logic with fake hooks, no device or NCCL (scenario 0: done after
+ * 3 polls -> LYTH_OK; 1: async error -> LYTH_E_NCCL, one abort; 2: never done -> LYTH_E_TIMEOUT at
+ * the deadline, one abort; 3: a CUDA error from the stream -> that status, no abort). */
+int lyth_sv_deadline_selftest(int scenario, double deadline_ms, int *aborts, uint64_t *polls);
 /* Counters since creation: data passes run, exchange steps run, bytes sent over NCCL. */
 int lyth_sv_stats(const lyth_sv *sv, uint64_t *passes, uint64_t *exchanges, uint64_t *bytes_sent);
 /* Kernel launches since creation (every pass, exchange chunk and permutation kernel). */

@@ -24,6 +24,7 @@
 // NCCL is opened with dlopen on first use by a multi-rank handle, so the library itself loads
 // (and serves every single-GPU entry point) without it.
 #include <dlfcn.h>
+#include <time.h>
 #include <unistd.h>
 #include <math.h>
 #include <nccl.h>
@@ -44,6 +45,7 @@ struct NcclApi {
     ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
     ncclResult_t (*GroupStart)() = nullptr;
     ncclResult_t (*GroupEnd)() = nullptr;
     ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
@@ -65,6 +67,7 @@ static bool load_nccl() {
     LYTH_SYM(CommInitRank, "ncclCommInitRank");
     LYTH_SYM(CommDestroy, "ncclCommDestroy");
     LYTH_SYM(CommAbort, "ncclCommAbort");
+    LYTH_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
     LYTH_SYM(GroupStart, "ncclGroupStart");
     LYTH_SYM(GroupEnd, "ncclGroupEnd");
     LYTH_SYM(Send, "ncclSend");
@@ -211,6 +214,41 @@ __global__ void flag_wait_kernel(const __grid_constant__ FlagSet fs, uint64_t ta
     flag_wait_bounded(fs.flag[t], target, kWaitNs, &g_sv_error);
 }
 
+// ---- host waits with a deadline (the NCCL transport's failure path)
+// query(): 0 = the awaited work is done, 1 = not yet, anything else a CUDA status to return.
+// async_error(): nonzero once the communicator reports an error (ncclCommGetAsyncError). On an
+// async error the communicator is aborted and LYTH_E_NCCL returned; past `deadline_ms` it is
+// aborted and LYTH_E_TIMEOUT returned. ncclCommAbort makes the NCCL kernels a dead peer left
+// waiting return, so the streams drain afterwards.
+struct WaitHooks {
+    void *ctx;
+    int (*query)(void *);
+    int (*async_error)(void *);
+    void (*abort)(void *);
+};
+
+int wait_with_deadline(const WaitHooks &h, double deadline_ms, uint32_t poll_us, uint64_t *polls) {
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    for (uint64_t i = 0;; i++) {
+        if (polls) *polls = i + 1;
+        const int q = h.query(h.ctx);
+        if (q == 0) return LYTH_OK;
+        if (q != 1) return q;
+        if (h.async_error && h.async_error(h.ctx)) {
+            if (h.abort) h.abort(h.ctx);
+            return LYTH_E_NCCL;
+        }
+        clock_gettime(CLOCK_MONOTONIC, &t1);
+        const double ms = (t1.tv_sec - t0.tv_sec) * 1e3 + (t1.tv_nsec - t0.tv_nsec) * 1e-6;
+        if (ms > deadline_ms) {
+            if (h.abort) h.abort(h.ctx);
+            return LYTH_E_TIMEOUT;
+        }
+        if (poll_us) usleep(poll_us);
+    }
+}
+
 }  // namespace lyth
 
 using namespace lyth;
@@ -229,6 +267,11 @@ struct lyth_sv {
     cudaEvent_t ev_recv[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_start = nullptr;
     cudaEvent_t ev_packed[2] = {nullptr, nullptr};
     ncclComm_t comm = nullptr;
+    // The communicator was aborted (an NCCL async error, or a host wait past the deadline): every
+    // later collective step of this handle refuses with LYTH_E_NCCL, and teardown skips
+    // ncclCommDestroy (the abort freed the communicator).
+    bool comm_aborted = false;
+    double deadline_ms = 300000.0;  // lyth_sv_set_deadline
     std::vector<uint32_t> pos;  // logical qubit -> physical bit
     std::vector<uint32_t> inv;  // physical bit -> logical qubit
     uint64_t passes = 0, exchanges = 0, bytes_sent = 0, launches = 0;
@@ -295,6 +338,39 @@ struct DeviceGuard {
 };
 
 int nccl_status(ncclResult_t r) { return r == ncclSuccess ? LYTH_OK : LYTH_E_NCCL; }
+
+// Synchronise `stream` of a handle. With a live communicator the wait polls the stream and the
+// communicator's async error and gives up at the handle's deadline (wait_with_deadline): a peer
+// that died leaves this rank with LYTH_E_NCCL or LYTH_E_TIMEOUT and an aborted communicator
+// instead of a hang. Without one it is a plain synchronisation.
+struct SyncCtx {
+    lyth_sv *sv;
+    cudaStream_t stream;
+};
+int sync_stream(lyth_sv *sv, cudaStream_t stream) {
+    if (!stream) return LYTH_OK;
+    if (!sv->comm || sv->comm_aborted || !g_nccl.CommGetAsyncError) return status_of(cudaStreamSynchronize(stream));
+    SyncCtx c{sv, stream};
+    WaitHooks h;
+    h.ctx = &c;
+    h.query = [](void *p) {
+        const cudaError_t e = cudaStreamQuery(static_cast<SyncCtx *>(p)->stream);
+        if (e == cudaSuccess) return 0;
+        if (e == cudaErrorNotReady) return 1;
+        return status_of(e);
+    };
+    h.async_error = [](void *p) {
+        ncclResult_t r = ncclSuccess;
+        if (g_nccl.CommGetAsyncError(static_cast<SyncCtx *>(p)->sv->comm, &r) != ncclSuccess) return 1;
+        return (r != ncclSuccess && r != ncclInProgress) ? 1 : 0;
+    };
+    h.abort = [](void *p) {
+        lyth_sv *v = static_cast<SyncCtx *>(p)->sv;
+        if (g_nccl.CommAbort && v->comm) g_nccl.CommAbort(v->comm);
+        v->comm_aborted = true;
+    };
+    return wait_with_deadline(h, sv->deadline_ms, 50, nullptr);
+}
 
 void reset_map(lyth_sv *sv) {
     sv->pos.resize(sv->qubits);
@@ -1018,7 +1094,7 @@ void teardown_ce(lyth_sv *sv) {
 
 void free_all(lyth_sv *sv) {
     teardown_ce(sv);
-    if (sv->comm && g_nccl.CommDestroy) g_nccl.CommDestroy(sv->comm);
+    if (sv->comm && !sv->comm_aborted && g_nccl.CommDestroy) g_nccl.CommDestroy(sv->comm);
     cudaFree(sv->flags);
     cudaFree(sv->re);
     cudaFree(sv->im);
@@ -1134,8 +1210,8 @@ int lyth_sv_destroy(lyth_sv *sv) {
         return LYTH_OK;
     }
     DeviceGuard guard(sv);
-    if (sv->stream) cudaStreamSynchronize(sv->stream);
-    if (sv->comm_stream) cudaStreamSynchronize(sv->comm_stream);
+    sync_stream(sv, sv->stream);
+    sync_stream(sv, sv->comm_stream);
     free_all(sv);
     delete sv;
     return LYTH_OK;
@@ -1198,6 +1274,7 @@ int lyth_sv_get_local(lyth_sv *sv, float *re, float *im) {
     if (!sv) return LYTH_E_INVALID;
     if (sv->plan) return normalize(sv);
     if (!re || !im) return LYTH_E_INVALID;
+    if (sv->comm_aborted) return LYTH_E_NCCL;
     DeviceGuard guard(sv);
     int st = normalize(sv);
     if (st) return st;
@@ -1208,6 +1285,7 @@ int lyth_sv_get_local(lyth_sv *sv, float *re, float *im) {
 
 int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count) {
     if (!sv || (count && !gates)) return LYTH_E_INVALID;
+    if (sv->comm_aborted) return LYTH_E_NCCL;
     DeviceGuard guard(sv);
     for (uint64_t i = 0; i < count; i++) {
         int st = apply_one(sv, gates, count, i);
@@ -1227,9 +1305,9 @@ int lyth_sv_set_transport(lyth_sv *sv, int copy_engine) {
         DeviceGuard guard(sv);
         // drain the current transport before switching: partners must have pulled every chunk,
         // and this rank's own pulls on the copy stream must have landed
-        int st = status_of(cudaStreamSynchronize(sv->comm_stream));
-        if (!st && sv->copy_stream) st = status_of(cudaStreamSynchronize(sv->copy_stream));
-        if (!st) st = status_of(cudaStreamSynchronize(sv->stream));
+        int st = sync_stream(sv, sv->comm_stream);
+        if (!st && sv->copy_stream) st = sync_stream(sv, sv->copy_stream);
+        if (!st) st = sync_stream(sv, sv->stream);
         if (st) return st;
         if (sv->ce && !copy_engine)
             for (int b = 0; b < 2; b++)
@@ -1248,9 +1326,9 @@ int lyth_sv_set_chunk(lyth_sv *sv, uint64_t elements) {
     if (elements < 1024 || (elements & (elements - 1)) || elements > cap) return LYTH_E_UNSUPPORTED;
     if (!sv->plan) {
         DeviceGuard guard(sv);
-        int st = status_of(cudaStreamSynchronize(sv->comm_stream));
-        if (!st && sv->copy_stream) st = status_of(cudaStreamSynchronize(sv->copy_stream));
-        if (!st) st = status_of(cudaStreamSynchronize(sv->stream));
+        int st = sync_stream(sv, sv->comm_stream);
+        if (!st && sv->copy_stream) st = sync_stream(sv, sv->copy_stream);
+        if (!st) st = sync_stream(sv, sv->stream);
         if (st) return st;
     }
     sv->chunk = elements;
@@ -1281,10 +1359,11 @@ int lyth_sv_sync(lyth_sv *sv) {
     if (!sv) return LYTH_E_INVALID;
     if (sv->plan) return LYTH_OK;
     DeviceGuard guard(sv);
-    int st = status_of(cudaStreamSynchronize(sv->comm_stream));
+    if (sv->comm_aborted) return LYTH_E_NCCL;
+    int st = sync_stream(sv, sv->comm_stream);
     if (st) return st;
-    if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
-    if ((st = fused_take_device_error())) return st;  // a staged pass that gave up a bounded wait
+    if ((st = sync_stream(sv, sv->stream))) return st;
+    if ((st = fused_take_device_error())) return st;  // a tile pass that gave up a bounded wait
     return sv->ce ? device_sv_error() : LYTH_OK;       // a transport flag wait that did
 }
 
@@ -1359,3 +1438,36 @@ int lyth_sv_plan_clear(lyth_sv *sv) {
 }
 
 }  // extern "C"
+
+int lyth_sv_set_deadline(lyth_sv *sv, double ms) {
+    if (!sv) return LYTH_E_INVALID;
+    if (!(ms >= 1.0)) return LYTH_E_UNSUPPORTED;
+    sv->deadline_ms = ms;
+    return LYTH_OK;
+}
+
+// Host-only check of wait_with_deadline with fake hooks (no device, no NCCL): scenario 0 = the
+// work completes after 3 polls; 1 = the communicator reports an async error at the 2nd poll;
+// 2 = the work never completes (the deadline passes); 3 = the stream reports a CUDA error.
+extern "C" int lyth_sv_deadline_selftest(int scenario, double deadline_ms, int *aborts, uint64_t *polls) {
+    struct Fake {
+        int scenario, n, aborts;
+    } f{scenario, 0, 0};
+    WaitHooks h;
+    h.ctx = &f;
+    h.query = [](void *p) {
+        Fake *x = static_cast<Fake *>(p);
+        x->n++;
+        if (x->scenario == 0) return x->n >= 3 ? 0 : 1;
+        if (x->scenario == 3) return x->n >= 2 ? (int)cudaErrorLaunchFailure : 1;
+        return 1;
+    };
+    h.async_error = [](void *p) {
+        Fake *x = static_cast<Fake *>(p);
+        return (x->scenario == 1 && x->n >= 2) ? 1 : 0;
+    };
+    h.abort = [](void *p) { static_cast<Fake *>(p)->aborts++; };
+    const int st = wait_with_deadline(h, deadline_ms, 100, polls);
+    if (aborts) *aborts = f.aborts;
+    return st;
+}

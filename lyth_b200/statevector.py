@@ -104,6 +104,11 @@ class StateVector:
         amplitudes and more), at most 6 bits (the register pass, smaller shards)."""
         check(lib.lyth_sv_set_fusion(self._h, max_qubits), "set_fusion")
 
+    def set_deadline(self, ms: float) -> None:
+        """Host deadline of the handle's NCCL waits (ms): past it, or on an NCCL async error, the
+        communicator is aborted and sync returns an error instead of hanging."""
+        check(lib.lyth_sv_set_deadline(self._h, float(ms)), "set_deadline")
+
     def set_remap(self, on: bool) -> None:
         """Rank-bit gates: swap the qubit into a local bit first (True, default) or exchange the
         whole shard and compute this rank's row (False)."""

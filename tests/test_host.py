@@ -227,3 +227,33 @@ def test_engine_fusion_groups_match_lyth_circuit_fuse(k):
                 assert o["kind"] in ("u", "cu"), o["kind"]
                 got.append(sorted({o["a"]} | ({o["b"]} if o["kind"] == "cu" else set()), reverse=True))
         assert got == [grp.qubits for grp in want], (q, k)
+
+
+def test_nccl_wait_deadline_logic_on_the_host():
+    # The multi-GPU sync's failure path (ncclCommGetAsyncError polling, ncclCommAbort on an error
+    # or at a host deadline) with fake hooks: no device, no NCCL.
+    import ctypes as C
+
+    import lyth_b200 as lb
+
+    aborts, polls = C.c_int32(), C.c_uint64()
+    assert lb.lib.lyth_sv_deadline_selftest(0, 1000.0, C.byref(aborts), C.byref(polls)) == lb.OK
+    assert aborts.value == 0 and polls.value == 3
+    assert lb.lib.lyth_sv_deadline_selftest(1, 1000.0, C.byref(aborts), C.byref(polls)) == lb.E_NCCL
+    assert aborts.value == 1 and polls.value == 2
+    import time
+
+    t0 = time.perf_counter()
+    assert lb.lib.lyth_sv_deadline_selftest(2, 50.0, C.byref(aborts), C.byref(polls)) == lb.E_TIMEOUT
+    assert aborts.value == 1 and 0.04 < time.perf_counter() - t0 < 5.0
+    assert lb.lib.lyth_sv_deadline_selftest(3, 1000.0, C.byref(aborts), C.byref(polls)) == 719  # cudaErrorLaunchFailure
+    assert aborts.value == 0
+
+
+def test_deadline_setting_is_checked():
+    import lyth_b200 as lb
+    from lyth_b200.statevector import Plan
+
+    with Plan(20, 0, 2) as p:
+        assert lb.lib.lyth_sv_set_deadline(p._h, 0.5) == lb.E_UNSUPPORTED
+        assert lb.lib.lyth_sv_set_deadline(p._h, 2000.0) == lb.OK
