@@ -424,6 +424,42 @@ def kernel_cases(dev, small: bool = False):
     transpose_case("copy2d_4096", lb.copy2d)
     transpose_case("transpose_naive_4096", lb.transpose_naive)
 
+    def big_transpose_case(name, fn, side):
+        def setup():
+            a = torch.rand(side, side, device=dev, generator=g)
+            b = torch.empty(side, side, device=dev)
+            return (lambda: fn(a, b)), 8.0 * side * side, "bytes"
+        cases[name] = setup
+
+    # at 16x L2 (2 GiB moved): the HBM figures of the transpose and its coalesced control
+    S = 8192 if small else 16384
+    big_transpose_case(f"transpose_tiled_{S}", lb.transpose_tiled, S)
+    big_transpose_case(f"copy2d_{S}", lb.copy2d, S)
+
+    def narrow_case(name, p, body, nbytes_per, dt):
+        def setup():
+            n = 1 << p
+            x = torch.rand(n, device=dev, generator=g).to(dt)
+            y = torch.rand(n, device=dev, generator=g).to(dt)
+            return (lambda: body(x, y)), nbytes_per * n, "bytes"
+        cases[name] = setup
+
+    # ADR-0024 narrow storage: the same kernels at half the bytes
+    narrow_case(f"saxpy_bf16_2^{P}", P, lambda x, y: lb.stream_narrow(lb.STREAM_SAXPY, [2.5], x, y, y), 6.0,
+                torch.bfloat16)
+    narrow_case(f"saxpy_f16_2^{P}", P, lambda x, y: lb.stream_narrow(lb.STREAM_SAXPY, [2.5], x, y, y), 6.0,
+                torch.float16)
+    narrow_case(f"sum_bf16_2^{P}", P, lambda x, y: lb.reduce_partials_narrow(lb.SUM, x), 2.0, torch.bfloat16)
+
+    def narrow_transpose_case(name, side):
+        def setup():
+            a = torch.rand(side, side, device=dev, generator=g).to(torch.bfloat16)
+            b = torch.empty(side, side, device=dev, dtype=torch.bfloat16)
+            return (lambda: lb.transpose_narrow(a, b)), 4.0 * side * side, "bytes"
+        cases[name] = setup
+
+    narrow_transpose_case(f"transpose_bf16_{S}", S)
+
     def gemv_case(name, fmt):
         def setup():
             rows, k, grp = 14336, 4096, 64

@@ -476,6 +476,26 @@ int lyth_b200_cu(uint64_t n, uint64_t wc, uint64_t wt, const float *m, const flo
 int lyth_b200_swap(uint64_t n, uint64_t wc, uint64_t wt, const float *re, const float *im, float *qr,
                    float *qi, cudaStream_t stream);
 
+/* ---- narrow storage (f16 / bf16 buffers, f32 arithmetic: crates/lyth-ptx/src/lib.rs:607-732,
+ * docs/ADR-0024-half-the-element.md). Each element is widened exactly on load, the body is the f32
+ * kernel's chain, and each drained value is rounded once, to nearest even, at the store
+ * (eval.rs:557-570 round_narrow_outputs). Buffers hold the 16-bit patterns. */
+#define LYTH_NARROW_F16 1
+#define LYTH_NARROW_BF16 2
+#define LYTH_STREAM_SAXPY 0   /* out = fma(a, x, y); scalars {a}; out may be y */
+#define LYTH_STREAM_AXPBY 1   /* out = fma(a, x, b * y); scalars {a, b} */
+#define LYTH_STREAM_LERP 2    /* out = fma(t, y - x, x); scalars {t} */
+#define LYTH_STREAM_HORNER 3  /* out = ((c3 x + c2) x + c1) x + c0 as three fmas; scalars {c0, c1, c2, c3} */
+#define LYTH_STREAM_COPY 4    /* out = x (examples/copy2d.lyth at 2 bytes an element) */
+int lyth_b200_stream_narrow(int op, int ty, uint64_t n, const float *scalars, const uint16_t *x, const uint16_t *y,
+                            uint16_t *out, cudaStream_t stream);
+/* b[j, i] = a[i, j] for 2-byte elements (examples/transpose-tiled.lyth at f16 / bf16 storage). */
+int lyth_b200_transpose_narrow(int ty, uint32_t rows, uint32_t cols, const uint16_t *a, uint16_t *b,
+                               cudaStream_t stream);
+/* One f32 partial per block from f16 / bf16 inputs, in lyth_b200_reduce_partials's order. */
+int lyth_b200_reduce_partials_narrow(int op, int ty, uint64_t n, const uint16_t *x, const uint16_t *y, uint32_t grid,
+                                     float *partial, cudaStream_t stream);
+
 /* ---- the back-end entry: a lowered kernel in, a kernel of this library (or a refusal) out.
  * Replaces lyth_ptx::emit(&KernelIr, arch) -> Module (crates/lyth-ptx/src/lib.rs:65-253; refusals
  * EmitError, :48-62) and Function::launch_shared with Arg slots in declaration order
@@ -564,6 +584,7 @@ typedef struct lyth_kernel {
     int32_t param_ty[32];
     int32_t slot[16];           /* class argument j <- declaration slot slot[j] */
     uint32_t retargeted;        /* 1: written for another machine the sm_100a file accepts */
+    int32_t storage;            /* 0: f32 buffers; LYTH_NARROW_F16 / _BF16: every data buffer 16-bit */
     char message[320];          /* why it was refused (EmitError's text), or a note */
 } lyth_kernel;
 typedef struct lyth_launch {    /* optional: NULL takes the kernel's own launch shape */

@@ -128,6 +128,9 @@ _sig("lyth_sv_plan_count", _u64, [_vp])
 _sig("lyth_sv_plan_op", _i32, [_vp, _u64, C.POINTER(SvOp)])
 _sig("lyth_sv_plan_clear", _i32, [_vp])
 _sig("lyth_b200_device_error", _i32, [])
+_sig("lyth_b200_stream_narrow", _i32, [_i32, _i32, _u64, C.POINTER(_f32), _vp, _vp, _vp, _vp])
+_sig("lyth_b200_transpose_narrow", _i32, [_i32, _u32, _u32, _vp, _vp, _vp])
+_sig("lyth_b200_reduce_partials_narrow", _i32, [_i32, _i32, _u64, _vp, _vp, _u32, _vp, _vp])
 _sig("lyth_b200_wait_selftest", _i32, [_i32, _u32, _vp])
 _sig("lyth_b200_fused_layout_selftest", _i32, [_u64, _u32, C.POINTER(_u32), C.POINTER(_u32)])
 
@@ -266,6 +269,49 @@ def reduce(op: int, x, y=None, out=None, workspace=None, stream=None):
                                _ptr(workspace, name="workspace"), workspace.numel() * workspace.element_size(),
                                _stream(stream)), "reduce")
     return out
+
+
+# ----------------------------------------------------------------------------- narrow storage
+NARROW_F16, NARROW_BF16 = 1, 2
+STREAM_SAXPY, STREAM_AXPBY, STREAM_LERP, STREAM_HORNER, STREAM_COPY = 0, 1, 2, 3, 4
+
+
+def _narrow_ty(t) -> int:
+    import torch
+
+    if t.dtype == torch.float16:
+        return NARROW_F16
+    if t.dtype == torch.bfloat16:
+        return NARROW_BF16
+    raise TypeError(f"narrow storage is float16 or bfloat16, got {t.dtype}")
+
+
+def stream_narrow(op: int, scalars, x, y, out, stream=None) -> None:
+    """ADR-0024 narrow-storage streams: x, y, out all float16 (or all bfloat16) CUDA tensors, the f32
+    chain of the op on the widened elements, each output rounded once (RNE) at the store."""
+    ty = _narrow_ty(out)
+    sc = (_f32 * 4)(*([float(v) for v in scalars] + [0.0] * (4 - len(scalars))))
+    check(lib.lyth_b200_stream_narrow(op, ty, out.numel(), sc, _ptr(x, x.dtype, "x"),
+                                      None if y is None else _ptr(y, x.dtype, "y"), _ptr(out, x.dtype, "out"),
+                                      _stream(stream)), "stream_narrow")
+
+
+def transpose_narrow(a, b, stream=None) -> None:
+    rows, cols = a.shape
+    check(lib.lyth_b200_transpose_narrow(_narrow_ty(a), rows, cols, _ptr(a, a.dtype, "a"), _ptr(b, a.dtype, "b"),
+                                         _stream(stream)), "transpose_narrow")
+
+
+def reduce_partials_narrow(op: int, x, y=None, grid: int | None = None, stream=None):
+    import torch
+
+    n = x.numel()
+    g = int(lib.lyth_b200_reduce_grid(n)) if grid is None else grid
+    part = torch.empty(g, dtype=torch.float32, device=x.device)
+    check(lib.lyth_b200_reduce_partials_narrow(op, _narrow_ty(x), n, _ptr(x, x.dtype, "x"),
+                                               None if y is None else _ptr(y, x.dtype, "y"), g,
+                                               _ptr(part, _f32t(), "partial"), _stream(stream)), "reduce_partials_narrow")
+    return part
 
 
 # ----------------------------------------------------------------------------- contraction

@@ -33,9 +33,11 @@ inline unsigned stream_grid(uint64_t units_total, uint64_t units_per_block) {
 }
 
 // LYTH_E_TIMEOUT (and the flag cleared) if a bounded device wait of that file's kernels ran
-// out since the last call, else LYTH_OK (k_gemv.cu, k_probe.cu; the fused pass's in fused.cuh).
+// out since the last call, else LYTH_OK (k_gemv.cu, k_probe.cu, k_stream.cu; the fused pass's in
+// fused.cuh).
 int gemv_take_device_error();
 int probe_take_device_error();
+int transpose_take_device_error();
 
 inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 

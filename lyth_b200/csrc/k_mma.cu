@@ -268,9 +268,11 @@ extern "C" int lyth_b200_device_error(void) {
     const int fused = fused_take_device_error();
     const int gemv = gemv_take_device_error();
     const int probe = probe_take_device_error();
+    const int tx = transpose_take_device_error();
     if (fused != LYTH_OK) return fused;
     if (gemv != LYTH_OK) return gemv;
     if (probe != LYTH_OK) return probe;
+    if (tx != LYTH_OK) return tx;
     int v = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
     if (e != cudaSuccess) return status_of(e);

@@ -42,10 +42,19 @@ LYTH_D float combine(float a, float b) {
     return OP == 1 ? fmaxf(a, b) : fminf(a, b);
 }
 
+// Element j of a buffer of storage type TY (0 f32, 1 f16, 2 bf16) as f32: the widening of a narrow
+// element is exact (ADR-0024: storage, not arithmetic, is narrow).
+template <int TY>
+LYTH_D float load_el(const void *p, uint64_t j) {
+    if (TY == 0) return static_cast<const float *>(p)[j];
+    const uint16_t h = static_cast<const uint16_t *>(p)[j];
+    return TY == 1 ? __half2float(__ushort_as_half(h)) : __uint_as_float((uint32_t)h << 16);
+}
+
 // One block's partial, in the reference's order. `grid` is the grid of the reference's launch
 // (the stride is grid * 256); blocks at or past it contribute the identity.
-template <int OP, bool DOT>
-LYTH_D float block_partial(uint64_t n, const float *x, const float *y, uint64_t grid, float *slots) {
+template <int OP, bool DOT, int TY = 0>
+LYTH_D float block_partial(uint64_t n, const void *x, const void *y, uint64_t grid, float *slots) {
     const unsigned t = threadIdx.x;
     const uint64_t stride = grid * kRedBlock;
     float acc = identity_of<OP>();
@@ -57,7 +66,7 @@ LYTH_D float block_partial(uint64_t n, const float *x, const float *y, uint64_t 
 #pragma unroll
             for (int u = 0; u < kRedPerThread; u++) {
                 const uint64_t j = i + (uint64_t)u * stride;
-                if (j < n) v[u] = DOT ? __fmul_rn(x[j], y[j]) : x[j];
+                if (j < n) v[u] = DOT ? __fmul_rn(load_el<TY>(x, j), load_el<TY>(y, j)) : load_el<TY>(x, j);
             }
 #pragma unroll
             for (int u = 0; u < kRedPerThread; u++) {
@@ -89,6 +98,15 @@ __global__ void __launch_bounds__(kRedBlock) reduce_partials_kernel(I n, const f
                                                                     float *partial) {
     __shared__ float slots[kRedBlock];
     const float v = block_partial<OP, DOT>((uint64_t)n, x, y, gridDim.x, slots);
+    if (threadIdx.x == 0) partial[blockIdx.x] = v;
+}
+
+// Narrow storage (f16 / bf16 inputs, f32 partials): the same order, each element widened exactly.
+template <int OP, bool DOT, int TY>
+__global__ void __launch_bounds__(kRedBlock) reduce_partials_narrow_kernel(uint64_t n, const uint16_t *x,
+                                                                           const uint16_t *y, float *partial) {
+    __shared__ float slots[kRedBlock];
+    const float v = block_partial<OP, DOT, TY>(n, x, y, gridDim.x, slots);
     if (threadIdx.x == 0) partial[blockIdx.x] = v;
 }
 
@@ -177,6 +195,25 @@ extern "C" uint32_t lyth_b200_reduce_grid(uint64_t n) {
     if (g == 0) g = 1;
     if (g > (1u << 20)) g = 1u << 20;
     return (uint32_t)g;
+}
+
+template <int TY>
+static int launch_partials_narrow(int op, uint64_t n, const uint16_t *x, const uint16_t *y, uint32_t grid,
+                                  float *partial, cudaStream_t s) {
+    if (op == 0 && y) reduce_partials_narrow_kernel<0, true, TY><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
+    else if (op == 0) reduce_partials_narrow_kernel<0, false, TY><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
+    else if (op == 1 && !y) reduce_partials_narrow_kernel<1, false, TY><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
+    else if (op == 2 && !y) reduce_partials_narrow_kernel<2, false, TY><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
+    else return LYTH_E_UNSUPPORTED;
+    return last_launch_status();
+}
+
+extern "C" int lyth_b200_reduce_partials_narrow(int op, int ty, uint64_t n, const uint16_t *x, const uint16_t *y,
+                                                uint32_t grid, float *partial, cudaStream_t s) {
+    if (!x || !partial || grid == 0) return LYTH_E_INVALID;
+    if (ty == LYTH_NARROW_F16) return launch_partials_narrow<1>(op, n, x, y, grid, partial, s);
+    if (ty == LYTH_NARROW_BF16) return launch_partials_narrow<2>(op, n, x, y, grid, partial, s);
+    return LYTH_E_UNSUPPORTED;
 }
 
 extern "C" int lyth_b200_reduce_partials(int op, uint64_t n, const float *x, const float *y, uint32_t grid,

@@ -6,7 +6,12 @@
 // the 148 SMs, two vectors per stream in flight per thread; a scalar path serves unaligned
 // buffers and the n % 4 tail. The arithmetic is the lowered body, op for op: fma only where
 // ir.rs:2388-2429 forms one, every other op one rounding (built with -fmad=false).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <string.h>
+
 #include "common.cuh"
+#include "mbar.cuh"
 
 namespace lyth {
 
@@ -182,6 +187,209 @@ __global__ void __launch_bounds__(256) transpose_tiled_kernel(I rows_, I cols_, 
     }
 }
 
+// ------------------------------------------------------------------ the TMA-staged transpose
+// The tiled transpose for shapes whose rows and columns are multiples of 4 (16-byte row pitches,
+// what a tensor map needs): 32 x 32 tiles move global -> shared and shared -> global as tensor-map
+// boxes (cp.async.bulk.tensor.2d, no multicast), never through the SM's load/store units.
+//
+// The reference skews its shared tile to a 33-word row (ir.rs:2056-2062): a column walk then hits
+// 32 distinct banks. A TMA box lands densely, 128 bytes a row, so the skew becomes the tensor
+// map's 128-byte swizzle: the 16-byte chunk c of row r is stored at chunk c ^ (r & 7). A thread
+// moves a 4 x 4 block -- four 128-bit loads of rows 4tr..4tr+3 at chunk tc, a transpose in
+// registers, four 128-bit stores into the output tile's rows 4tc..4tc+3 at chunk tr -- and the
+// 64 threads of a tile take (tr, tc) = (p ^ q, p) for lane p = t % 8 of group q = t / 8, so the 8
+// lanes of every quarter-warp reach 8 distinct chunks on both the loads (tc ^ (4tr + i) & 7) and
+// the stores (tr ^ (4tc + j) & 7): no bank conflicts, which is what the skew was for.
+//
+// A CTA is four teams of 64 threads; a team double-buffers its input tiles (the tile two ahead is
+// loaded while this one is transposed), writes the transposed tile to its output buffer, and its
+// leader stores it with one box (edges clip: coordinates past the extents are not written) and
+// waits for the store to have read the buffer before the team writes it again. Every wait is
+// bounded; the team decides together (bar.red.and) whether a tile arrived.
+constexpr int kTxTeams = 4, kTxTeamThreads = 64;
+constexpr uint32_t kTxTileBytes = 32 * 32 * sizeof(float);
+constexpr size_t kTxSmem = 1024 + (size_t)kTxTeams * 3 * kTxTileBytes + kTxTeams * 2 * sizeof(uint64_t);
+__device__ int g_tx_error;
+
+LYTH_D void tensor_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+LYTH_D void tensor_store_2d(const CUtensorMap *map, int c0, int c1, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"((uint64_t)map),
+                 "r"(c0), "r"(c1), "r"(src)
+                 : "memory");
+}
+LYTH_D float4 tx_lds(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a) : "memory");
+    return v;
+}
+LYTH_D void tx_sts(uint32_t a, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
+}
+LYTH_D void team_sync(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "n"(kTxTeamThreads) : "memory"); }
+LYTH_D bool team_all(int id, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred a, b;\n\t"
+        "setp.ne.u32 a, %1, 0;\n\t"
+        "bar.red.and.pred b, %2, %3, a;\n\t"
+        "selp.u32 %0, 1, 0, b;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)p), "r"(id), "n"(kTxTeamThreads)
+        : "memory");
+    return r != 0;
+}
+
+__global__ void __launch_bounds__(kTxTeams * kTxTeamThreads)
+    transpose_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ CUtensorMap tout,
+                         uint32_t rows, uint32_t cols) {
+    extern __shared__ uint8_t tx_raw[];
+    const uint32_t raw = smem_u32(tx_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;  // the 128-byte swizzle repeats every 1 KiB
+    const int team = threadIdx.x / kTxTeamThreads, t = threadIdx.x % kTxTeamThreads;
+    const int bar_id = 1 + team;
+    const uint32_t in0 = base + (uint32_t)team * 3 * kTxTileBytes, out = in0 + 2 * kTxTileBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(tx_raw + (base - raw) + (size_t)kTxTeams * 3 * kTxTileBytes) + team * 2;
+    const uint32_t tiles_x = (cols + 31) / 32, tiles_y = (rows + 31) / 32;
+    const uint64_t tiles = (uint64_t)tiles_x * tiles_y;
+    const uint64_t stride = (uint64_t)gridDim.x * kTxTeams;
+    const uint64_t first = (uint64_t)blockIdx.x * kTxTeams + team;
+    const uint64_t mine = tiles > first ? (tiles - first + stride - 1) / stride : 0;
+    auto tile_of = [&](uint64_t k) { return first + k * stride; };
+    auto load = [&](uint64_t k) {
+        const uint64_t tl = tile_of(k);
+        const uint32_t b = smem_u32(bars + (k & 1));
+        mbar_expect_tx(b, kTxTileBytes);
+        tensor_load_2d(in0 + (uint32_t)(k & 1) * kTxTileBytes, &tin, (int)((tl % tiles_x) * 32), (int)((tl / tiles_x) * 32),
+                       b);
+    };
+    if (t == 0) {
+        mbar_init(smem_u32(bars), 1);
+        mbar_init(smem_u32(bars + 1), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (uint64_t k = 0; k < 2 && k < mine; k++) load(k);
+    }
+    team_sync(bar_id);
+    const int p = t & 7, q = t >> 3;
+    const int tc = p, tr = p ^ q;
+    uint64_t armed = mine < 2 ? mine : 2, used = 0;
+    for (uint64_t k = 0; k < mine; k++) {
+        const bool ok = mbar_wait(smem_u32(bars + (k & 1)), (uint32_t)(k >> 1) & 1u, &g_tx_error);
+        if (!team_all(bar_id, ok)) break;
+        used++;
+        const uint32_t in = in0 + (uint32_t)(k & 1) * kTxTileBytes;
+        float4 v[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t r = 4 * tr + i;
+            v[i] = tx_lds(in + r * 128u + (uint32_t)((tc ^ (r & 7)) << 4));
+        }
+        if (t == 0) bulk_wait_read0();  // the previous tile's store has read the output buffer
+        team_sync(bar_id);
+        // every thread has read this stage: the leader may refill it with the tile two ahead
+        if (t == 0 && k + 2 < mine) {
+            load(k + 2);
+            armed++;
+        }
+        const float4 o[4] = {make_float4(v[0].x, v[1].x, v[2].x, v[3].x), make_float4(v[0].y, v[1].y, v[2].y, v[3].y),
+                             make_float4(v[0].z, v[1].z, v[2].z, v[3].z), make_float4(v[0].w, v[1].w, v[2].w, v[3].w)};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t r = 4 * tc + j;
+            tx_sts(out + r * 128u + (uint32_t)((tr ^ (r & 7)) << 4), o[j]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        team_sync(bar_id);
+        if (t == 0) {
+            const uint64_t tl = tile_of(k);
+            tensor_store_2d(&tout, (int)((tl / tiles_x) * 32), (int)((tl % tiles_x) * 32), out);
+            bulk_commit();
+        }
+    }
+    if (t == 0) {
+        bulk_wait0();
+        // after a timed-out wait, a load may still be in flight: wait for it (bounded)
+        for (uint64_t k = used; k < armed; k++) mbar_wait(smem_u32(bars + (k & 1)), (uint32_t)(k >> 1) & 1u, &g_tx_error);
+    }
+}
+
+// ------------------------------------------------------------------ narrow storage (ADR-0024)
+// f16 / bf16 buffers, f32 arithmetic: each element is widened exactly on load, the body runs the
+// same f32 chain as the f32 kernel, and each drained value is rounded once, to nearest even, at
+// the store (cvt.rn: eval.rs:557-570's round_narrow_outputs). 128-bit vectors carry 8 elements.
+template <int TY>
+LYTH_D float widen(uint16_t h) {
+    return TY == 1 ? __half2float(__ushort_as_half(h)) : __uint_as_float((uint32_t)h << 16);
+}
+template <int TY>
+LYTH_D uint16_t narrow(float f) {
+    return TY == 1 ? __half_as_ushort(__float2half_rn(f)) : __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+template <int TY, typename F>
+LYTH_D uint32_t pair(const F &f, uint32_t x, uint32_t y) {
+    const uint16_t lo = narrow<TY>(f(widen<TY>((uint16_t)(x & 0xffffu)), widen<TY>((uint16_t)(y & 0xffffu))));
+    const uint16_t hi = narrow<TY>(f(widen<TY>((uint16_t)(x >> 16)), widen<TY>((uint16_t)(y >> 16))));
+    return (uint32_t)lo | ((uint32_t)hi << 16);
+}
+
+template <int TY, bool TWO_IN, typename F>
+__global__ void __launch_bounds__(256) stream_narrow_kernel(uint64_t n, F f, const uint16_t *x, const uint16_t *y,
+                                                            uint16_t *out) {
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t nthreads = (uint64_t)gridDim.x * blockDim.x;
+    const bool vec = ((((uintptr_t)x) | ((uintptr_t)out) | (TWO_IN ? (uintptr_t)y : 0)) & 15u) == 0;
+    if (vec) {
+        const uint64_t nv = n >> 3;  // 8 elements per 16-byte vector
+        for (uint64_t v = tid; v < nv; v += nthreads) {
+            const uint4 xv = *reinterpret_cast<const uint4 *>(x + 8 * v);
+            const uint4 yv = TWO_IN ? *reinterpret_cast<const uint4 *>(y + 8 * v) : make_uint4(0, 0, 0, 0);
+            uint4 o;
+            o.x = pair<TY>(f, xv.x, yv.x);
+            o.y = pair<TY>(f, xv.y, yv.y);
+            o.z = pair<TY>(f, xv.z, yv.z);
+            o.w = pair<TY>(f, xv.w, yv.w);
+            *reinterpret_cast<uint4 *>(out + 8 * v) = o;
+        }
+        for (uint64_t i = (nv << 3) + tid; i < n; i += nthreads)
+            out[i] = narrow<TY>(f(widen<TY>(x[i]), TWO_IN ? widen<TY>(y[i]) : 0.f));
+    } else {
+        for (uint64_t i = tid; i < n; i += nthreads)
+            out[i] = narrow<TY>(f(widen<TY>(x[i]), TWO_IN ? widen<TY>(y[i]) : 0.f));
+    }
+}
+
+// The transpose of 2-byte elements (either narrow type: a transpose moves bits): 32 x 32 tiles in
+// shared memory with a 34-element row (17 words, coprime with the 32 banks: the derived skew for
+// 2-byte elements), 8 rows per warp pass.
+__global__ void __launch_bounds__(256) transpose_u16_kernel(uint32_t rows, uint32_t cols, const uint16_t *a,
+                                                            uint16_t *b) {
+    __shared__ uint16_t tile[32 * 34];
+    const uint32_t tiles_x = (cols + 31) / 32, tiles_y = (rows + 31) / 32;
+    const uint64_t tiles = (uint64_t)tiles_x * tiles_y;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (uint64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const uint32_t r0 = (uint32_t)(t / tiles_x) * 32, c0 = (uint32_t)(t % tiles_x) * 32;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t r = r0 + ty + 8 * k, c = c0 + tx;
+            tile[(ty + 8 * k) * 34 + tx] = (r < rows && c < cols) ? a[(uint64_t)r * cols + c] : (uint16_t)0;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t oc = ty + 8 * k;  // output row c0 + oc, output column r0 + tx
+            const uint32_t c = c0 + oc, r = r0 + tx;
+            if (c < cols && r < rows) b[(uint64_t)c * rows + r] = tile[tx * 34 + oc];
+        }
+        __syncthreads();
+    }
+}
+
 // Explicit instantiations: u32 for the ADR-0016 launchers, u64 for the B200 surface.
 template __global__ void saxpy_kernel<uint32_t>(uint32_t, float, const float *, float *);
 template __global__ void axpby_kernel<uint32_t>(uint32_t, float, float, const float *, float *);
@@ -239,11 +447,110 @@ extern "C" int lyth_b200_transpose_naive(uint32_t rows, uint32_t cols, const flo
     transpose_kernel<uint32_t><<<stream_grid(n, kStreamBlock), kStreamBlock, 0, s>>>(rows, cols, a, b);
     return last_launch_status();
 }
+namespace {
+// The tensor maps of the TMA transpose: a (rows x cols, row-major) and b (cols x rows), 32 x 32
+// boxes, 128-byte swizzle. False when the shape or the buffers do not allow one.
+bool transpose_maps(uint32_t rows, uint32_t cols, const float *a, float *b, CUtensorMap &ta, CUtensorMap &tb) {
+    if ((rows & 3u) || (cols & 3u) || !aligned16(a) || !aligned16(b)) return false;
+    PFN_encode_tiled enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint32_t box[2] = {32, 32}, estr[2] = {1, 1};
+    const cuuint64_t da[2] = {cols, rows}, sa[1] = {(cuuint64_t)cols * sizeof(float)};
+    const cuuint64_t db[2] = {rows, cols}, sb[1] = {(cuuint64_t)rows * sizeof(float)};
+    memset(&ta, 0, sizeof ta);
+    memset(&tb, 0, sizeof tb);
+    return enc(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a), da, sa, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
+           enc(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, b, db, sb, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+               CUDA_SUCCESS;
+}
+}  // namespace
+
+namespace lyth {
+int transpose_take_device_error() {
+    int v = 0;
+    const cudaError_t e = cudaMemcpyFromSymbol(&v, g_tx_error, sizeof(int));
+    if (e != cudaSuccess) return status_of(e);
+    if (v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_tx_error, &zero, sizeof(int));
+        return LYTH_E_TIMEOUT;
+    }
+    return LYTH_OK;
+}
+}  // namespace lyth
+
 extern "C" int lyth_b200_transpose_tiled(uint32_t rows, uint32_t cols, const float *a, float *b, cudaStream_t s) {
     if ((uint64_t)rows * cols == 0) return LYTH_OK;
     if (!a || !b) return LYTH_E_INVALID;
+    CUtensorMap ta, tb;
+    if (transpose_maps(rows, cols, a, b, ta, tb)) {
+        static bool attr_done[64] = {false};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return LYTH_E_INVALID;
+        if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+            const cudaError_t e =
+                cudaFuncSetAttribute(transpose_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTxSmem);
+            if (e != cudaSuccess) return status_of(e);
+            attr_done[dev] = true;
+        }
+        const uint64_t tiles = (uint64_t)((rows + 31) / 32) * ((cols + 31) / 32);
+        uint64_t grid = (tiles + kTxTeams - 1) / kTxTeams;
+        const uint64_t cap = (uint64_t)device_sms() * 4;  // four CTAs (16 teams) per SM
+        if (grid > cap) grid = cap;
+        transpose_tma_kernel<<<(unsigned)grid, kTxTeams * kTxTeamThreads, kTxSmem, s>>>(ta, tb, rows, cols);
+        return last_launch_status();
+    }
     const uint64_t tiles = (uint64_t)((rows + kTile - 1) / kTile) * ((cols + kTile - 1) / kTile);
     const unsigned grid = (unsigned)(tiles < 0x7fffffffull ? tiles : 0x7fffffffull);
     transpose_tiled_kernel<uint32_t><<<grid, 256, 0, s>>>(rows, cols, a, b);
+    return last_launch_status();
+}
+
+// ------------------------------------------------------------------ narrow storage surface
+namespace {
+template <int TY>
+int launch_stream_narrow(int op, uint64_t n, const float *c, const uint16_t *x, const uint16_t *y, uint16_t *out,
+                         cudaStream_t s) {
+    const unsigned grid = stream_grid((n + 7) / 8, kStreamBlock);
+    switch (op) {
+        case LYTH_STREAM_SAXPY: stream_narrow_kernel<TY, true><<<grid, kStreamBlock, 0, s>>>(n, SaxpyBody{c[0]}, x, y, out); break;
+        case LYTH_STREAM_AXPBY: stream_narrow_kernel<TY, true><<<grid, kStreamBlock, 0, s>>>(n, AxpbyBody{c[0], c[1]}, x, y, out); break;
+        case LYTH_STREAM_LERP: stream_narrow_kernel<TY, true><<<grid, kStreamBlock, 0, s>>>(n, LerpBody{c[0]}, x, y, out); break;
+        case LYTH_STREAM_HORNER:
+            stream_narrow_kernel<TY, false><<<grid, kStreamBlock, 0, s>>>(n, HornerBody{c[0], c[1], c[2], c[3]}, x, y, out);
+            break;
+        case LYTH_STREAM_COPY: stream_narrow_kernel<TY, false><<<grid, kStreamBlock, 0, s>>>(n, CopyBody{}, x, y, out); break;
+        default: return LYTH_E_UNSUPPORTED;
+    }
+    return last_launch_status();
+}
+}  // namespace
+
+extern "C" int lyth_b200_stream_narrow(int op, int ty, uint64_t n, const float *scalars, const uint16_t *x,
+                                       const uint16_t *y, uint16_t *out, cudaStream_t s) {
+    if (n == 0) return LYTH_OK;
+    const bool two_in = op == LYTH_STREAM_SAXPY || op == LYTH_STREAM_AXPBY || op == LYTH_STREAM_LERP;
+    if (!x || !out || (two_in && !y) || (op != LYTH_STREAM_COPY && !scalars)) return LYTH_E_INVALID;
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    const int nc = op == LYTH_STREAM_HORNER ? 4 : (op == LYTH_STREAM_AXPBY ? 2 : (op == LYTH_STREAM_COPY ? 0 : 1));
+    for (int i = 0; i < nc; i++) c[i] = scalars[i];
+    if (ty == LYTH_NARROW_F16) return launch_stream_narrow<1>(op, n, c, x, y, out, s);
+    if (ty == LYTH_NARROW_BF16) return launch_stream_narrow<2>(op, n, c, x, y, out, s);
+    return LYTH_E_UNSUPPORTED;
+}
+
+extern "C" int lyth_b200_transpose_narrow(int ty, uint32_t rows, uint32_t cols, const uint16_t *a, uint16_t *b,
+                                          cudaStream_t s) {
+    if (ty != LYTH_NARROW_F16 && ty != LYTH_NARROW_BF16) return LYTH_E_UNSUPPORTED;
+    if ((uint64_t)rows * cols == 0) return LYTH_OK;
+    if (!a || !b) return LYTH_E_INVALID;
+    const uint64_t tiles = (uint64_t)((rows + 31) / 32) * ((cols + 31) / 32);
+    uint64_t grid = tiles;
+    const uint64_t cap = (uint64_t)device_sms() * 8;
+    if (grid > cap) grid = cap;
+    transpose_u16_kernel<<<(unsigned)grid, 256, 0, s>>>(rows, cols, a, b);
     return last_launch_status();
 }

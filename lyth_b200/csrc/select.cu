@@ -277,15 +277,40 @@ extern "C" int lyth_b200_select(const lyth_ir *ir, lyth_kernel *out) {
     }
     std::string types;
     for (uint32_t i = 0; i < ir->nparams; i++) types += type_letter(ir->params[i].ty);
+    // Narrow storage (ADR-0024): the streams, the transposes and the reductions also run with every
+    // data buffer f16, or every one bf16 (a reduction's partials stay f32), as the f32 class.
+    int storage = 0;
+    std::string widened = types;
+    {
+        const int into = ir->reduce_op >= 0 ? cn.param(ir->reduce_into) : -1;
+        bool mixed = false;
+        for (uint32_t i = 0; i < ir->nparams; i++) {
+            const int ty = ir->params[i].ty;
+            if (ty != LYTH_TY_BUF_F16 && ty != LYTH_TY_BUF_BF16) continue;
+            const int st = ty == LYTH_TY_BUF_F16 ? LYTH_NARROW_F16 : LYTH_NARROW_BF16;
+            if ((int)i == into || (storage && storage != st)) mixed = true;
+            storage = st;
+            widened[i] = 'B';
+        }
+        if (mixed) storage = -1;
+    }
     const uint32_t rank = ir->rank ? ir->rank : 1;
     const uint32_t tiled = (ir->tile[0] || ir->tile[1]) ? 1u : 0u;
     for (const ClassSpec &c : kClasses) {
-        if (types != c.types || rank != c.rank || ir->contract != c.contract || body != c.body) continue;
+        if (rank != c.rank || ir->contract != c.contract || body != c.body) continue;
+        const bool narrow_ok = c.cls != LYTH_CLASS_MATMUL_F32 && c.cls != LYTH_CLASS_MATMUL_BF16 &&
+                               c.cls != LYTH_CLASS_HADAMARD_Q && c.cls != LYTH_CLASS_GATE_Q && c.cls != LYTH_CLASS_CU_Q &&
+                               c.cls != LYTH_CLASS_SWAP_Q && c.cls != LYTH_CLASS_TRANSPOSE;
+        int st = 0;
+        if (types == c.types) st = 0;
+        else if (storage > 0 && narrow_ok && widened == c.types) st = storage;
+        else continue;
         if (c.cls == LYTH_CLASS_TRANSPOSE || c.cls == LYTH_CLASS_TRANSPOSE_TILED) {
             if (tiled != c.tiled) continue;
         }
         out->cls = c.cls;
-        snprintf(out->entry, sizeof out->entry, "%s", c.entry);
+        out->storage = st;
+        snprintf(out->entry, sizeof out->entry, "%s%s", c.entry, st == LYTH_NARROW_F16 ? "_f16" : (st == LYTH_NARROW_BF16 ? "_bf16" : ""));
         for (uint32_t i = 0; i < ir->nparams && i < 16; i++) out->slot[i] = (int32_t)i;
         if (out->retargeted)
             snprintf(out->message, sizeof out->message, "kernel `%s` written for `%s`, run as %s on sm_100a (retarget "
@@ -317,6 +342,36 @@ extern "C" int lyth_b200_launch(const lyth_kernel *k, void *const *args, const l
         for (int j = 0; j < 8; j++) m[j] = f(i0 + j);
     };
     float m[8];
+    if (k->storage > 0) {
+        auto bn = [&](int i) { return reinterpret_cast<uint16_t *>(*static_cast<const uint64_t *>(args[i])); };
+        const int ty = k->storage;
+        float c[4];
+        switch (k->cls) {
+            case LYTH_CLASS_SAXPY: c[0] = f(1); return lyth_b200_stream_narrow(LYTH_STREAM_SAXPY, ty, u(0), c, bn(2), bn(3), bn(3), s);
+            case LYTH_CLASS_AXPBY:
+                c[0] = f(1); c[1] = f(2);
+                return lyth_b200_stream_narrow(LYTH_STREAM_AXPBY, ty, u(0), c, bn(3), bn(4), bn(4), s);
+            case LYTH_CLASS_LERP: c[0] = f(1); return lyth_b200_stream_narrow(LYTH_STREAM_LERP, ty, u(0), c, bn(2), bn(3), bn(4), s);
+            case LYTH_CLASS_HORNER:
+                for (int i = 0; i < 4; i++) c[i] = f(1 + i);
+                return lyth_b200_stream_narrow(LYTH_STREAM_HORNER, ty, u(0), c, bn(5), nullptr, bn(6), s);
+            case LYTH_CLASS_COPY2D:
+                return lyth_b200_stream_narrow(LYTH_STREAM_COPY, ty, (uint64_t)u(0) * u(1), nullptr, bn(2), nullptr, bn(3), s);
+            case LYTH_CLASS_TRANSPOSE_TILED: return lyth_b200_transpose_narrow(ty, u(0), u(1), bn(2), bn(3), s);
+            case LYTH_CLASS_SUM:
+            case LYTH_CLASS_MAX:
+            case LYTH_CLASS_MIN: {
+                const int op = k->cls == LYTH_CLASS_SUM ? 0 : (k->cls == LYTH_CLASS_MAX ? 1 : 2);
+                const uint32_t grid = launch && launch->grid ? launch->grid : lyth_b200_reduce_grid(u(0));
+                return lyth_b200_reduce_partials_narrow(op, ty, u(0), bn(1), nullptr, grid, bf(2), s);
+            }
+            case LYTH_CLASS_DOT: {
+                const uint32_t grid = launch && launch->grid ? launch->grid : lyth_b200_reduce_grid(u(0));
+                return lyth_b200_reduce_partials_narrow(0, ty, u(0), bn(1), bn(2), grid, bf(3), s);
+            }
+            default: return LYTH_E_UNSUPPORTED;
+        }
+    }
     switch (k->cls) {
         case LYTH_CLASS_SAXPY: return lyth_b200_saxpy(u(0), f(1), bf(2), bf(3), s);
         case LYTH_CLASS_AXPBY: return lyth_b200_axpby(u(0), f(1), f(2), bf(3), bf(4), s);

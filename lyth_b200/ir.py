@@ -59,7 +59,8 @@ class _Ir(C.Structure):
 
 class _Kernel(C.Structure):
     _fields_ = [("cls", C.c_int32), ("entry", C.c_char * 48), ("nparams", C.c_uint32), ("param_ty", C.c_int32 * 32),
-                ("slot", C.c_int32 * 16), ("retargeted", C.c_uint32), ("message", C.c_char * 320)]
+                ("slot", C.c_int32 * 16), ("retargeted", C.c_uint32), ("storage", C.c_int32),
+                ("message", C.c_char * 320)]
 
 
 class _Launch(C.Structure):
@@ -83,6 +84,7 @@ class Selected:
         self.cls = int(k.cls)
         self.entry = k.entry.decode()
         self.retargeted = bool(k.retargeted)
+        self.storage = int(k.storage)  # 0 f32, 1 f16, 2 bf16 (every data buffer)
         self.note = k.message.decode()
         self.types = [int(k.param_ty[i]) for i in range(k.nparams)]
 

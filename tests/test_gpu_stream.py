@@ -78,7 +78,8 @@ def test_adr16_family_elementwise(cuda):
 
 
 # ADR-0017's ragged shapes, plus the headline 4096^2.
-SHAPES = [(1, 1), (33, 17), (31, 129), (1024, 33), (64, 64), (257, 300), (4095, 4095), (4097, 4097), (4096, 4096)]
+SHAPES = [(1, 1), (33, 17), (31, 129), (1024, 33), (64, 64), (257, 300), (4095, 4095), (4097, 4097), (4096, 4096),
+          (4, 4), (36, 100), (100, 68), (1028, 516), (8, 4096)]  # multiples of 4: the TMA path, edges clipped
 
 
 @pytest.mark.parametrize("rows,cols", SHAPES)

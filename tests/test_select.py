@@ -44,10 +44,27 @@ def test_out_of_scope_bodies_are_refused():
                            ("cr", "f32[]")])
     k.drain("cr", k.sub(k.mul(k.load("ar"), k.load("br")), k.mul(k.load("ai"), k.load("bi"))))
     assert "no kernel for" in refused(k)
-    # narrow storage saxpy is not a class of this library
-    k = ir.Kernel("saxpy16", [("n", "u32"), ("a", "f32"), ("x", "f16[]"), ("y", "f16[]")])
+    # mixed narrow storage (an f16 input, a bf16 output) is no class of this library
+    k = ir.Kernel("saxpy_mixed", [("n", "u32"), ("a", "f32"), ("x", "f16[]"), ("y", "bf16[]")])
     k.drain("y", k.fma(k.param("a"), k.load("x"), k.load("y")))
     refused(k)
+    # a narrow state-vector gate is not either (the gate kernels are f32)
+    k = ex.gate_q()
+    k.params = [(n, 3 if t == 2 else t) for n, t in k.params]
+    refused(k)
+
+
+@pytest.mark.parametrize("name", ["saxpy", "axpby", "lerp", "horner", "copy2d", "transpose_tiled", "sum", "dot",
+                                  "max_of", "min_of"])
+@pytest.mark.parametrize("ty", ["f16[]", "bf16[]"])
+def test_narrow_storage_selects_the_class(name, ty):
+    # ADR-0024: every data buffer f16 (or every one bf16), f32 arithmetic; partials stay f32
+    k = ex.IN_SCOPE[name]()
+    into = k.reduction[2] if k.reduction else None
+    k.params = [(n, ir.TY[ty] if t == ir.TY["f32[]"] and n != into else t) for n, t in k.params]
+    sel = k.select()
+    assert sel.entry == name + ("_f16" if ty == "f16[]" else "_bf16")
+    assert sel.storage == (1 if ty == "f16[]" else 2)
 
 
 def test_lyth_ptx_refusals():
