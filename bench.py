@@ -112,6 +112,8 @@ def args_():
                     help="most rank-bit qubits per swap-in (1..6; default: the engine's)")
     ap.add_argument("--transport", choices=["copy_engine", "nccl"], default=None,
                     help="swap-in transport at N > 1 (default: the engine's)")
+    ap.add_argument("--pull-queues", type=int, default=None,
+                    help="copy-engine queues per swap-in pull at N > 1 (1..8; default: the engine's)")
     ap.add_argument("--case", default=None, help="run one kernel case (small config) and exit")
     ap.add_argument("--case-reps", type=int, default=3)
     ap.add_argument("--list-cases", action="store_true")
@@ -737,6 +739,8 @@ def ours(a, dist: Dist) -> None:
         sv.set_swap_batch(a.swap_batch)
     if a.transport and dist.world > 1:
         sv.set_transport(a.transport == "copy_engine")
+    if a.pull_queues and dist.world > 1:
+        lb.check(lb.lib.lyth_sv_set_pull_queues(sv._h, a.pull_queues), "set_pull_queues")
     total_layers = a.warmup + a.steps
     gates = cc.layered(q, total_layers, cc.Rng(cc.BENCH_SEED))
     per = len(gates) // total_layers

@@ -111,6 +111,7 @@ _sig("lyth_sv_get_local", _i32, [_vp, _vp, _vp])
 _sig("lyth_sv_apply", _i32, [_vp, C.POINTER(Gate), _u64])
 _sig("lyth_sv_sync", _i32, [_vp])
 _sig("lyth_sv_set_deadline", _i32, [_vp, C.c_double])
+_sig("lyth_sv_set_pull_queues", _i32, [_vp, _i32])
 _sig("lyth_sv_deadline_selftest", _i32, [_i32, C.c_double, C.POINTER(_i32), C.POINTER(_u64)])
 _sig("lyth_sv_stats", _i32, [_vp, C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_u64)])
 _sig("lyth_sv_launches", _u64, [_vp])

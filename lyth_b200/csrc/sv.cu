@@ -264,6 +264,12 @@ struct lyth_sv {
     cudaStream_t stream = nullptr, comm_stream = nullptr;
     cudaStream_t copy_stream = nullptr;  // second copy-engine queue (the im halves of the pulls)
     cudaEvent_t ev_pull = nullptr, ev_copied = nullptr;
+    // Further copy-engine queues: a pull is cut into `pull_queues` pieces per component, issued
+    // round-robin over comm_stream, copy_stream and these (lyth_sv_set_pull_queues).
+    static constexpr int kExtraQueues = 6;
+    cudaStream_t xq[kExtraQueues] = {};
+    cudaEvent_t ev_xq[kExtraQueues] = {};
+    int pull_queues = 2;
     cudaEvent_t ev_recv[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_start = nullptr;
     cudaEvent_t ev_packed[2] = {nullptr, nullptr};
     ncclComm_t comm = nullptr;
@@ -718,18 +724,33 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
             // engines in flight
             if ((st = wait_own(sv, sv->comm_stream, partner, 0, b, seq))) return st;
             if ((st = status_of(cudaEventRecord(sv->ev_pull, sv->comm_stream)))) return st;
-            if ((st = status_of(cudaStreamWaitEvent(sv->copy_stream, sv->ev_pull, 0)))) return st;
+            // the queues: comm_stream, copy_stream, then the extra ones; Q pieces per component
+            const int Q = sv->pull_queues;
+            cudaStream_t qs[2 + lyth_sv::kExtraQueues] = {sv->comm_stream, sv->copy_stream};
+            for (int i = 0; i < lyth_sv::kExtraQueues; i++) qs[2 + i] = sv->xq[i];
+            for (int i = 1; i < Q; i++)
+                if ((st = status_of(cudaStreamWaitEvent(qs[i], sv->ev_pull, 0)))) return st;
+            const uint64_t piece = (C + (uint64_t)Q - 1) / (uint64_t)Q;
+            int next = 0;
             for (uint32_t y = 0; y < P; y++) {
                 const uint64_t off = (uint64_t)y * C, src = (uint64_t)myslice[y] * C;
-                if ((st = status_of(cudaMemcpyAsync(sv->rre[b] + off, sv->peer_sre[b][partner[y]] + src, C * sizeof(float),
-                                                    cudaMemcpyDeviceToDevice, sv->comm_stream))))
-                    return st;
-                if ((st = status_of(cudaMemcpyAsync(sv->rim[b] + off, sv->peer_sim[b][partner[y]] + src, C * sizeof(float),
-                                                    cudaMemcpyDeviceToDevice, sv->copy_stream))))
-                    return st;
+                for (int comp = 0; comp < 2; comp++) {
+                    float *dst = (comp ? sv->rim[b] : sv->rre[b]) + off;
+                    const float *from = (comp ? sv->peer_sim[b][partner[y]] : sv->peer_sre[b][partner[y]]) + src;
+                    for (uint64_t p0 = 0; p0 < C; p0 += piece) {
+                        const uint64_t len = C - p0 < piece ? C - p0 : piece;
+                        if ((st = status_of(cudaMemcpyAsync(dst + p0, from + p0, len * sizeof(float),
+                                                            cudaMemcpyDeviceToDevice, qs[next]))))
+                            return st;
+                        next = (next + 1) % Q;
+                    }
+                }
             }
-            if ((st = status_of(cudaEventRecord(sv->ev_copied, sv->copy_stream)))) return st;
-            if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_copied, 0)))) return st;
+            for (int i = 1; i < Q; i++) {
+                cudaEvent_t ev = i == 1 ? sv->ev_copied : sv->ev_xq[i - 2];
+                if ((st = status_of(cudaEventRecord(ev, qs[i])))) return st;
+                if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, ev, 0)))) return st;
+            }
             if ((st = put_peers(sv, sv->comm_stream, partner, kPulledAt, b, seq))) return st;
         } else {
             if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_packed[b], 0)))) return st;
@@ -1084,6 +1105,8 @@ void teardown_ce(lyth_sv *sv) {
     cudaStreamSynchronize(sv->stream);
     cudaStreamSynchronize(sv->comm_stream);
     cudaStreamSynchronize(sv->copy_stream);
+    for (int i = 0; i < lyth_sv::kExtraQueues; i++)
+        if (sv->xq[i]) cudaStreamSynchronize(sv->xq[i]);
     for (int b = 0; b < 2; b++)
         if (sv->slot_seq[b]) wait_own(sv, sv->stream, sv->slot_partners[b], kPulledAt, b, sv->slot_seq[b]);
     cudaStreamSynchronize(sv->stream);
@@ -1116,6 +1139,10 @@ void free_all(lyth_sv *sv) {
     if (sv->stream) cudaStreamDestroy(sv->stream);
     if (sv->comm_stream) cudaStreamDestroy(sv->comm_stream);
     if (sv->copy_stream) cudaStreamDestroy(sv->copy_stream);
+    for (int i = 0; i < lyth_sv::kExtraQueues; i++) {
+        if (sv->xq[i]) cudaStreamDestroy(sv->xq[i]);
+        if (sv->ev_xq[i]) cudaEventDestroy(sv->ev_xq[i]);
+    }
 }
 
 }  // namespace
@@ -1184,6 +1211,10 @@ int lyth_sv_create(lyth_sv **out, uint32_t qubits, int device, int rank, int nra
     if ((st = status_of(cudaStreamCreateWithPriority(&sv->copy_stream, cudaStreamNonBlocking, prio_hi)))) return fail(st);
     if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_pull, cudaEventDisableTiming)))) return fail(st);
     if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_copied, cudaEventDisableTiming)))) return fail(st);
+    for (int i = 0; i < lyth_sv::kExtraQueues; i++) {
+        if ((st = status_of(cudaStreamCreateWithPriority(&sv->xq[i], cudaStreamNonBlocking, prio_hi)))) return fail(st);
+        if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_xq[i], cudaEventDisableTiming)))) return fail(st);
+    }
     for (int b = 0; b < 2; b++) {
         if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_recv[b], cudaEventDisableTiming)))) return fail(st);
         if ((st = status_of(cudaEventCreateWithFlags(&sv->ev_done[b], cudaEventDisableTiming)))) return fail(st);
@@ -1438,6 +1469,20 @@ int lyth_sv_plan_clear(lyth_sv *sv) {
 }
 
 }  // extern "C"
+
+int lyth_sv_set_pull_queues(lyth_sv *sv, int queues) {
+    if (!sv) return LYTH_E_INVALID;
+    if (queues < 1 || queues > 2 + lyth_sv::kExtraQueues) return LYTH_E_UNSUPPORTED;
+    if (!sv->plan) {
+        DeviceGuard guard(sv);
+        int st = sync_stream(sv, sv->comm_stream);
+        if (!st && sv->copy_stream) st = sync_stream(sv, sv->copy_stream);
+        for (int i = 0; !st && i < lyth_sv::kExtraQueues; i++) st = sync_stream(sv, sv->xq[i]);
+        if (st) return st;
+    }
+    sv->pull_queues = queues;
+    return LYTH_OK;
+}
 
 int lyth_sv_set_deadline(lyth_sv *sv, double ms) {
     if (!sv) return LYTH_E_INVALID;

@@ -17,7 +17,7 @@ def _ngpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _worker(rank, nranks, q, case, nid, out_dir, remap=True, batch=6, ce=True, chunk=None):
+def _worker(rank, nranks, q, case, nid, out_dir, remap=True, batch=6, ce=True, chunk=None, queues=None):
     import sys
 
     sys.path.insert(0, ROOT)
@@ -38,6 +38,8 @@ def _worker(rank, nranks, q, case, nid, out_dir, remap=True, batch=6, ce=True, c
         sv.set_transport(ce)
         if chunk:
             sv.set_chunk(chunk)
+        if queues:
+            lb.check(lb.lib.lyth_sv_set_pull_queues(sv._h, queues), "set_pull_queues")
         transport = sv.transport
         sv.set_local(np.ascontiguousarray(re0[lo:hi]), np.ascontiguousarray(im0[lo:hi]))
         sv.apply(gates)
@@ -74,12 +76,13 @@ def case_gates(case, q):
     return "rank-bit gates", q, g
 
 
-def _run_ranks(nranks, q, case, remap, batch, tmp_path, ce=True, chunk=None):
+def _run_ranks(nranks, q, case, remap, batch, tmp_path, ce=True, chunk=None, queues=None):
     import lyth_b200 as lb
 
     nid = lb.unique_id()
     ctx = torch.multiprocessing.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, nranks, q, case, nid, str(tmp_path), remap, batch, ce, chunk))
+    procs = [ctx.Process(target=_worker, args=(r, nranks, q, case, nid, str(tmp_path), remap, batch, ce, chunk,
+                                               queues))
              for r in range(nranks)]
     for p in procs:
         p.start()
@@ -108,6 +111,14 @@ def test_two_ranks_many_chunks(case, ce, tmp_path):
     # 1024-amplitude chunks: every swap-in and exchange runs as a long pipeline, so both send and
     # receive slots are reused many times within one exchange (flags, events, slot waits)
     _run_ranks(2, 18, case, True, 6, tmp_path, ce=ce, chunk=1024)
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("queues", [1, 5, 8])
+def test_two_ranks_pull_queues(queues, tmp_path):
+    # a swap-in pull cut into pieces over 1, 5 or 8 copy-engine queues (and short chunks, so the
+    # pieces of consecutive chunks interleave on every queue)
+    _run_ranks(2, 18, 0, True, 6, tmp_path, chunk=4096, queues=queues)
 
 
 @pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
