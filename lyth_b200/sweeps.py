@@ -97,7 +97,8 @@ def grid_sweep(passes=5, reps=5) -> dict:
 
 
 def split_sweep(passes=5, reps=5) -> dict:
-    """ADR-0028: a 1-qubit gate (gate_q) over 2^23 amplitudes at every split width w = 2^q.
+    """ADR-0028: a 1-qubit gate (gate_q) over 2^27 amplitudes (1 GiB: 8x L2; the reference's 2^23
+    fit its 16 GB card's DRAM but sit in B200's 126 MiB L2) at every split width w = 2^q.
     Predictions: P1 the payload is width-independent (16 B per amplitude, by construction); the
     time is width-independent within 5 % (B200: every width takes the vectorised path except
     q = 0, 1, which pair inside a 16-byte vector)."""
@@ -106,7 +107,7 @@ def split_sweep(passes=5, reps=5) -> dict:
     import lyth_b200 as lb
     from lyth_b200 import circuit as cc
 
-    q_all = 23
+    q_all = 27
     n = 1 << q_all
     re = torch.rand(n, device="cuda")
     im = torch.rand(n, device="cuda")
@@ -122,7 +123,7 @@ def split_sweep(passes=5, reps=5) -> dict:
 
 
 def cu_sweep(passes=3, reps=5) -> dict:
-    """ADR-0029: cu_q over 2^23 amplitudes at every ordered pair of qubits {0,1,2,3,4,8,16,22},
+    """ADR-0029: cu_q over 2^27 amplitudes at every ordered pair of qubits {0,1,2,3,4,8,16,26},
     against a 1-qubit gate_q at the target as the control. Prediction: cu_q (in place, it moves
     only the control = 1 half: 8 B per amplitude) takes at most 1.10x the control's time x 0.5."""
     import torch
@@ -130,11 +131,11 @@ def cu_sweep(passes=3, reps=5) -> dict:
     import lyth_b200 as lb
     from lyth_b200 import circuit as cc
 
-    n = 1 << 23
+    n = 1 << 27
     re = torch.rand(n, device="cuda")
     im = torch.rand(n, device="cuda")
     m = cc.f32s(cc.zyz(0.3, 1.1, -0.7))
-    qs = [0, 1, 2, 3, 4, 8, 16, 22]
+    qs = [0, 1, 2, 3, 4, 8, 16, 26]
     pts = {}
     for c in qs:
         for t in qs:
@@ -153,15 +154,16 @@ def cu_sweep(passes=3, reps=5) -> dict:
 
 
 def fusion_sweep(passes=3, reps=3) -> dict:
-    """ADR-0030 Q2/Q3 on B200: Q2 -- a group of g gates on a fixed qubit set costs about one pass
-    whatever g (g = 1, 2, 5, 10, 20, 40 on sets A = {7,6,5,4,3} and B = {4,3,2,1,0}); Q3 -- the
-    23-qubit random circuit (depth 10) runs faster fused, at every fusion width 1..13."""
+    """ADR-0030 Q2/Q3 on B200, at 2^27 amplitudes (the reference's 2^23 is L2-resident here): Q2 --
+    a group of g gates on a fixed qubit set costs about one pass whatever g (g = 1, 2, 5, 10, 20, 40
+    on sets A = {7,6,5,4,3} and B = {4,3,2,1,0}); Q3 -- a 27-qubit random circuit (depth 10) runs
+    faster fused, at every fusion width 2..13."""
     import torch
 
     import lyth_b200 as lb
     from lyth_b200 import circuit as cc
 
-    q = 23
+    q = 27
     re = torch.rand(1 << q, device="cuda")
     im = torch.rand(1 << q, device="cuda")
     sets = {"A": [7, 6, 5, 4, 3], "B": [4, 3, 2, 1, 0]}
