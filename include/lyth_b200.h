@@ -694,6 +694,15 @@ int lyth_sv_set_fusion(lyth_sv *sv, int max_qubits);
  * then runs the gate as a local (fusable) pass; on = 0 exchanges the whole shard with the partner
  * rank and computes this rank's row of the gate. Both are bit-exact. */
 int lyth_sv_set_remap(lyth_sv *sv, int on);
+/* A diagonal gate (off-diagonal entries zero: phases, Z, S, T, controlled phases) whose target
+ * lives on a rank bit: on = 1 (default) moves no data -- on a shard whose rank bit is v the gate
+ * is the scalar u_vv, applied (under the gate's control where it has one) as the local gate
+ * diag(u_vv, u_vv) in the open fused group, and skipped where u_vv = 1. Every amplitude gets the
+ * value the full gate gives it; the chains differ only by products with the zero entries, so the
+ * sign of an amplitude that is exactly zero may differ from the evaluator's (a non-finite partner
+ * would also not turn it into NaN). on = 0 treats it like any other gate (swap-in or exchange)
+ * and is bit-identical with the evaluator in every case. Collective: every rank, same value. */
+int lyth_sv_set_diagonal(lyth_sv *sv, int on);
 /* With remap on: the most rank-bit qubits one swap-in brings in together (1..6, default 1 = one at
  * a time). Extra ones join only while each is needed before the local qubit it displaces; k of
  * them cost one exchange of (2^k - 1) / 2^k of the shard among 2^k ranks instead of k half-shard

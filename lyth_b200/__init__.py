@@ -120,6 +120,7 @@ _sig("lyth_sv_timing", _i32, [_vp, _i32, C.POINTER(_u64), C.POINTER(C.c_double)]
 _sig("lyth_sv_reset_timing", _i32, [_vp])
 _sig("lyth_sv_set_fusion", _i32, [_vp, _i32])
 _sig("lyth_sv_set_remap", _i32, [_vp, _i32])
+_sig("lyth_sv_set_diagonal", _i32, [_vp, _i32])
 _sig("lyth_sv_set_swap_batch", _i32, [_vp, _i32])
 _sig("lyth_sv_set_transport", _i32, [_vp, _i32])
 _sig("lyth_sv_transport", _i32, [_vp])

@@ -5,17 +5,18 @@
 //  * updates the state in place (one copy of 2^q amplitudes: 33 qubits is 64 GiB, which leaves
 //    room on a 180 GB part), with the same fma chains as the out-of-place kernels, so every
 //    amplitude is bit-identical to the reference's;
-//  * fuses consecutive local gates on at most 6 qubits into one pass (k_fused.cu), applying them
-//    in circuit order, bit-identical to the unfused passes (lyth-circuit fuse, lib.rs:72-100);
+//  * fuses consecutive local gates on at most 13 qubits into one pass (k_fused.cu), applying
+//    them in circuit order, bit-identical to the unfused passes (lyth-circuit fuse, lib.rs:72-100);
 //  * keeps a logical -> physical qubit map, so a SWAP moves no data: it relabels two qubits.
 //    The map is undone by real permutation passes only when the state is read out, which is
 //    exact because a swap is a permutation;
 //  * skips the control=0 half of a CU (it is a copy in the reference: identity in place);
 //  * shards 2^q amplitudes over 2^g ranks on the g highest physical bits: rank r holds physical
 //    indices [r * 2^L, (r+1) * 2^L), L = q - g. A gate on a local bit is a local (fusable) pass.
-//    A CU whose control is a rank bit runs (as a local U) only on the ranks whose bit is 1. A gate
-//    whose target is a rank bit first swaps that qubit into a local bit (the local qubit used
-//    furthest ahead leaves): half the shard is packed, moved to the partner and unpacked into
+//    A CU whose control is a rank bit runs (as a local U) only on the ranks whose bit is 1. A
+//    diagonal gate whose target is a rank bit is a scalar on each shard and moves no data. Any
+//    other gate whose target is a rank bit first swaps that qubit into a local bit (the local bit
+//    needed furthest ahead leaves): half the shard is packed, moved to the partner and unpacked into
 //    the positions it vacated, chunk by chunk, the move on the copy engines (cudaMemcpyAsync
 //    pulls through CUDA IPC mappings, ordered by sequence flags) or NCCL. With remap off the
 //    pair exchanges whole shards instead and each computes its own row of the gate as chunks
@@ -298,6 +299,10 @@ struct lyth_sv {
     // time by default: measured at 4 GPUs, a pairwise pull runs at 516 GB/s each way and a pull
     // from three partners at ~390 in aggregate, so single swaps win despite the larger volume.
     int swap_batch = 1;
+    // Diagonal gates on rank bits (lyth_sv_set_diagonal): 1 = no exchange -- on a shard whose
+    // rank bit is v the gate is the scalar u_vv (under its control, when it has one), applied as
+    // a local gate diag(u_vv, u_vv); 0 = swap-in or exchange like any other gate.
+    int diag = 1;
     // Copy-engine transport for swap-ins (multi-rank): every rank's send chunks and flag block
     // mapped through CUDA IPC; a rank pulls its partners' packed slices with cudaMemcpyAsync on
     // the copy engines. Flag block (kFlagWords u64): [r * 2 + b] = last chunk rank r packed for
@@ -440,6 +445,27 @@ void set_m(lyth_sv_op &op, const U8 &m) {
 
 // The rank bit b of this rank.
 inline int rank_bit(const lyth_sv *sv, uint32_t b) { return (sv->rank >> b) & 1; }
+
+// Off-diagonal entries all zero (either sign).
+inline bool is_diag(const U8 &m) { return m.br == 0.f && m.bi == 0.f && m.cr == 0.f && m.ci == 0.f; }
+
+// Row v of a diagonal gate as the local gate diag(u_vv, u_vv). Its fma chains give every
+// amplitude the value the full gate gives it (u_vv times the amplitude): the terms dropped are
+// products with the zero off-diagonal entries, which change no nonzero sum, only the sign an
+// exactly-zero result takes (and NaN from a non-finite partner).
+inline U8 scalar_row(const U8 &m, int v) {
+    const float r = v ? m.dr : m.ar, i = v ? m.di : m.ai;
+    return U8{r, i, 0.f, 0.f, 0.f, 0.f, r, i};
+}
+inline bool is_one(const U8 &s) { return s.ar == 1.f && s.ai == 0.f; }
+
+// A local bit to carry a scalar gate: one the open fused group already holds (so the group does
+// not widen), else bit 0 / 1; never `avoid` (the control of a controlled scalar).
+uint32_t carrier(const lyth_sv *sv, int avoid) {
+    for (int l = 0; l < sv->open.k; l++)
+        if ((int)sv->open.bits[l] != avoid) return sv->open.bits[l];
+    return avoid == 0 ? 1u : 0u;
+}
 
 // A gate whose target is rank bit b: chunked pairwise exchange, then this rank's row.
 int exchange_gate(lyth_sv *sv, uint32_t b, const U8 &m, int ctrl_bit) {
@@ -928,30 +954,38 @@ int swap_in(lyth_sv *sv, uint32_t gp, const lyth_gate *gates, uint64_t count, ui
     int st = flush_group(sv);
     if (st) return st;
     const uint32_t L = sv->local_bits;
+    // next[p] = the first gate from i on that needs physical bit p to be local: the target of a
+    // gate that is not a rank-bit-free diagonal. SWAPs move the labels, not the data, so the
+    // walk follows each bit's logical qubit through them; controls never need a local bit.
     std::vector<uint64_t> next(sv->qubits, UINT64_MAX);
+    std::vector<uint32_t> at = sv->pos;
     uint32_t seen = 0;
     for (uint64_t j = i; j < count && seen < sv->qubits; j++) {
         const lyth_gate &h = gates[j];
-        const uint32_t qs[2] = {h.q0, h.q1};
-        const int nq = h.kind == LYTH_GATE_U ? 1 : 2;
-        for (int e = 0; e < nq; e++)
-            if (qs[e] < sv->qubits && next[qs[e]] == UINT64_MAX) {
-                next[qs[e]] = j;
-                seen++;
-            }
+        if (h.q0 >= sv->qubits || (h.kind != LYTH_GATE_U && h.q1 >= sv->qubits)) break;
+        if (h.kind == LYTH_GATE_SWAP) {
+            std::swap(at[h.q0], at[h.q1]);
+            continue;
+        }
+        if (sv->diag && is_diag(u8_of(h.m))) continue;
+        const uint32_t p = at[h.kind == LYTH_GATE_U ? h.q0 : h.q1];
+        if (next[p] == UINT64_MAX) {
+            next[p] = j;
+            seen++;
+        }
     }
     // local bits by next use, furthest first (ties: highest bit)
     std::vector<uint32_t> loc(L);
     for (uint32_t b = 0; b < L; b++) loc[b] = L - 1 - b;
-    std::stable_sort(loc.begin(), loc.end(), [&](uint32_t x, uint32_t y) { return next[sv->inv[x]] > next[sv->inv[y]]; });
+    std::stable_sort(loc.begin(), loc.end(), [&](uint32_t x, uint32_t y) { return next[x] > next[y]; });
     // the other rank bits by next use, soonest first
     std::vector<uint32_t> glob;
     for (uint32_t b = L; b < sv->qubits; b++)
         if (b != gp) glob.push_back(b);
-    std::stable_sort(glob.begin(), glob.end(), [&](uint32_t x, uint32_t y) { return next[sv->inv[x]] < next[sv->inv[y]]; });
+    std::stable_sort(glob.begin(), glob.end(), [&](uint32_t x, uint32_t y) { return next[x] < next[y]; });
     std::vector<uint32_t> V{loc[0]}, G{gp};
     for (uint32_t j = 0; j < glob.size() && (int)V.size() < sv->swap_batch && V.size() < L; j++) {
-        if (next[sv->inv[glob[j]]] < next[sv->inv[loc[V.size()]]]) {
+        if (next[glob[j]] < next[loc[V.size()]]) {
             V.push_back(loc[V.size()]);
             G.push_back(glob[j]);
         } else {
@@ -976,6 +1010,10 @@ int apply_one(lyth_sv *sv, const lyth_gate *gates, uint64_t count, uint64_t i) {
         }
         case LYTH_GATE_U: {
             uint32_t p = sv->pos[g.q0];
+            if (p >= L && sv->diag && is_diag(m)) {  // this shard's row: a scalar, no exchange
+                const U8 s = scalar_row(m, rank_bit(sv, p - L));
+                return is_one(s) ? LYTH_OK : add_local(sv, -1, carrier(sv, -1), s);
+            }
             if (p >= L && sv->remap) {
                 int st = swap_in(sv, p, gates, count, i);
                 if (st) return st;
@@ -987,7 +1025,8 @@ int apply_one(lyth_sv *sv, const lyth_gate *gates, uint64_t count, uint64_t i) {
             return exchange_gate(sv, p - L, m, -1);
         }
         case LYTH_GATE_CU: {
-            if (sv->pos[g.q1] >= L && sv->remap) {
+            const bool diag = sv->diag && is_diag(m);
+            if (sv->pos[g.q1] >= L && sv->remap && !diag) {
                 int st = swap_in(sv, sv->pos[g.q1], gates, count, i);
                 if (st) return st;
             }
@@ -995,6 +1034,12 @@ int apply_one(lyth_sv *sv, const lyth_gate *gates, uint64_t count, uint64_t i) {
             if (pc < L && pt < L) return add_local(sv, (int)pc, pt, m);
             if (pc >= L && !rank_bit(sv, pc - L)) return LYTH_OK;  // control 0 on this whole shard
             if (pt < L) return add_local(sv, -1, pt, m);
+            if (diag) {  // diagonal on a rank-bit target: this shard's row is a scalar
+                const U8 s = scalar_row(m, rank_bit(sv, pt - L));
+                if (is_one(s)) return LYTH_OK;
+                if (pc >= L) return add_local(sv, -1, carrier(sv, -1), s);  // control 1 here
+                return add_local(sv, (int)pc, carrier(sv, (int)pc), s);      // under the local control
+            }
             int st = flush_group(sv);
             if (st) return st;
             return exchange_gate(sv, pt - L, m, pc < L ? (int)pc : -1);
@@ -1376,6 +1421,12 @@ int lyth_sv_set_swap_batch(lyth_sv *sv, int max_qubits) {
 int lyth_sv_set_remap(lyth_sv *sv, int on) {
     if (!sv) return LYTH_E_INVALID;
     sv->remap = on != 0;
+    return LYTH_OK;
+}
+
+int lyth_sv_set_diagonal(lyth_sv *sv, int on) {
+    if (!sv) return LYTH_E_INVALID;
+    sv->diag = on != 0;
     return LYTH_OK;
 }
 

@@ -114,6 +114,12 @@ class StateVector:
         whole shard and compute this rank's row (False)."""
         check(lib.lyth_sv_set_remap(self._h, int(on)), "set_remap")
 
+    def set_diagonal(self, on: bool) -> None:
+        """Diagonal gates on rank-bit targets: no exchange, each shard applies its row's scalar
+        (True, default; equal in value, the sign of an exactly-zero amplitude may differ) or like
+        any other gate (False; bit-identical in every case). Collective."""
+        check(lib.lyth_sv_set_diagonal(self._h, int(on)), "set_diagonal")
+
     def set_swap_batch(self, max_qubits: int) -> None:
         """Most rank-bit qubits one swap-in brings in together (default 1 = one at a time)."""
         check(lib.lyth_sv_set_swap_batch(self._h, max_qubits), "set_swap_batch")
@@ -192,6 +198,9 @@ class Plan:
 
     def set_remap(self, on: bool) -> None:
         check(lib.lyth_sv_set_remap(self._h, int(on)), "set_remap")
+
+    def set_diagonal(self, on: bool) -> None:
+        check(lib.lyth_sv_set_diagonal(self._h, int(on)), "set_diagonal")
 
     def set_swap_batch(self, max_qubits: int) -> None:
         check(lib.lyth_sv_set_swap_batch(self._h, max_qubits), "set_swap_batch")

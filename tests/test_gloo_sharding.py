@@ -197,30 +197,46 @@ def _worker(rank, nranks, q, port, out_dir):
         L = (1 << q) // nranks
         local_bits = L.bit_length() - 1
         lo, hi = rank * L, (rank + 1) * L
-        for ci, (name, gates) in enumerate(circuits(q)):
+        cases = [(name, gates, False) for name, gates in circuits(q)]
+        cases.append(("layered, zeros", circuits(q)[0][1], True))
+        for ci, (name, gates, zeros) in enumerate(cases):
             re0, im0 = orc.random_state(400 + ci, q)
+            if zeros:  # a third of the components exactly +0 or -0
+                rng = np.random.default_rng(ci)
+                for a in (re0, im0):
+                    hit = rng.random(a.size) < 1 / 3
+                    a[hit] = np.where(rng.random(hit.sum()) < 0.5, np.float32(0.0), np.float32(-0.0))
             want_r, want_i = orc.run_gates(as_tuples(gates), re0, im0)
-            for fuse, remap, batch in ((6, True, 6), (6, True, 1), (3, True, 6), (1, True, 6), (6, False, 6),
-                                       (1, False, 6)):
-                if True:
-                    with Plan(q, rank, nranks) as p:
-                        p.set_fusion(fuse)
-                        p.set_remap(remap)
-                        p.set_swap_batch(batch)
-                        p.apply(gates)
-                        p.finish()
-                        ops, st = p.ops(), p.stats()
-                    comm = [(o["kind"], o["a"], o["b"], p) for o in ops if o["kind"] in COMM
-                            for p in partners_of(o, rank)]
-                    seqs = [None] * nranks
-                    dist.all_gather_object(seqs, comm)
-                    same = pairs_agree(seqs)
-                    re, im = replay(ops, rank, local_bits, np.ascontiguousarray(re0[lo:hi]),
-                                    np.ascontiguousarray(im0[lo:hi]))
-                    ok = np.array_equal(re.view(np.uint32), want_r[lo:hi].view(np.uint32)) and \
-                        np.array_equal(im.view(np.uint32), want_i[lo:hi].view(np.uint32))
-                    nmulti = sum(o["kind"] == "swap_multi" for o in ops)
-                    lines.append(f"{name}|{fuse}|{int(remap)}/{batch}|{int(ok)}|{int(same)}|{len(comm)}|{nmulti}")
+            for fuse, remap, batch, diag in ((6, True, 6, True), (6, True, 1, True), (3, True, 6, True),
+                                             (1, True, 6, True), (6, False, 6, True), (1, False, 6, True),
+                                             (6, True, 1, False), (6, False, 6, False)):
+                with Plan(q, rank, nranks) as p:
+                    p.set_fusion(fuse)
+                    p.set_remap(remap)
+                    p.set_swap_batch(batch)
+                    p.set_diagonal(diag)
+                    p.apply(gates)
+                    p.finish()
+                    ops, st = p.ops(), p.stats()
+                comm = [(o["kind"], o["a"], o["b"], p) for o in ops if o["kind"] in COMM
+                        for p in partners_of(o, rank)]
+                seqs = [None] * nranks
+                dist.all_gather_object(seqs, comm)
+                same = pairs_agree(seqs)
+                re, im = replay(ops, rank, local_bits, np.ascontiguousarray(re0[lo:hi]),
+                                np.ascontiguousarray(im0[lo:hi]))
+                wr, wi = want_r[lo:hi], want_i[lo:hi]
+                bits = np.array_equal(re.view(np.uint32), wr.view(np.uint32)) and \
+                    np.array_equal(im.view(np.uint32), wi.view(np.uint32))
+                # Rank-bit diagonals as scalars: equal in value, and bit for bit wherever the
+                # result is not an exact zero (whose sign may differ); bit for bit otherwise.
+                value = np.array_equal(re, wr) and np.array_equal(im, wi) and \
+                    np.array_equal(re.view(np.uint32)[wr != 0], wr.view(np.uint32)[wr != 0]) and \
+                    np.array_equal(im.view(np.uint32)[wi != 0], wi.view(np.uint32)[wi != 0])
+                ok = value if (diag and zeros) else bits
+                nmulti = sum(o["kind"] == "swap_multi" for o in ops)
+                lines.append(f"{name}|{fuse}|{int(remap)}/{batch}/{int(diag)}|{int(ok)}|{int(same)}|{len(comm)}|"
+                             f"{nmulti}")
     finally:
         dist.destroy_process_group()
     with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
@@ -244,8 +260,8 @@ def test_sharded_plan_replays_bit_exact(nranks, q, tmp_path):
     for r in range(nranks):
         for line in open(tmp_path / f"r{r}.txt").read().splitlines():
             name, fuse, remap, ok, same, ncomm, nmulti = line.split("|")
-            assert ok == "1", f"rank {r}: {name} fuse={fuse} remap/batch={remap}: shard differs"
-            assert same == "1", f"{name} fuse={fuse} remap/batch={remap}: a pair of ranks disagree on their steps"
+            assert ok == "1", f"rank {r}: {name} fuse={fuse} remap/batch/diag={remap}: shard differs"
+            assert same == "1", f"{name} fuse={fuse} remap/batch/diag={remap}: a pair of ranks disagree on their steps"
             total_comm += int(ncomm)
             total_multi += int(nmulti)
     assert total_comm > 0
@@ -349,3 +365,34 @@ def test_stream_ranges_cover_once(world, tmp_path):
             assert off == pos and cnt >= 0 and off % 1024 == 0
             pos += cnt
         assert pos == n
+
+
+def test_diagonal_rank_gates_move_no_data():
+    # A diagonal gate on a rank-bit target (a phase, a controlled phase) is a scalar on each shard:
+    # no swap-in, no exchange. On the benchmark circuit at 8 ranks only the H gates on the three
+    # rank-bit qubits move data: three single swap-ins per layer, one batched one.
+    from lyth_b200 import circuit as cc
+    from lyth_b200.statevector import Plan
+
+    layers = 6
+    gates = cc.layered(33, layers, cc.Rng(cc.BENCH_SEED))
+    counts = {}
+    for diag in (True, False):
+        for batch in (1, 3):
+            with Plan(33, 5, 8) as p:
+                p.set_diagonal(diag)
+                p.set_swap_batch(batch)
+                p.apply(gates)
+                ops = p.ops()
+            counts[diag, batch] = sum(o["kind"] in COMM for o in ops)
+    assert counts[True, 1] == 3 * layers
+    assert counts[True, 3] == layers
+    assert counts[False, 1] > counts[True, 1] and counts[False, 3] > counts[True, 3]
+    t = 32  # a rank bit at 8 ranks, before any swap
+    for g in ([cc.U(t, cc.phase(0.3))], [cc.CU(0, t, cc.phase(0.3))], [cc.CU(t - 1, t, cc.phase(0.3))],
+              [cc.U(t, cc.Z)]):
+        for rank in range(8):
+            with Plan(33, rank, 8) as p:
+                p.apply(g)
+                ops = p.ops()
+            assert not any(o["kind"] in COMM for o in ops), (g, rank, ops)
