@@ -107,13 +107,16 @@ def args_():
     ap.add_argument("--ref-gates", type=int, default=1, help="gates per reference-arm step")
     ap.add_argument("--parity-qubits", type=int, default=22)
     ap.add_argument("--skip-parity", action="store_true")
-    ap.add_argument("--fuse", type=int, default=None, help="max qubits per fused pass (1..6; default: the engine's)")
+    ap.add_argument("--fuse", type=int, default=None, help="max qubits per fused pass (1..13; default: the engine's)")
     ap.add_argument("--swap-batch", type=int, default=None,
                     help="most rank-bit qubits per swap-in (1..6; default: the engine's)")
     ap.add_argument("--transport", choices=["copy_engine", "nccl"], default=None,
                     help="swap-in transport at N > 1 (default: the engine's)")
     ap.add_argument("--pull-queues", type=int, default=None,
                     help="copy-engine queues per swap-in pull at N > 1 (1..8; default: the engine's)")
+    ap.add_argument("--diagonal", type=int, choices=[0, 1], default=None,
+                    help="diagonal rank-bit gates without an exchange (1) or like any other gate (0); "
+                         "default: the engine's")
     ap.add_argument("--case", default=None, help="run one kernel case (small config) and exit")
     ap.add_argument("--case-reps", type=int, default=3)
     ap.add_argument("--list-cases", action="store_true")
@@ -666,11 +669,28 @@ def sharded_streams(dist: Dist, peak: float, log2n: int = 33, reps: int = 5) -> 
 
 
 # --------------------------------------------------------------------------- parity before timing
+def configure(sv, a, dist: Dist) -> None:
+    """The engine settings of the command line (collective ones on every rank alike)."""
+    import lyth_b200 as lb
+
+    if a.fuse:
+        sv.set_fusion(a.fuse)
+    if a.swap_batch:
+        sv.set_swap_batch(a.swap_batch)
+    if a.diagonal is not None:
+        sv.set_diagonal(bool(a.diagonal))
+    if a.transport and dist.world > 1:
+        sv.set_transport(a.transport == "copy_engine")
+    if a.pull_queues and dist.world > 1:
+        lb.check(lb.lib.lyth_sv_set_pull_queues(sv._h, a.pull_queues), "set_pull_queues")
+
+
 def sharded_parity(a, dist: Dist) -> dict:
     """Bit-exactness on the same N ranks, before anything is timed: a `--parity-qubits` (default 22)
-    state sharded over the N ranks exactly as the timed run shards its state, two layers of the
-    layered circuit through the engine (fused staged passes, swap-ins of rank-bit qubits, SWAPs as
-    relabels, read-out undoing the qubit map), and every rank's shard compared bit for bit with the
+    state sharded over the N ranks exactly as the timed run shards its state, with the timed run's
+    engine settings, two layers of the layered circuit through the engine (tile passes, swap-ins of
+    rank-bit qubits, diagonal rank-bit gates as scalars, SWAPs as relabels, read-out undoing the
+    qubit map), and every rank's shard compared bit for bit with the
     host evaluator applying the same gates unfused in order to the same input
     (crates/lyth-circuit/tests/fusion.rs:53-92). Every rank takes the same collective steps
     whatever happens locally; `ok` is the minimum over ranks."""
@@ -690,6 +710,7 @@ def sharded_parity(a, dist: Dist) -> dict:
         orc.set_threads(max(1, (os.cpu_count() or 1) // dist.world))
         wr, wi = orc.run_gates(cc.as_tuples(gates), re0.copy(), im0.copy(), inplace=True)
         with lb.StateVector(q, device=dist.local, rank=dist.rank, nranks=dist.world, nccl_id=nid) as sv:
+            configure(sv, a, dist)
             n = sv.local_len
             lo = dist.rank * n
             sv.set_local(np.ascontiguousarray(re0[lo:lo + n]), np.ascontiguousarray(im0[lo:lo + n]))
@@ -733,14 +754,7 @@ def ours(a, dist: Dist) -> None:
     nid = lb.unique_id() if (dist.world > 1 and dist.rank == 0) else None
     nid = dist.bcast_bytes(nid)
     sv = lb.StateVector(q, device=dist.local, rank=dist.rank, nranks=dist.world, nccl_id=nid)
-    if a.fuse:
-        sv.set_fusion(a.fuse)
-    if a.swap_batch:
-        sv.set_swap_batch(a.swap_batch)
-    if a.transport and dist.world > 1:
-        sv.set_transport(a.transport == "copy_engine")
-    if a.pull_queues and dist.world > 1:
-        lb.check(lb.lib.lyth_sv_set_pull_queues(sv._h, a.pull_queues), "set_pull_queues")
+    configure(sv, a, dist)
     total_layers = a.warmup + a.steps
     gates = cc.layered(q, total_layers, cc.Rng(cc.BENCH_SEED))
     per = len(gates) // total_layers
@@ -775,6 +789,7 @@ def ours(a, dist: Dist) -> None:
     tim = sv.timing()
     launches = dist.sum(float(sv.stats()["launches"] - launches0))
     st = sv.stats()
+    sv_transport = sv.transport() == "copy_engine"
     gates_timed = a.steps * per
     value = gates_timed / (ms * 1e-3)
 
@@ -872,7 +887,11 @@ def ours(a, dist: Dist) -> None:
             "gpu_launches": int(launches),
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"]},
-            "engine": {"passes": st["passes"], "exchanges": st["exchanges"], "bytes_sent": st["bytes_sent"]},
+            "engine": {"passes": st["passes"], "exchanges": st["exchanges"], "bytes_sent": st["bytes_sent"],
+                       "settings": {"fusion": a.fuse or 13, "swap_batch": a.swap_batch or 1,
+                                    "diagonal_rank_gates": "no exchange" if a.diagonal in (None, 1) else "exchange",
+                                    "transport": ("copy_engine" if sv_transport else "nccl") if dist.world > 1
+                                    else None, "pull_queues": (a.pull_queues or 2) if dist.world > 1 else None}},
             "parity": parity,
         }
         if cpu:
