@@ -479,10 +479,11 @@ def kernel_cases(dev, small: bool = False):
     gemv_case("gemv_int4_4096x14336", lb.GEMV_INT4)
     gemv_case("gemv_nf4_4096x14336", lb.GEMV_NF4)
 
-    def mm_case(name, fn, m):
+    def mm_case(name, fn, m, dtype=torch.float32):
+        # operands made (and rounded to the storage type) in setup: only the contraction is timed
         def setup():
-            A = torch.randn(m, m, device=dev, generator=g) / 64.0
-            B = torch.randn(m, m, device=dev, generator=g) / 64.0
+            A = (torch.randn(m, m, device=dev, generator=g) / 64.0).to(dtype)
+            B = (torch.randn(m, m, device=dev, generator=g) / 64.0).to(dtype)
             C = torch.empty(m, m, device=dev)
             return (lambda: fn(A, B, C)), 2.0 * m ** 3, "flops"
         cases[name] = setup
@@ -490,7 +491,8 @@ def kernel_cases(dev, small: bool = False):
     M = 2048 if small else 4096
     mm_case(f"matmul_f32_ffma_{M}", lambda A, B, C: lb.matmul_f32(A, B, C, exact=False), M)
     mm_case(f"matmul_f32_exact_{M}", lambda A, B, C: lb.matmul_f32(A, B, C, exact=True), M)
-    mm_case(f"matmul_bf16_{M}", lambda A, B, C: lb.matmul_bf16(A.bfloat16(), B.bfloat16(), C), M)
+    mm_case(f"matmul_bf16_{M}", lambda A, B, C: lb.matmul_bf16(A, B, C), M, torch.bfloat16)
+    mm_case(f"matmul_bf16_1sm_{M}", lambda A, B, C: lb.matmul_bf16(A, B, C, pair=False), M, torch.bfloat16)
 
     def gate_case(name, q, fn):
         def setup():

@@ -428,11 +428,16 @@ int lyth_b200_matmul_f32(uint32_t m, uint32_t n, uint32_t k, const float *a, con
                          int exact, cudaStream_t stream);
 /* bf16 inputs (raw bfloat16 bits), f32 accumulate and output, on the tcgen05 tensor cores with
  * TMEM accumulators. m a multiple of 128, n of 256 and k of 64 (16-byte aligned buffers) take the
- * tensor-core path; other shapes return LYTH_E_UNSUPPORTED. No reference kernel: the reference
- * never uses tensor cores. Compared with eval_contraction on the bf16-rounded inputs within 1e-2
- * relative. */
+ * tensor-core path; other shapes return LYTH_E_UNSUPPORTED. m a multiple of 256 runs on CTA pairs
+ * (tcgen05.mma.cta_group::2, 256 x 256 tiles, each SM staging half of each operand), other m on
+ * single SMs (128 x 256 tiles). No reference kernel: the reference never uses tensor cores.
+ * Compared with eval_contraction on the bf16-rounded inputs within 1e-2 relative. */
 int lyth_b200_matmul_bf16(uint32_t m, uint32_t n, uint32_t k, const uint16_t *a, const uint16_t *b,
                           float *c, cudaStream_t stream);
+/* The same with the form chosen: pair = 1 the CTA-pair kernel (m a multiple of 256, else
+ * LYTH_E_UNSUPPORTED), pair = 0 the single-SM kernel. For tests and measurements of both. */
+int lyth_b200_matmul_bf16_form(int pair, uint32_t m, uint32_t n, uint32_t k, const uint16_t *a,
+                               const uint16_t *b, float *c, cudaStream_t stream);
 /* LYTH_E_TIMEOUT when a bounded device-side wait of any kernel in this library ran out since the
  * last call (the flag is then cleared), else LYTH_OK. Synchronises with the current device. */
 int lyth_b200_device_error(void);

@@ -92,6 +92,7 @@ _sig("lyth_b200_reduce_workspace_bytes", C.c_size_t, [_u64])
 _sig("lyth_b200_reduce", _i32, [_i32, _u64, _vp, _vp, _vp, _vp, C.c_size_t, _vp])
 _sig("lyth_b200_matmul_f32", _i32, [_u32, _u32, _u32, _vp, _vp, _vp, _i32, _vp])
 _sig("lyth_b200_matmul_bf16", _i32, [_u32, _u32, _u32, _vp, _vp, _vp, _vp])
+_sig("lyth_b200_matmul_bf16_form", _i32, [_i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp])
 _sig("lyth_b200_gemv_q4", _i32, [_i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp])
 _sig("lyth_b200_gemv_dequant", _i32, [_i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp])
 _sig("lyth_b200_nf4_codebook", None, [C.POINTER(_f32)])
@@ -327,16 +328,21 @@ def matmul_f32(a, b, c, exact: bool = False, stream=None) -> None:
                                    int(exact), _stream(stream)), "matmul_f32")
 
 
-def matmul_bf16(a, b, c, stream=None) -> None:
-    """bf16 a (m x k), b (k x n), f32 c on the tcgen05 tensor cores."""
+def matmul_bf16(a, b, c, stream=None, pair: bool | None = None) -> None:
+    """bf16 a (m x k), b (k x n), f32 c on the tcgen05 tensor cores. pair: None = the library's
+    choice (CTA pairs when m is a multiple of 256), True / False = that form."""
     import torch
 
     m, k = a.shape
     k2, n = b.shape
     if k2 != k or tuple(c.shape) != (m, n):
         raise ValueError(f"matmul shapes {tuple(a.shape)} x {tuple(b.shape)} -> {tuple(c.shape)}")
-    check(lib.lyth_b200_matmul_bf16(m, n, k, _ptr(a, torch.bfloat16, "a"), _ptr(b, torch.bfloat16, "b"),
-                                    _ptr(c, _f32t(), "c"), _stream(stream)), "matmul_bf16")
+    args = (m, n, k, _ptr(a, torch.bfloat16, "a"), _ptr(b, torch.bfloat16, "b"), _ptr(c, _f32t(), "c"),
+            _stream(stream))
+    if pair is None:
+        check(lib.lyth_b200_matmul_bf16(*args), "matmul_bf16")
+    else:
+        check(lib.lyth_b200_matmul_bf16_form(int(pair), *args), "matmul_bf16")
 
 
 # ----------------------------------------------------------------------------- GEMV

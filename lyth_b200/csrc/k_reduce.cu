@@ -93,21 +93,90 @@ LYTH_D float block_partial(uint64_t n, const void *x, const void *y, uint64_t gr
     return v;  // valid in thread 0
 }
 
-template <int OP, bool DOT, typename I>
-__global__ void __launch_bounds__(kRedBlock) reduce_partials_kernel(I n, const float *x, const float *y,
-                                                                    float *partial) {
-    __shared__ float slots[kRedBlock];
-    const float v = block_partial<OP, DOT>((uint64_t)n, x, y, gridDim.x, slots);
-    if (threadIdx.x == 0) partial[blockIdx.x] = v;
+// The B200 surface's partials: the same reference blocks, each still folded and tree-reduced by
+// 256 threads in the reference's order, but a persistent grid walks them (block b takes reference
+// blocks b, b + gridDim.x, ...) and issues the loads of its next reference block before the tree
+// of the current one. One CUDA block per reference block leaves too few bytes in flight per SM
+// when the reference block is small (2048 elements: 8 KiB of f32, 4 KiB of bf16), and the tree's
+// barriers then stall the loads; here a block always has its next block's loads outstanding.
+template <int OP, bool DOT, int TY>
+__global__ void __launch_bounds__(kRedBlock) partials_persistent_kernel(uint64_t n, const void *x, const void *y,
+                                                                        uint64_t grid, float *partial) {
+    __shared__ float slots[2][kRedBlock];
+    const unsigned t = threadIdx.x;
+    const uint64_t stride = grid * kRedBlock;
+    const uint64_t span = (uint64_t)kRedPerThread * stride;
+    float cx[kRedPerThread], cy[kRedPerThread], nx[kRedPerThread], ny[kRedPerThread];
+    auto fetch = [&](uint64_t rb, float *vx, float *vy) {
+        const uint64_t i = rb * kRedBlock + t;
+#pragma unroll
+        for (int u = 0; u < kRedPerThread; u++) {
+            const uint64_t j = i + (uint64_t)u * stride;
+            vx[u] = j < n ? load_el<TY>(x, j) : 0.0f;
+            if (DOT) vy[u] = j < n ? load_el<TY>(y, j) : 0.0f;
+        }
+    };
+    uint64_t rb = blockIdx.x;
+    if (rb < grid) fetch(rb, cx, cy);
+    for (int p = 0; rb < grid; rb += gridDim.x, p ^= 1) {
+        const uint64_t rn = rb + gridDim.x;
+        if (rn < grid) fetch(rn, nx, ny);
+        float acc = identity_of<OP>();
+        uint64_t i = rb * kRedBlock + t;
+#pragma unroll
+        for (int u = 0; u < kRedPerThread; u++)
+            if (i + (uint64_t)u * stride < n) acc = combine<OP>(acc, DOT ? __fmul_rn(cx[u], cy[u]) : cx[u]);
+        for (i += span; i < n; i += span) {  // inputs longer than 8 * 256 * grid (grid capped at 2^20)
+            float v[kRedPerThread];
+#pragma unroll
+            for (int u = 0; u < kRedPerThread; u++) {
+                const uint64_t j = i + (uint64_t)u * stride;
+                if (j < n) v[u] = DOT ? __fmul_rn(load_el<TY>(x, j), load_el<TY>(y, j)) : load_el<TY>(x, j);
+            }
+#pragma unroll
+            for (int u = 0; u < kRedPerThread; u++)
+                if (i + (uint64_t)u * stride < n) acc = combine<OP>(acc, v[u]);
+        }
+        // The tree, on this iteration's half of the double-buffered slots (the other half may
+        // still be read by warp 0 of the previous iteration until the first barrier below).
+        float *sl = slots[p];
+        sl[t] = acc;
+        __syncthreads();
+        if (t < 128) sl[t] = combine<OP>(sl[t], sl[t + 128]);
+        __syncthreads();
+        if (t < 64) sl[t] = combine<OP>(sl[t], sl[t + 64]);
+        __syncthreads();
+        if (t < 32) {
+            float v = combine<OP>(sl[t], sl[t + 32]);
+#pragma unroll
+            for (int s = 16; s > 0; s >>= 1) v = combine<OP>(v, __shfl_down_sync(0xffffffffu, v, s));
+            if (t == 0) partial[rb] = v;
+        }
+#pragma unroll
+        for (int u = 0; u < kRedPerThread; u++) {
+            cx[u] = nx[u];
+            if (DOT) cy[u] = ny[u];
+        }
+    }
 }
 
-// Narrow storage (f16 / bf16 inputs, f32 partials): the same order, each element widened exactly.
+// Blocks of the persistent grid: as many as fit on the device at once, at most one per
+// reference block.
 template <int OP, bool DOT, int TY>
-__global__ void __launch_bounds__(kRedBlock) reduce_partials_narrow_kernel(uint64_t n, const uint16_t *x,
-                                                                           const uint16_t *y, float *partial) {
-    __shared__ float slots[kRedBlock];
-    const float v = block_partial<OP, DOT, TY>(n, x, y, gridDim.x, slots);
-    if (threadIdx.x == 0) partial[blockIdx.x] = v;
+int launch_persistent(uint64_t n, const void *x, const void *y, uint32_t grid, float *partial, cudaStream_t s) {
+    static int per_sm = 0;
+    if (per_sm == 0) {
+        int b = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, partials_persistent_kernel<OP, DOT, TY>, kRedBlock, 0) !=
+                cudaSuccess ||
+            b < 1)
+            b = 1;
+        per_sm = b;
+    }
+    const uint64_t cap = (uint64_t)device_sms() * per_sm;
+    const unsigned blocks = (unsigned)(grid < cap ? grid : cap);
+    partials_persistent_kernel<OP, DOT, TY><<<blocks, kRedBlock, 0, s>>>(n, x, y, grid, partial);
+    return last_launch_status();
 }
 
 // The ADR-0016 kernels, in the reference's parameter order.
@@ -198,33 +267,27 @@ extern "C" uint32_t lyth_b200_reduce_grid(uint64_t n) {
 }
 
 template <int TY>
-static int launch_partials_narrow(int op, uint64_t n, const uint16_t *x, const uint16_t *y, uint32_t grid,
-                                  float *partial, cudaStream_t s) {
-    if (op == 0 && y) reduce_partials_narrow_kernel<0, true, TY><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
-    else if (op == 0) reduce_partials_narrow_kernel<0, false, TY><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
-    else if (op == 1 && !y) reduce_partials_narrow_kernel<1, false, TY><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
-    else if (op == 2 && !y) reduce_partials_narrow_kernel<2, false, TY><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
-    else return LYTH_E_UNSUPPORTED;
-    return last_launch_status();
+static int launch_partials(int op, uint64_t n, const void *x, const void *y, uint32_t grid, float *partial,
+                           cudaStream_t s) {
+    if (op == 0 && y) return launch_persistent<0, true, TY>(n, x, y, grid, partial, s);
+    if (op == 0) return launch_persistent<0, false, TY>(n, x, y, grid, partial, s);
+    if (op == 1 && !y) return launch_persistent<1, false, TY>(n, x, y, grid, partial, s);
+    if (op == 2 && !y) return launch_persistent<2, false, TY>(n, x, y, grid, partial, s);
+    return LYTH_E_UNSUPPORTED;
 }
 
 extern "C" int lyth_b200_reduce_partials_narrow(int op, int ty, uint64_t n, const uint16_t *x, const uint16_t *y,
                                                 uint32_t grid, float *partial, cudaStream_t s) {
     if (!x || !partial || grid == 0) return LYTH_E_INVALID;
-    if (ty == LYTH_NARROW_F16) return launch_partials_narrow<1>(op, n, x, y, grid, partial, s);
-    if (ty == LYTH_NARROW_BF16) return launch_partials_narrow<2>(op, n, x, y, grid, partial, s);
+    if (ty == LYTH_NARROW_F16) return launch_partials<1>(op, n, x, y, grid, partial, s);
+    if (ty == LYTH_NARROW_BF16) return launch_partials<2>(op, n, x, y, grid, partial, s);
     return LYTH_E_UNSUPPORTED;
 }
 
 extern "C" int lyth_b200_reduce_partials(int op, uint64_t n, const float *x, const float *y, uint32_t grid,
                                          float *partial, cudaStream_t s) {
     if (!x || !partial || grid == 0) return LYTH_E_INVALID;
-    if (op == 0 && y) reduce_partials_kernel<0, true, uint64_t><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
-    else if (op == 0) reduce_partials_kernel<0, false, uint64_t><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
-    else if (op == 1 && !y) reduce_partials_kernel<1, false, uint64_t><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
-    else if (op == 2 && !y) reduce_partials_kernel<2, false, uint64_t><<<grid, kRedBlock, 0, s>>>(n, x, y, partial);
-    else return LYTH_E_UNSUPPORTED;
-    return last_launch_status();
+    return launch_partials<0>(op, n, x, y, grid, partial, s);
 }
 
 extern "C" size_t lyth_b200_reduce_workspace_bytes(uint64_t n) {

@@ -68,6 +68,53 @@ LYTH_D bool flag_wait_bounded(const uint64_t *flag, uint64_t target, uint64_t ns
     }
 }
 
+// Cluster-scope forms, for CTA pairs that share barriers (the 2-SM tensor-core contraction).
+// The address of this CTA's shared-memory word `addr` in the shared memory of cluster CTA `rank`.
+LYTH_D uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+LYTH_D uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// All threads of every CTA of the cluster (warp-aligned).
+LYTH_D void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive (and expect `bytes`) on a barrier given by its shared::cluster address.
+LYTH_D void mbar_expect_tx_cluster(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+LYTH_D void mbar_arrive_cluster(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// mbar_wait_limited with cluster-scope acquire: the arrivals come from the other CTA of the pair.
+LYTH_D bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int *err) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((i & 255u) == 0) {
+            const uint64_t t = global_ns();
+            if (i == 0) t0 = t;
+            else if (t - t0 > kWaitNs) break;
+        }
+    }
+    atomicExch(err, 1);
+    return false;
+}
+
 LYTH_D void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
