@@ -1,6 +1,7 @@
 // Fused state-vector passes (lyth-circuit Group, crates/lyth-circuit/src/lib.rs:72-208 and
 // docs/ADR-0030): one pass over the state applies a run of consecutive gates that together
-// touch at most K <= 6 qubits.
+// touch at most K qubits -- K <= 13 in the tile pass (states of 2^14 amplitudes and more, below),
+// K <= 6 in the register pass described first, which small states take.
 //
 // A tuple is the 2^K amplitudes that differ only in the group's K bits. It is loaded once
 // (consecutive threads take consecutive values of the other bits, so every load of a warp is
