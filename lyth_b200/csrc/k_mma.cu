@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
                 const int m0 = (int)((tile % tiles_m) * M2_BM + 128 * crank);
                 const int n0 = (int)((tile / tiles_m) * M2_BN + 128 * crank);
                 for (uint32_t kb = 0; kb < kblocks; kb++) {
-                    if (!mbar_wait_cluster(empty(stage), phase ^ 1, &g_device_error)) { ok = false; break; }
+                    if (!mm_wait(empty(stage), phase ^ 1)) { ok = false; break; }
                     const uint32_t lf = mapa_shared(full(stage), 0);
                     mbar_expect_tx_cluster(lf, M2_STAGE_BYTES);
                     const int k0 = (int)(kb * MM_BK);
@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             // this CTA's barriers when it leaves.
             if (ok)
                 for (int s = 0; s < M2_STAGES; s++) {
-                    if (!mbar_wait_cluster(empty(stage), phase ^ 1, &g_device_error)) break;
+                    if (!mm_wait(empty(stage), phase ^ 1)) break;
                     if (++stage == M2_STAGES) { stage = 0; phase ^= 1; }
                 }
         }
@@ -353,11 +353,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             bool ok = true;
             for (uint32_t tile = pair; tile < ntiles && ok; tile += npairs, local++) {
                 const uint32_t ab = local & 1, aphase = (local >> 1) & 1;
-                if (!mbar_wait_cluster(tempty(ab), aphase ^ 1, &g_device_error)) { ok = false; break; }
+                if (!mm_wait(tempty(ab), aphase ^ 1)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + ab * M2_BN;
                 for (uint32_t kb = 0; kb < kblocks; kb++) {
-                    if (!mbar_wait_cluster(full(stage), phase, &g_device_error)) { ok = false; break; }
+                    if (!mm_wait(full(stage), phase)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_base = smem_u32(sA + stage * M2_A_BYTES);
                     const uint32_t b_base = smem_u32(sB + stage * M2_B_BYTES);
@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             // chance to land (both CTAs' copies complete on these barriers) before the pair leaves.
             if (!ok) {
                 for (int s = 0; s < M2_STAGES; s++) {
-                    mbar_wait_cluster(full(stage), phase, &g_device_error);
+                    mm_wait(full(stage), phase);
                     if (++stage == M2_STAGES) { stage = 0; phase ^= 1; }
                 }
             }
@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         uint32_t local = 0;
         for (uint32_t tile = pair; tile < ntiles; tile += npairs, local++) {
             const uint32_t ab = local & 1, aphase = (local >> 1) & 1;
-            if (!mbar_wait_cluster(tfull(ab), aphase, &g_device_error)) break;
+            if (!mm_wait(tfull(ab), aphase)) break;
             tc_fence_after();
             const uint32_t m0 = (tile % tiles_m) * M2_BM + 128 * crank, n0 = (tile / tiles_m) * M2_BN;
             const uint32_t row = m0 + quad * 32 + lane;

@@ -16,6 +16,7 @@
 
 #include <cooperative_groups.h>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -94,88 +95,116 @@ LYTH_D float block_partial(uint64_t n, const void *x, const void *y, uint64_t gr
 }
 
 // The B200 surface's partials: the same reference blocks, each still folded and tree-reduced by
-// 256 threads in the reference's order, but a persistent grid walks them (block b takes reference
-// blocks b, b + gridDim.x, ...) and issues the loads of its next reference block before the tree
-// of the current one. One CUDA block per reference block leaves too few bytes in flight per SM
-// when the reference block is small (2048 elements: 8 KiB of f32, 4 KiB of bf16), and the tree's
-// barriers then stall the loads; here a block always has its next block's loads outstanding.
+// 256 threads in the reference's order, but a CUDA block takes D of them at a time: its threads
+// issue the loads of all D (8 x D per thread) before folding any, and the D trees share their
+// barriers (three per D reference blocks instead of three per block). One CUDA block per
+// reference block keeps too few bytes in flight per SM when a reference block is small (2048
+// elements: 8 KiB of f32, 4 KiB of bf16) and pays its barriers and its launch per block.
 template <int OP, bool DOT, int TY>
-__global__ void __launch_bounds__(kRedBlock) partials_persistent_kernel(uint64_t n, const void *x, const void *y,
-                                                                        uint64_t grid, float *partial) {
-    __shared__ float slots[2][kRedBlock];
-    const unsigned t = threadIdx.x;
+__host__ __device__ constexpr int partials_batch() {
+    return DOT ? 2 : 4;
+}
+template <int OP, bool DOT, int TY>
+__global__ void __launch_bounds__(kRedBlock) partials_batched_kernel(uint64_t n, const void *x, const void *y,
+                                                                     uint64_t grid, float *partial) {
+    constexpr int D = partials_batch<OP, DOT, TY>();
+    __shared__ float slots[D][kRedBlock];
+    const unsigned t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const uint64_t stride = grid * kRedBlock;
     const uint64_t span = (uint64_t)kRedPerThread * stride;
-    float cx[kRedPerThread], cy[kRedPerThread], nx[kRedPerThread], ny[kRedPerThread];
-    auto fetch = [&](uint64_t rb, float *vx, float *vy) {
-        const uint64_t i = rb * kRedBlock + t;
-#pragma unroll
-        for (int u = 0; u < kRedPerThread; u++) {
-            const uint64_t j = i + (uint64_t)u * stride;
-            vx[u] = j < n ? load_el<TY>(x, j) : 0.0f;
-            if (DOT) vy[u] = j < n ? load_el<TY>(y, j) : 0.0f;
-        }
-    };
-    uint64_t rb = blockIdx.x;
-    if (rb < grid) fetch(rb, cx, cy);
-    for (int p = 0; rb < grid; rb += gridDim.x, p ^= 1) {
-        const uint64_t rn = rb + gridDim.x;
-        if (rn < grid) fetch(rn, nx, ny);
-        float acc = identity_of<OP>();
-        uint64_t i = rb * kRedBlock + t;
-#pragma unroll
-        for (int u = 0; u < kRedPerThread; u++)
-            if (i + (uint64_t)u * stride < n) acc = combine<OP>(acc, DOT ? __fmul_rn(cx[u], cy[u]) : cx[u]);
-        for (i += span; i < n; i += span) {  // inputs longer than 8 * 256 * grid (grid capped at 2^20)
-            float v[kRedPerThread];
+    const uint64_t batches = (grid + D - 1) / D;
+    for (uint64_t bt = blockIdx.x; bt < batches; bt += gridDim.x) {
+        float vx[D][kRedPerThread], vy[D][kRedPerThread];
+        const uint64_t i0 = bt * D * kRedBlock + t;
+        if ((bt + 1) * D <= grid && i0 + (D - 1) * kRedBlock + (kRedPerThread - 1) * stride < n) {
+            // the whole batch is inside: element (d, u) sits d * 256 after (0, u)
+            using E = typename std::conditional<TY == 0, float, uint16_t>::type;
+            const E *px = static_cast<const E *>(x) + i0;
+            const E *py = static_cast<const E *>(y) + i0;
 #pragma unroll
             for (int u = 0; u < kRedPerThread; u++) {
-                const uint64_t j = i + (uint64_t)u * stride;
-                if (j < n) v[u] = DOT ? __fmul_rn(load_el<TY>(x, j), load_el<TY>(y, j)) : load_el<TY>(x, j);
+#pragma unroll
+                for (int d = 0; d < D; d++) {
+                    vx[d][u] = load_el<TY>(px, d * kRedBlock);
+                    if (DOT) vy[d][u] = load_el<TY>(py, d * kRedBlock);
+                }
+                px += stride;
+                if (DOT) py += stride;
             }
+        } else {
 #pragma unroll
-            for (int u = 0; u < kRedPerThread; u++)
-                if (i + (uint64_t)u * stride < n) acc = combine<OP>(acc, v[u]);
-        }
-        // The tree, on this iteration's half of the double-buffered slots (the other half may
-        // still be read by warp 0 of the previous iteration until the first barrier below).
-        float *sl = slots[p];
-        sl[t] = acc;
-        __syncthreads();
-        if (t < 128) sl[t] = combine<OP>(sl[t], sl[t + 128]);
-        __syncthreads();
-        if (t < 64) sl[t] = combine<OP>(sl[t], sl[t + 64]);
-        __syncthreads();
-        if (t < 32) {
-            float v = combine<OP>(sl[t], sl[t + 32]);
+            for (int d = 0; d < D; d++) {
+                const uint64_t i = i0 + d * kRedBlock;  // reference blocks past `grid` load nothing
 #pragma unroll
-            for (int s = 16; s > 0; s >>= 1) v = combine<OP>(v, __shfl_down_sync(0xffffffffu, v, s));
-            if (t == 0) partial[rb] = v;
+                for (int u = 0; u < kRedPerThread; u++) {
+                    const uint64_t j = i + (uint64_t)u * stride;
+                    const bool in = bt * D + d < grid && j < n;
+                    vx[d][u] = in ? load_el<TY>(x, j) : 0.0f;
+                    if (DOT) vy[d][u] = in ? load_el<TY>(y, j) : 0.0f;
+                }
+            }
         }
 #pragma unroll
-        for (int u = 0; u < kRedPerThread; u++) {
-            cx[u] = nx[u];
-            if (DOT) cy[u] = ny[u];
+        for (int d = 0; d < D; d++) {
+            float acc = identity_of<OP>();
+            uint64_t i = (bt * D + d) * kRedBlock + t;
+            if (bt * D + d < grid) {
+#pragma unroll
+                for (int u = 0; u < kRedPerThread; u++)
+                    if (i + (uint64_t)u * stride < n)
+                        acc = combine<OP>(acc, DOT ? __fmul_rn(vx[d][u], vy[d][u]) : vx[d][u]);
+                for (i += span; i < n; i += span) {  // inputs longer than 8 * 256 * grid (grid capped at 2^20)
+                    float v[kRedPerThread];
+#pragma unroll
+                    for (int u = 0; u < kRedPerThread; u++) {
+                        const uint64_t j = i + (uint64_t)u * stride;
+                        if (j < n) v[u] = DOT ? __fmul_rn(load_el<TY>(x, j), load_el<TY>(y, j)) : load_el<TY>(x, j);
+                    }
+#pragma unroll
+                    for (int u = 0; u < kRedPerThread; u++)
+                        if (i + (uint64_t)u * stride < n) acc = combine<OP>(acc, v[u]);
+                }
+            }
+            slots[d][t] = acc;
         }
+        // The D trees, level by level: 128, 64 in shared memory, then warp d finishes tree d
+        // (32 through the last shuffles).
+        __syncthreads();
+        if (t < 128)
+#pragma unroll
+            for (int d = 0; d < D; d++) slots[d][t] = combine<OP>(slots[d][t], slots[d][t + 128]);
+        __syncthreads();
+        if (t < 64)
+#pragma unroll
+            for (int d = 0; d < D; d++) slots[d][t] = combine<OP>(slots[d][t], slots[d][t + 64]);
+        __syncthreads();
+        if (warp < (unsigned)D && bt * D + warp < grid) {
+            float v = combine<OP>(slots[warp][lane], slots[warp][lane + 32]);
+#pragma unroll
+            for (int s2 = 16; s2 > 0; s2 >>= 1) v = combine<OP>(v, __shfl_down_sync(0xffffffffu, v, s2));
+            if (lane == 0) partial[bt * D + warp] = v;
+        }
+        __syncthreads();  // the slots are rewritten by the next batch
     }
 }
 
-// Blocks of the persistent grid: as many as fit on the device at once, at most one per
-// reference block.
+// Blocks of the grid: as many as fit on the device at once, at most one per batch of reference
+// blocks.
 template <int OP, bool DOT, int TY>
-int launch_persistent(uint64_t n, const void *x, const void *y, uint32_t grid, float *partial, cudaStream_t s) {
+int launch_batched(uint64_t n, const void *x, const void *y, uint32_t grid, float *partial, cudaStream_t s) {
     static int per_sm = 0;
     if (per_sm == 0) {
         int b = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, partials_persistent_kernel<OP, DOT, TY>, kRedBlock, 0) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, partials_batched_kernel<OP, DOT, TY>, kRedBlock, 0) !=
                 cudaSuccess ||
             b < 1)
             b = 1;
         per_sm = b;
     }
     const uint64_t cap = (uint64_t)device_sms() * per_sm;
-    const unsigned blocks = (unsigned)(grid < cap ? grid : cap);
-    partials_persistent_kernel<OP, DOT, TY><<<blocks, kRedBlock, 0, s>>>(n, x, y, grid, partial);
+    const uint64_t batches = (grid + partials_batch<OP, DOT, TY>() - 1) / partials_batch<OP, DOT, TY>();
+    const unsigned blocks = (unsigned)(batches < cap ? batches : cap);
+    partials_batched_kernel<OP, DOT, TY><<<blocks, kRedBlock, 0, s>>>(n, x, y, grid, partial);
     return last_launch_status();
 }
 
@@ -269,10 +298,10 @@ extern "C" uint32_t lyth_b200_reduce_grid(uint64_t n) {
 template <int TY>
 static int launch_partials(int op, uint64_t n, const void *x, const void *y, uint32_t grid, float *partial,
                            cudaStream_t s) {
-    if (op == 0 && y) return launch_persistent<0, true, TY>(n, x, y, grid, partial, s);
-    if (op == 0) return launch_persistent<0, false, TY>(n, x, y, grid, partial, s);
-    if (op == 1 && !y) return launch_persistent<1, false, TY>(n, x, y, grid, partial, s);
-    if (op == 2 && !y) return launch_persistent<2, false, TY>(n, x, y, grid, partial, s);
+    if (op == 0 && y) return launch_batched<0, true, TY>(n, x, y, grid, partial, s);
+    if (op == 0) return launch_batched<0, false, TY>(n, x, y, grid, partial, s);
+    if (op == 1 && !y) return launch_batched<1, false, TY>(n, x, y, grid, partial, s);
+    if (op == 2 && !y) return launch_batched<2, false, TY>(n, x, y, grid, partial, s);
     return LYTH_E_UNSUPPORTED;
 }
 

@@ -84,37 +84,16 @@ LYTH_D uint32_t cluster_ctarank() {
 LYTH_D void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// Arrive (and expect `bytes`) on a barrier given by its shared::cluster address.
+// Arrive (and expect `bytes`) on a barrier given by its shared::cluster address (this CTA's or
+// the partner's). The data a barrier guards is ordered by the copy's complete_tx or, for tensor
+// memory, by the tcgen05 fences around the arrive and the wait, so the default semantics suffice
+// (a cluster-scope acquire in every poll of a wait would cost each poll a cluster-wide fence).
 LYTH_D void mbar_expect_tx_cluster(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 LYTH_D void mbar_arrive_cluster(uint32_t bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// mbar_wait_limited with cluster-scope acquire: the arrivals come from the other CTA of the pair.
-LYTH_D bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int *err) {
-    uint64_t t0 = 0;
-    for (uint32_t i = 0; i < kWaitPolls; ++i) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if ((i & 255u) == 0) {
-            const uint64_t t = global_ns();
-            if (i == 0) t0 = t;
-            else if (t - t0 > kWaitNs) break;
-        }
-    }
-    atomicExch(err, 1);
-    return false;
-}
-
 LYTH_D void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
