@@ -188,6 +188,128 @@ __global__ void __launch_bounds__(kRedBlock) partials_batched_kernel(uint64_t n,
     }
 }
 
+// 16-bit elements: a thread takes two neighbouring reference threads (elements 2j and 2j + 1 of
+// a reference block) with one 32-bit load each step and keeps their two folds apart, so a CUDA
+// block of 256 threads covers two reference blocks per slot; D reference blocks (S slots) per
+// iteration. Every fold and every tree is still the reference's.
+template <int OP, bool DOT, int TY>
+__host__ __device__ constexpr int pair_slots() {
+    return DOT ? 2 : 4;
+}
+template <int TY>
+LYTH_D float widen16(uint32_t h) {
+    return TY == 1 ? __half2float(__ushort_as_half((uint16_t)h)) : __uint_as_float(h << 16);
+}
+template <int OP, bool DOT, int TY>
+__global__ void __launch_bounds__(kRedBlock) partials_pair_kernel(uint64_t n, const uint16_t *x, const uint16_t *y,
+                                                                  uint64_t grid, float *partial) {
+    constexpr int S = pair_slots<OP, DOT, TY>(), D = 2 * S;
+    __shared__ float slots[D][kRedBlock];
+    const unsigned t = threadIdx.x, warp = t >> 5, lane = t & 31, h = t >> 7, tt = t & 127;
+    const uint64_t stride = grid * kRedBlock;
+    const uint64_t span = (uint64_t)kRedPerThread * stride;
+    const uint64_t batches = (grid + D - 1) / D;
+    for (uint64_t bt = blockIdx.x; bt < batches; bt += gridDim.x) {
+        const uint64_t rb0 = bt * D;
+        float lo[S], hi[S];
+        if ((bt + 1) * D <= grid && span >= n && (rb0 + D) * kRedBlock + (kRedPerThread - 1) * stride <= n) {
+            uint32_t wx[S][kRedPerThread], wy[S][kRedPerThread];
+#pragma unroll
+            for (int q = 0; q < S; q++) {
+                const uint32_t *px = reinterpret_cast<const uint32_t *>(x + (rb0 + 2 * q + h) * kRedBlock + 2 * tt);
+                const uint32_t *py = reinterpret_cast<const uint32_t *>(y + (rb0 + 2 * q + h) * kRedBlock + 2 * tt);
+#pragma unroll
+                for (int u = 0; u < kRedPerThread; u++) {
+                    wx[q][u] = px[(uint64_t)u * (stride >> 1)];
+                    if (DOT) wy[q][u] = py[(uint64_t)u * (stride >> 1)];
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < S; q++) {
+                float a0 = identity_of<OP>(), a1 = identity_of<OP>();
+#pragma unroll
+                for (int u = 0; u < kRedPerThread; u++) {
+                    const float x0 = widen16<TY>(wx[q][u] & 0xFFFFu), x1 = widen16<TY>(wx[q][u] >> 16);
+                    if (DOT) {
+                        const float y0 = widen16<TY>(wy[q][u] & 0xFFFFu), y1 = widen16<TY>(wy[q][u] >> 16);
+                        a0 = combine<OP>(a0, __fmul_rn(x0, y0));
+                        a1 = combine<OP>(a1, __fmul_rn(x1, y1));
+                    } else {
+                        a0 = combine<OP>(a0, x0);
+                        a1 = combine<OP>(a1, x1);
+                    }
+                }
+                lo[q] = a0;
+                hi[q] = a1;
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < S; q++) {
+                const uint64_t rb = rb0 + 2 * q + h;
+                float a[2] = {identity_of<OP>(), identity_of<OP>()};
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    if (rb >= grid) continue;  // reference blocks past `grid` load nothing
+                    for (uint64_t i = rb * kRedBlock + 2 * tt + e; i < n; i += span) {
+                        float v[kRedPerThread];
+#pragma unroll
+                        for (int u = 0; u < kRedPerThread; u++) {
+                            const uint64_t j = i + (uint64_t)u * stride;
+                            if (j < n) v[u] = DOT ? __fmul_rn(load_el<TY>(x, j), load_el<TY>(y, j)) : load_el<TY>(x, j);
+                        }
+#pragma unroll
+                        for (int u = 0; u < kRedPerThread; u++)
+                            if (i + (uint64_t)u * stride < n) a[e] = combine<OP>(a[e], v[u]);
+                    }
+                }
+                lo[q] = a[0];
+                hi[q] = a[1];
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < S; q++) {
+            slots[2 * q + h][2 * tt] = lo[q];
+            slots[2 * q + h][2 * tt + 1] = hi[q];
+        }
+        // The D trees level by level (128, 64 in shared memory), then warp d finishes tree d.
+        __syncthreads();
+#pragma unroll
+        for (unsigned k = t; k < (unsigned)D * 128; k += kRedBlock)
+            slots[k >> 7][k & 127] = combine<OP>(slots[k >> 7][k & 127], slots[k >> 7][(k & 127) + 128]);
+        __syncthreads();
+#pragma unroll
+        for (unsigned k = t; k < (unsigned)D * 64; k += kRedBlock)
+            slots[k >> 6][k & 63] = combine<OP>(slots[k >> 6][k & 63], slots[k >> 6][(k & 63) + 64]);
+        __syncthreads();
+        if (warp < (unsigned)D && rb0 + warp < grid) {
+            float v = combine<OP>(slots[warp][lane], slots[warp][lane + 32]);
+#pragma unroll
+            for (int s2 = 16; s2 > 0; s2 >>= 1) v = combine<OP>(v, __shfl_down_sync(0xffffffffu, v, s2));
+            if (lane == 0) partial[rb0 + warp] = v;
+        }
+        __syncthreads();  // the slots are rewritten by the next batch
+    }
+}
+
+template <int OP, bool DOT, int TY>
+int launch_pair(uint64_t n, const uint16_t *x, const uint16_t *y, uint32_t grid, float *partial, cudaStream_t s) {
+    static int per_sm = 0;
+    if (per_sm == 0) {
+        int b = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, partials_pair_kernel<OP, DOT, TY>, kRedBlock, 0) !=
+                cudaSuccess ||
+            b < 1)
+            b = 1;
+        per_sm = b;
+    }
+    constexpr int D = 2 * pair_slots<OP, DOT, TY>();
+    const uint64_t cap = (uint64_t)device_sms() * per_sm;
+    const uint64_t batches = (grid + D - 1) / D;
+    const unsigned blocks = (unsigned)(batches < cap ? batches : cap);
+    partials_pair_kernel<OP, DOT, TY><<<blocks, kRedBlock, 0, s>>>(n, x, y, grid, partial);
+    return last_launch_status();
+}
+
 // Blocks of the grid: as many as fit on the device at once, at most one per batch of reference
 // blocks.
 template <int OP, bool DOT, int TY>
@@ -305,9 +427,24 @@ static int launch_partials(int op, uint64_t n, const void *x, const void *y, uin
     return LYTH_E_UNSUPPORTED;
 }
 
+template <int TY>
+static int launch_partials_pair(int op, uint64_t n, const uint16_t *x, const uint16_t *y, uint32_t grid,
+                                float *partial, cudaStream_t s) {
+    if (op == 0 && y) return launch_pair<0, true, TY>(n, x, y, grid, partial, s);
+    if (op == 0) return launch_pair<0, false, TY>(n, x, y, grid, partial, s);
+    if (op == 1 && !y) return launch_pair<1, false, TY>(n, x, y, grid, partial, s);
+    if (op == 2 && !y) return launch_pair<2, false, TY>(n, x, y, grid, partial, s);
+    return LYTH_E_UNSUPPORTED;
+}
+
 extern "C" int lyth_b200_reduce_partials_narrow(int op, int ty, uint64_t n, const uint16_t *x, const uint16_t *y,
                                                 uint32_t grid, float *partial, cudaStream_t s) {
     if (!x || !partial || grid == 0) return LYTH_E_INVALID;
+    // buffers on 4-byte boundaries take the paired 32-bit loads
+    if (!((((uintptr_t)x) | ((uintptr_t)y)) & 3u)) {
+        if (ty == LYTH_NARROW_F16) return launch_partials_pair<1>(op, n, x, y, grid, partial, s);
+        if (ty == LYTH_NARROW_BF16) return launch_partials_pair<2>(op, n, x, y, grid, partial, s);
+    }
     if (ty == LYTH_NARROW_F16) return launch_partials<1>(op, n, x, y, grid, partial, s);
     if (ty == LYTH_NARROW_BF16) return launch_partials<2>(op, n, x, y, grid, partial, s);
     return LYTH_E_UNSUPPORTED;

@@ -71,13 +71,17 @@ def test_transpose_bit_exact(cuda, ty, rows, cols):
     assert np.array_equal(dev_bits(bd).ravel(), ab.reshape(rows, cols).T.ravel())
 
 
+# n = 2^22 fills every batch of reference blocks exactly (the paired 32-bit loads throughout);
+# offset = 1 starts both buffers on an odd element (2-byte aligned: the 16-bit loads).
 @pytest.mark.parametrize("ty", ["f16", "bf16"])
-@pytest.mark.parametrize("n", [1, 2049, 1_000_003])
-def test_reduction_partials_bit_exact(cuda, ty, n):
+@pytest.mark.parametrize("n,offset", [(1, 0), (2049, 0), (1_000_003, 0), (1 << 22, 0), (1_000_003, 1)])
+def test_reduction_partials_bit_exact(cuda, ty, n, offset):
     xb, yb = narrow_input(16, n, ty), narrow_input(17, n, ty)
     x, y = widen(xb, ty), widen(yb, ty)
     grid = int(lb.lib.lyth_b200_reduce_grid(n))
-    xd, yd = to_dev(xb, ty, cuda), to_dev(yb, ty, cuda)
+    pad = np.zeros(offset, np.uint16)
+    xd = to_dev(np.concatenate([pad, xb]), ty, cuda)[offset:]
+    yd = to_dev(np.concatenate([pad, yb]), ty, cuda)[offset:]
     for op, yy, want in ((lb.SUM, None, orc.reduce(orc.SUM, x, grid=grid)),
                          (lb.SUM, yd, orc.reduce(orc.SUM, x, y, grid=grid)),
                          (lb.MAX, None, orc.reduce(orc.MAX, x, grid=grid)),
