@@ -139,10 +139,7 @@ LYTH_D void quads_body(uint64_t n, bool pow2, unsigned c, unsigned t, uint64_t w
     const bool inplace = (re == qr) && (im == qi);
     const bool vec = pow2 && (c >= 2 && t >= 2) && (n & 15u) == 0 &&
                      ((((uintptr_t)re) | ((uintptr_t)im) | ((uintptr_t)qr) | ((uintptr_t)qi)) & 15u) == 0;
-    // In place, the untouched quarters are skipped -- unless a skipped 16-byte vector shares a
-    // 32-byte sector with a written one (the skipped bit is bit 2): a half-written sector may be
-    // merged in L2 from a fresh DRAM read, which costs more than writing the same values back.
-    const bool copy_all = !inplace || (vec && (KIND == 0 ? c == 2 : (c == 2 || t == 2)));
+    const bool copy_all = !inplace;
     if (vec) {
         const uint64_t groups = quads >> 2;
         for (uint64_t g = tid; g < groups; g += nthreads) {

@@ -318,6 +318,101 @@ __global__ void __launch_bounds__(kTxTeams * kTxTeamThreads)
     }
 }
 
+// The same for 16-bit elements (the narrow transpose): a 128-byte box row holds 64 elements, so
+// a tile is 64 x 64 (8 KiB) and a thread moves an 8 x 8 block -- eight 128-bit loads of rows
+// 8tr..8tr+7 at chunk tc, a transpose in registers (one PRMT per output word: word w of output
+// row j takes element j of input rows 2w and 2w+1), eight 128-bit stores into output rows
+// 8tc..8tc+7 at chunk tr. The swizzled chunk of row r is c ^ (r & 7) and r & 7 is the block's own
+// row index, so with (tr, tc) = (p ^ q, p) every quarter-warp again reaches 8 distinct chunks.
+constexpr uint32_t kTx16TileBytes = 64 * 64 * 2;
+constexpr size_t kTx16Smem = 1024 + (size_t)kTxTeams * 3 * kTx16TileBytes + kTxTeams * 2 * sizeof(uint64_t);
+
+__global__ void __launch_bounds__(kTxTeams * kTxTeamThreads)
+    transpose_tma16_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ CUtensorMap tout,
+                           uint32_t rows, uint32_t cols) {
+    extern __shared__ uint8_t tx_raw[];
+    const uint32_t raw = smem_u32(tx_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;  // the 128-byte swizzle repeats every 1 KiB
+    const int team = threadIdx.x / kTxTeamThreads, t = threadIdx.x % kTxTeamThreads;
+    const int bar_id = 1 + team;
+    const uint32_t in0 = base + (uint32_t)team * 3 * kTx16TileBytes, out = in0 + 2 * kTx16TileBytes;
+    uint64_t *bars =
+        reinterpret_cast<uint64_t *>(tx_raw + (base - raw) + (size_t)kTxTeams * 3 * kTx16TileBytes) + team * 2;
+    const uint32_t tiles_x = (cols + 63) / 64, tiles_y = (rows + 63) / 64;
+    const uint64_t tiles = (uint64_t)tiles_x * tiles_y;
+    const uint64_t stride = (uint64_t)gridDim.x * kTxTeams;
+    const uint64_t first = (uint64_t)blockIdx.x * kTxTeams + team;
+    const uint64_t mine = tiles > first ? (tiles - first + stride - 1) / stride : 0;
+    auto tile_of = [&](uint64_t k) { return first + k * stride; };
+    auto load = [&](uint64_t k) {
+        const uint64_t tl = tile_of(k);
+        const uint32_t b = smem_u32(bars + (k & 1));
+        mbar_expect_tx(b, kTx16TileBytes);
+        tensor_load_2d(in0 + (uint32_t)(k & 1) * kTx16TileBytes, &tin, (int)((tl % tiles_x) * 64),
+                       (int)((tl / tiles_x) * 64), b);
+    };
+    if (t == 0) {
+        mbar_init(smem_u32(bars), 1);
+        mbar_init(smem_u32(bars + 1), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (uint64_t k = 0; k < 2 && k < mine; k++) load(k);
+    }
+    team_sync(bar_id);
+    const int p = t & 7, q = t >> 3;
+    const int tc = p, tr = p ^ q;
+    uint64_t armed = mine < 2 ? mine : 2, used = 0;
+    for (uint64_t k = 0; k < mine; k++) {
+        const bool ok = mbar_wait(smem_u32(bars + (k & 1)), (uint32_t)(k >> 1) & 1u, &g_tx_error);
+        if (!team_all(bar_id, ok)) break;
+        used++;
+        const uint32_t in = in0 + (uint32_t)(k & 1) * kTx16TileBytes;
+        uint4 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t r = 8 * tr + i;
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v[i].x), "=r"(v[i].y), "=r"(v[i].z), "=r"(v[i].w)
+                         : "r"(in + r * 128u + (uint32_t)((tc ^ i) << 4))
+                         : "memory");
+        }
+        if (t == 0) bulk_wait_read0();  // the previous tile's store has read the output buffer
+        team_sync(bar_id);
+        // every thread has read this stage: the leader may refill it with the tile two ahead
+        if (t == 0 && k + 2 < mine) {
+            load(k + 2);
+            armed++;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            uint32_t w[4];
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                const uint32_t *a = reinterpret_cast<const uint32_t *>(&v[2 * h]);
+                const uint32_t *b = reinterpret_cast<const uint32_t *>(&v[2 * h + 1]);
+                uint32_t d;
+                asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a[j >> 1]), "r"(b[j >> 1]), "r"((j & 1) ? 0x7632u : 0x5410u));
+                w[h] = d;
+            }
+            const uint32_t r = 8 * tc + j;
+            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(out + r * 128u + (uint32_t)((tr ^ j) << 4)),
+                         "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                         : "memory");
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        team_sync(bar_id);
+        if (t == 0) {
+            const uint64_t tl = tile_of(k);
+            tensor_store_2d(&tout, (int)((tl / tiles_x) * 64), (int)((tl % tiles_x) * 64), out);
+            bulk_commit();
+        }
+    }
+    if (t == 0) {
+        bulk_wait0();
+        // after a timed-out wait, a load may still be in flight: wait for it (bounded)
+        for (uint64_t k = used; k < armed; k++) mbar_wait(smem_u32(bars + (k & 1)), (uint32_t)(k >> 1) & 1u, &g_tx_error);
+    }
+}
+
 // ------------------------------------------------------------------ narrow storage (ADR-0024)
 // f16 / bf16 buffers, f32 arithmetic: each element is widened exactly on load, the body runs the
 // same f32 chain as the f32 kernel, and each drained value is rounded once, to nearest even, at
@@ -547,6 +642,38 @@ extern "C" int lyth_b200_transpose_narrow(int ty, uint32_t rows, uint32_t cols, 
     if (ty != LYTH_NARROW_F16 && ty != LYTH_NARROW_BF16) return LYTH_E_UNSUPPORTED;
     if ((uint64_t)rows * cols == 0) return LYTH_OK;
     if (!a || !b) return LYTH_E_INVALID;
+    // 16-byte row pitches (rows and cols multiples of 8) and aligned buffers: the TMA tiles
+    PFN_encode_tiled enc = tensor_map_encoder();
+    if (!(rows & 7u) && !(cols & 7u) && aligned16(a) && aligned16(b) && enc) {
+        const cuuint32_t box[2] = {64, 64}, estr[2] = {1, 1};
+        const cuuint64_t da[2] = {cols, rows}, sa[1] = {(cuuint64_t)cols * 2};
+        const cuuint64_t db[2] = {rows, cols}, sb[1] = {(cuuint64_t)rows * 2};
+        CUtensorMap ta, tb;
+        memset(&ta, 0, sizeof ta);
+        memset(&tb, 0, sizeof tb);
+        if (enc(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t *>(a), da, sa, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
+            enc(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, b, db, sb, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+            static bool attr_done[64] = {false};
+            int dev = 0;
+            if (cudaGetDevice(&dev) != cudaSuccess) return LYTH_E_INVALID;
+            if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+                const cudaError_t e = cudaFuncSetAttribute(transpose_tma16_kernel,
+                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTx16Smem);
+                if (e != cudaSuccess) return status_of(e);
+                attr_done[dev] = true;
+            }
+            const uint64_t tiles = (uint64_t)((rows + 63) / 64) * ((cols + 63) / 64);
+            uint64_t grid = (tiles + kTxTeams - 1) / kTxTeams;
+            const uint64_t cap = (uint64_t)device_sms() * 2;  // two CTAs (8 teams) per SM
+            if (grid > cap) grid = cap;
+            transpose_tma16_kernel<<<(unsigned)grid, kTxTeams * kTxTeamThreads, kTx16Smem, s>>>(ta, tb, rows, cols);
+            return last_launch_status();
+        }
+    }
     const uint64_t tiles = (uint64_t)((rows + 31) / 32) * ((cols + 31) / 32);
     uint64_t grid = tiles;
     const uint64_t cap = (uint64_t)device_sms() * 8;

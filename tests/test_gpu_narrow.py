@@ -62,7 +62,9 @@ def test_saxpy_in_place(cuda, ty):
 
 
 @pytest.mark.parametrize("ty", ["f16", "bf16"])
-@pytest.mark.parametrize("rows,cols", [(1, 1), (33, 17), (257, 300), (4096, 4096), (31, 129)])
+# rows and cols multiples of 8 take the TMA tiles (64 x 64, edges clipped); the rest the plain tile
+@pytest.mark.parametrize("rows,cols", [(1, 1), (33, 17), (257, 300), (4096, 4096), (31, 129), (8, 8), (64, 200),
+                                       (136, 72), (1024, 8), (8, 1032)])
 def test_transpose_bit_exact(cuda, ty, rows, cols):
     ab = narrow_input(15, rows * cols, ty)
     ad = to_dev(ab, ty, cuda).view(rows, cols)
