@@ -519,6 +519,8 @@ def per_kernel(pk: dict, only: str | None = None, small: bool = False, reps: int
     leaves clean lines, so no write-back lands inside the timed window), median of the reps."""
     import torch
 
+    import lyth_b200 as lb
+
     dev = torch.device("cuda")
     hbm = pk["hbm_gbs"]
     flush = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
@@ -558,6 +560,8 @@ def per_kernel(pk: dict, only: str | None = None, small: bool = False, reps: int
             r = {"TFLOP_s": round(tf, 2), "ms": round(ms, 4)}
             if "bf16" in name:
                 r["frac_bf16_measured"] = round(tf / pk["bf16_tflops"], 4)
+                if "1sm" not in name:
+                    r["cta_pairs"] = int(lb.lib.lyth_b200_matmul_bf16_pairs())
             else:
                 r["frac_fp32_nominal"] = round(tf / ffma_peak, 4)
                 r["fp32_nominal_tflops"] = round(ffma_peak, 1)

@@ -438,6 +438,9 @@ int lyth_b200_matmul_bf16(uint32_t m, uint32_t n, uint32_t k, const uint16_t *a,
  * LYTH_E_UNSUPPORTED), pair = 0 the single-SM kernel. For tests and measurements of both. */
 int lyth_b200_matmul_bf16_form(int pair, uint32_t m, uint32_t n, uint32_t k, const uint16_t *a,
                                const uint16_t *b, float *c, cudaStream_t stream);
+/* CTA pairs the pair form runs on the current device (clusters of 2 resident at once), or a
+ * negative status. */
+int lyth_b200_matmul_bf16_pairs(void);
 /* LYTH_E_TIMEOUT when a bounded device-side wait of any kernel in this library ran out since the
  * last call (the flag is then cleared), else LYTH_OK. Synchronises with the current device. */
 int lyth_b200_device_error(void);

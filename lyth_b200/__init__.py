@@ -93,6 +93,7 @@ _sig("lyth_b200_reduce", _i32, [_i32, _u64, _vp, _vp, _vp, _vp, C.c_size_t, _vp]
 _sig("lyth_b200_matmul_f32", _i32, [_u32, _u32, _u32, _vp, _vp, _vp, _i32, _vp])
 _sig("lyth_b200_matmul_bf16", _i32, [_u32, _u32, _u32, _vp, _vp, _vp, _vp])
 _sig("lyth_b200_matmul_bf16_form", _i32, [_i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp])
+_sig("lyth_b200_matmul_bf16_pairs", _i32, [])
 _sig("lyth_b200_gemv_q4", _i32, [_i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp])
 _sig("lyth_b200_gemv_dequant", _i32, [_i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp])
 _sig("lyth_b200_nf4_codebook", None, [C.POINTER(_f32)])

@@ -436,6 +436,23 @@ static bool make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_
 
 using namespace lyth;
 
+// CTA pairs of the pair kernel resident at once on device `dev` (a GPC with an odd count of SMs
+// holds one pair fewer than half its SMs), asked once per device. `cfg` is the launch's
+// configuration (block, shared memory, cluster shape); its grid is overwritten.
+static int mma2_pairs(int dev, int sms, cudaLaunchConfig_t &cfg) {
+    static int fit_of[64] = {0};
+    const int pairs = sms / 2;
+    if (dev < 0 || dev >= 64) return pairs;
+    if (fit_of[dev] == 0) {
+        cfg.gridDim = dim3(2u * (unsigned)pairs);
+        int fit = 0;
+        if (cudaOccupancyMaxActiveClusters(&fit, mma2_bf16_kernel, &cfg) != cudaSuccess || fit < 1) fit = pairs;
+        cudaGetLastError();
+        fit_of[dev] = fit < pairs ? fit : pairs;
+    }
+    return fit_of[dev];
+}
+
 // pair: 1 = the 2-SM kernel (m a multiple of 256), 0 = the 1-SM kernel, -1 = the 2-SM kernel
 // where the shape allows it.
 static int matmul_bf16_launch(uint32_t m, uint32_t n, uint32_t k, const uint16_t *a, const uint16_t *b, float *c,
@@ -479,18 +496,7 @@ static int matmul_bf16_launch(uint32_t m, uint32_t n, uint32_t k, const uint16_t
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    // CTA pairs resident at once (a GPC with an odd count of SMs holds one pair fewer than half
-    // its SMs), asked once per device.
-    static int fit_of[64] = {0};
-    int pairs = sms / 2;
-    if (dev >= 0 && dev < 64 && fit_of[dev] == 0) {
-        cfg.gridDim = dim3(2u * (unsigned)pairs);
-        int fit = 0;
-        if (cudaOccupancyMaxActiveClusters(&fit, mma2_bf16_kernel, &cfg) != cudaSuccess || fit < 1) fit = pairs;
-        cudaGetLastError();
-        fit_of[dev] = fit;
-    }
-    if (dev >= 0 && dev < 64 && fit_of[dev] < pairs) pairs = fit_of[dev];
+    int pairs = mma2_pairs(dev, sms, cfg);
     if ((uint32_t)pairs > tiles) pairs = (int)tiles;
     cfg.gridDim = dim3(2u * (unsigned)pairs);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, mma2_bf16_kernel, ta, tb, c, m, n, k);
@@ -501,6 +507,25 @@ static int matmul_bf16_launch(uint32_t m, uint32_t n, uint32_t k, const uint16_t
 extern "C" int lyth_b200_matmul_bf16(uint32_t m, uint32_t n, uint32_t k, const uint16_t *a, const uint16_t *b,
                                      float *c, cudaStream_t s) {
     return matmul_bf16_launch(m, n, k, a, b, c, s, -1);
+}
+
+extern "C" int lyth_b200_matmul_bf16_pairs(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return LYTH_E_INVALID;
+    const cudaError_t e =
+        cudaFuncSetAttribute(mma2_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)M2_SMEM);
+    if (e != cudaSuccess) return status_of(e);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(MM_THREADS);
+    cfg.dynamicSmemBytes = M2_SMEM;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return mma2_pairs(dev, device_sms(), cfg);
 }
 
 extern "C" int lyth_b200_matmul_bf16_form(int pair, uint32_t m, uint32_t n, uint32_t k, const uint16_t *a,

@@ -81,3 +81,10 @@ def test_unsupported_shapes_are_refused(cuda):
     with pytest.raises(lb.LythError) as e:
         lb.matmul_bf16(a, b, c)
     assert e.value.status == lb.E_UNSUPPORTED
+
+
+def test_pair_count_is_the_resident_clusters(cuda):
+    # the pair form runs as many CTA pairs as fit at once: at most half the SMs, at least one
+    p = int(lb.lib.lyth_b200_matmul_bf16_pairs())
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    assert 1 <= p <= sms // 2
