@@ -894,7 +894,7 @@ def ours(a, dist: Dist) -> None:
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"]},
             "engine": {"passes": st["passes"], "exchanges": st["exchanges"], "bytes_sent": st["bytes_sent"],
-                       "settings": {"fusion": a.fuse or 13, "swap_batch": a.swap_batch or 1,
+                       "settings": {"fusion": a.fuse or 13, "swap_batch": a.swap_batch or 6,
                                     "diagonal_rank_gates": "no exchange" if a.diagonal in (None, 1) else "exchange",
                                     "transport": ("copy_engine" if sv_transport else "nccl") if dist.world > 1
                                     else None, "pull_queues": (a.pull_queues or 2) if dist.world > 1 else None}},

@@ -711,11 +711,11 @@ int lyth_sv_set_remap(lyth_sv *sv, int on);
  * would also not turn it into NaN). on = 0 treats it like any other gate (swap-in or exchange)
  * and is bit-identical with the evaluator in every case. Collective: every rank, same value. */
 int lyth_sv_set_diagonal(lyth_sv *sv, int on);
-/* With remap on: the most rank-bit qubits one swap-in brings in together (1..6, default 1 = one at
- * a time). Extra ones join only while each is needed before the local qubit it displaces; k of
+/* With remap on: the most rank-bit qubits one swap-in brings in together (1..6, default 6; 1 = one
+ * at a time). Extra ones join only while each is needed before the local bit it displaces; k of
  * them cost one exchange of (2^k - 1) / 2^k of the shard among 2^k ranks instead of k half-shard
- * swaps (fewer bytes, but a pull from several partners runs slower than a pairwise one on B200).
- * Bit-exact either way. */
+ * swaps (fewer bytes and fewer passes, though a pull from several partners runs slower per byte
+ * than a pairwise one). Bit-exact either way. Collective: every rank, same value. */
 int lyth_sv_set_swap_batch(lyth_sv *sv, int max_qubits);
 /* Transport of swap-ins on a multi-rank handle: 1 = copy engines (each rank pulls its partners'
  * packed chunks over NVLink with cudaMemcpyAsync through CUDA IPC mappings, ordered by sequence

@@ -295,10 +295,11 @@ struct lyth_sv {
     // Rank-bit gates: 1 = swap the qubit into a local bit first (default), 0 = pairwise
     // exchange of the whole shard and compute this rank's row.
     int remap = 1;
-    // Most rank-bit qubits one swap-in may bring in together (lyth_sv_set_swap_batch). One at a
-    // time by default: measured at 4 GPUs, a pairwise pull runs at 516 GB/s each way and a pull
-    // from three partners at ~390 in aggregate, so single swaps win despite the larger volume.
-    int swap_batch = 1;
+    // Most rank-bit qubits one swap-in may bring in together (lyth_sv_set_swap_batch). With
+    // diagonal rank-bit gates moving no data, the swap-ins left are the rank-bit qubits' non-
+    // diagonal gates, which a batch takes in one exchange among 2^k ranks: fewer bytes than k
+    // single swaps, and no single-gate passes squeezed between consecutive swap-ins.
+    int swap_batch = 6;
     // Diagonal gates on rank bits (lyth_sv_set_diagonal): 1 = no exchange -- on a shard whose
     // rank bit is v the gate is the scalar u_vv (under its control, when it has one), applied as
     // a local gate diag(u_vv, u_vv); 0 = swap-in or exchange like any other gate.
@@ -381,6 +382,18 @@ int sync_stream(lyth_sv *sv, cudaStream_t stream) {
         v->comm_aborted = true;
     };
     return wait_with_deadline(h, sv->deadline_ms, 50, nullptr);
+}
+
+// Every queue of the handle drained: the communication and copy queues first (pulls and NCCL),
+// then the compute stream. The pulls on the extra queues are also joined into the communication
+// stream by events; draining them here keeps that from being the only guarantee.
+int drain_all(lyth_sv *sv) {
+    int st = sync_stream(sv, sv->comm_stream);
+    if (!st && sv->copy_stream) st = sync_stream(sv, sv->copy_stream);
+    for (int i = 0; !st && i < lyth_sv::kExtraQueues; i++)
+        if (sv->xq[i]) st = sync_stream(sv, sv->xq[i]);
+    if (!st) st = sync_stream(sv, sv->stream);
+    return st;
 }
 
 void reset_map(lyth_sv *sv) {
@@ -1381,9 +1394,7 @@ int lyth_sv_set_transport(lyth_sv *sv, int copy_engine) {
         DeviceGuard guard(sv);
         // drain the current transport before switching: partners must have pulled every chunk,
         // and this rank's own pulls on the copy stream must have landed
-        int st = sync_stream(sv, sv->comm_stream);
-        if (!st && sv->copy_stream) st = sync_stream(sv, sv->copy_stream);
-        if (!st) st = sync_stream(sv, sv->stream);
+        int st = drain_all(sv);
         if (st) return st;
         if (sv->ce && !copy_engine)
             for (int b = 0; b < 2; b++)
@@ -1402,9 +1413,7 @@ int lyth_sv_set_chunk(lyth_sv *sv, uint64_t elements) {
     if (elements < 1024 || (elements & (elements - 1)) || elements > cap) return LYTH_E_UNSUPPORTED;
     if (!sv->plan) {
         DeviceGuard guard(sv);
-        int st = sync_stream(sv, sv->comm_stream);
-        if (!st && sv->copy_stream) st = sync_stream(sv, sv->copy_stream);
-        if (!st) st = sync_stream(sv, sv->stream);
+        const int st = drain_all(sv);
         if (st) return st;
     }
     sv->chunk = elements;
@@ -1442,9 +1451,8 @@ int lyth_sv_sync(lyth_sv *sv) {
     if (sv->plan) return LYTH_OK;
     DeviceGuard guard(sv);
     if (sv->comm_aborted) return LYTH_E_NCCL;
-    int st = sync_stream(sv, sv->comm_stream);
+    int st = drain_all(sv);
     if (st) return st;
-    if ((st = sync_stream(sv, sv->stream))) return st;
     if ((st = fused_take_device_error())) return st;  // a tile pass that gave up a bounded wait
     return sv->ce ? device_sv_error() : LYTH_OK;       // a transport flag wait that did
 }
@@ -1526,9 +1534,7 @@ int lyth_sv_set_pull_queues(lyth_sv *sv, int queues) {
     if (queues < 1 || queues > 2 + lyth_sv::kExtraQueues) return LYTH_E_UNSUPPORTED;
     if (!sv->plan) {
         DeviceGuard guard(sv);
-        int st = sync_stream(sv, sv->comm_stream);
-        if (!st && sv->copy_stream) st = sync_stream(sv, sv->copy_stream);
-        for (int i = 0; !st && i < lyth_sv::kExtraQueues; i++) st = sync_stream(sv, sv->xq[i]);
+        const int st = drain_all(sv);
         if (st) return st;
     }
     sv->pull_queues = queues;

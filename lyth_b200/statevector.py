@@ -121,7 +121,8 @@ class StateVector:
         check(lib.lyth_sv_set_diagonal(self._h, int(on)), "set_diagonal")
 
     def set_swap_batch(self, max_qubits: int) -> None:
-        """Most rank-bit qubits one swap-in brings in together (default 1 = one at a time)."""
+        """Most rank-bit qubits one swap-in brings in together (default 6; 1 = one at a time).
+        Collective: every rank sets the same value at the same point."""
         check(lib.lyth_sv_set_swap_batch(self._h, max_qubits), "set_swap_batch")
 
     def set_transport(self, copy_engine: bool) -> None:
