@@ -795,7 +795,7 @@ def ours(a, dist: Dist) -> None:
     tim = sv.timing()
     launches = dist.sum(float(sv.stats()["launches"] - launches0))
     st = sv.stats()
-    sv_transport = sv.transport() == "copy_engine"
+    sv_transport = sv.transport == "copy_engine"
     gates_timed = a.steps * per
     value = gates_timed / (ms * 1e-3)
 
