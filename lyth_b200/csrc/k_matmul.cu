@@ -7,7 +7,8 @@
 // tile of C and each thread an 8 x 8 register tile (two 4-row by two 4-column quarters, so the
 // shared-memory reads of a warp are broadcasts and 128-bit vectors), K moves in steps of 16
 // with the next step's operands prefetched into registers while this step's are used. A is
-// stored transposed in shared memory so both operands are read as vectors along the tile.
+// stored transposed (and XOR-swizzled, see sgemm_tile) in shared memory so both operands are read
+// as vectors along the tile.
 //
 // EXACT = true keeps the reference's contract bit for bit: every output is its own
 // accumulator, p strictly ascending, product rounded, then sum rounded. EXACT = false uses
@@ -48,11 +49,15 @@ LYTH_D void sgemm_tile(uint32_t n, uint32_t k, const float *a, const float *b, f
         for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
 
     float4 ra0 = ld4(ap0), ra1 = ld4(ap1), rb0 = ld4(bp0), rb1 = ld4(bp1);
+    // A is stored transposed with its rows XOR'ed by sw(p) = 8 * ((p >> 2) & 3): the 8 rows and
+    // 4 k-groups a warp stores then land in 32 distinct banks (unswizzled, the 4 k-groups of a
+    // row share a bank), and a 4-row group stays contiguous for the 128-bit reads below.
+    const int sw = 8 * ((a_col >> 2) & 3);
     auto stage = [&](int buf) {
-        As[buf][a_col + 0][a_row] = ra0.x; As[buf][a_col + 1][a_row] = ra0.y;
-        As[buf][a_col + 2][a_row] = ra0.z; As[buf][a_col + 3][a_row] = ra0.w;
-        As[buf][a_col + 0][a_row + 64] = ra1.x; As[buf][a_col + 1][a_row + 64] = ra1.y;
-        As[buf][a_col + 2][a_row + 64] = ra1.z; As[buf][a_col + 3][a_row + 64] = ra1.w;
+        As[buf][a_col + 0][a_row ^ sw] = ra0.x; As[buf][a_col + 1][a_row ^ sw] = ra0.y;
+        As[buf][a_col + 2][a_row ^ sw] = ra0.z; As[buf][a_col + 3][a_row ^ sw] = ra0.w;
+        As[buf][a_col + 0][(a_row + 64) ^ sw] = ra1.x; As[buf][a_col + 1][(a_row + 64) ^ sw] = ra1.y;
+        As[buf][a_col + 2][(a_row + 64) ^ sw] = ra1.z; As[buf][a_col + 3][(a_row + 64) ^ sw] = ra1.w;
         *reinterpret_cast<float4 *>(&Bs[buf][b_row][b_col]) = rb0;
         *reinterpret_cast<float4 *>(&Bs[buf][b_row + 8][b_col]) = rb1;
     };
@@ -69,8 +74,9 @@ LYTH_D void sgemm_tile(uint32_t n, uint32_t k, const float *a, const float *b, f
         }
 #pragma unroll
         for (int p = 0; p < kBK; p++) {
-            const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][p][ty * 4]);
-            const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][p][64 + ty * 4]);
+            const int swp = 8 * ((p >> 2) & 3);
+            const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][p][(ty * 4) ^ swp]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][p][(64 + ty * 4) ^ swp]);
             const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][p][tx * 4]);
             const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][p][64 + tx * 4]);
             const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
