@@ -21,3 +21,31 @@ def test_reference_arm_prints_one_contract_line():
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert "workload" in line["config"]
+
+
+def test_bench_uses_the_handle_api_as_declared():
+    # bench.py's GPU path cannot run here; at least every `sv.<name>` it uses must exist on the
+    # StateVector handle, called when it is a method and read when it is a property.
+    import ast
+    import inspect
+
+    from lyth_b200.statevector import StateVector
+
+    tree = ast.parse(open(os.path.join(ROOT, "bench.py")).read())
+    called = {n.func.attr for n in ast.walk(tree)
+              if isinstance(n, ast.Call) and isinstance(n.func, ast.Attribute)
+              and isinstance(n.func.value, ast.Name) and n.func.value.id == "sv"}
+    used = {n.attr for n in ast.walk(tree)
+            if isinstance(n, ast.Attribute) and isinstance(n.value, ast.Name) and n.value.id == "sv"}
+    assert used, "bench.py drives a handle named sv"
+    src = inspect.getsource(StateVector)
+    for name in used:
+        if not hasattr(StateVector, name):  # an attribute the constructor sets
+            assert f"self.{name} =" in src or f"self.{name}, " in src, name
+            assert name not in called, f"sv.{name} is data, called as a method"
+            continue
+        member = inspect.getattr_static(StateVector, name)
+        if name in called:
+            assert not isinstance(member, property), f"sv.{name} is a property, called as a method"
+        elif isinstance(member, property):
+            continue
