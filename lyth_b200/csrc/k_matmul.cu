@@ -106,9 +106,11 @@ LYTH_D bool tiles_fit(uint32_t m, uint32_t n, uint32_t k, const float *a, const 
            ((((uintptr_t)a) | ((uintptr_t)b) | ((uintptr_t)c)) & 15u) == 0;
 }
 
-// One block per tile of C, grid-stride over tiles (row-major tile order).
+// One block per tile of C, grid-stride over tiles (row-major tile order). Two blocks per SM (128
+// registers a thread: a few bytes of the next step's prefetch spill once per K step), so one
+// block's shared-memory waits overlap the other's FMAs.
 template <bool EXACT>
-__global__ void __launch_bounds__(256) sgemm_tiled_kernel(uint32_t m, uint32_t n, uint32_t k, const float *a,
+__global__ void __launch_bounds__(256, 2) sgemm_tiled_kernel(uint32_t m, uint32_t n, uint32_t k, const float *a,
                                                           const float *b, float *c) {
     __shared__ __align__(16) float As[2][kBK][kBM];
     __shared__ __align__(16) float Bs[2][kBK][kBN];
