@@ -113,7 +113,7 @@ def args_():
     ap.add_argument("--transport", choices=["copy_engine", "nccl"], default=None,
                     help="swap-in transport at N > 1 (default: the engine's)")
     ap.add_argument("--pull-queues", type=int, default=None,
-                    help="copy-engine queues per swap-in pull at N > 1 (1..8; default: the engine's)")
+                    help="copy-engine queues per swap-in pull at N > 1 (1..8; default: the engine's, one per partner slice)")
     ap.add_argument("--diagonal", type=int, choices=[0, 1], default=None,
                     help="diagonal rank-bit gates without an exchange (1) or like any other gate (0); "
                          "default: the engine's")
@@ -897,7 +897,8 @@ def ours(a, dist: Dist) -> None:
                        "settings": {"fusion": a.fuse or 13, "swap_batch": a.swap_batch or 6,
                                     "diagonal_rank_gates": "no exchange" if a.diagonal in (None, 1) else "exchange",
                                     "transport": ("copy_engine" if sv_transport else "nccl") if dist.world > 1
-                                    else None, "pull_queues": (a.pull_queues or 2) if dist.world > 1 else None}},
+                                    else None, "pull_queues": (a.pull_queues or "one per partner slice") if dist.world > 1
+                                    else None}},
             "parity": parity,
         }
         if cpu:

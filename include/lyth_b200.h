@@ -669,9 +669,11 @@ int lyth_sv_sync(lyth_sv *sv);
 /* The host-side deadline of the handle's NCCL waits, in milliseconds (>= 1; default 300000). No
  * counterpart in the reference (no multi-GPU code). */
 int lyth_sv_set_deadline(lyth_sv *sv, double ms);
-/* Copy-engine queues one swap-in pull is spread over (1..8; default 2: re and im on one queue
- * each): each component's slice from each partner is cut into this many pieces, issued
- * round-robin. No counterpart in the reference. */
+/* Copy-engine queues one swap-in pull is spread over (1..8): each component's slice from each
+ * partner is cut into this many pieces, issued round-robin. 0 (the default): every partner's re
+ * and im slices get a queue each, up to 8 -- 2 queues for a pairwise swap-in, 6 for a batched one
+ * among 4 ranks -- so the pulls from several partners run at once. Collective: every rank, same
+ * value. No counterpart in the reference. */
 int lyth_sv_set_pull_queues(lyth_sv *sv, int queues);
 /* Host-only check of the deadline logic with fake hooks, no device or NCCL (scenario 0: done after
  * 3 polls -> LYTH_OK; 1: async error -> LYTH_E_NCCL, one abort; 2: never done -> LYTH_E_TIMEOUT at

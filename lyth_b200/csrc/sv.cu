@@ -266,11 +266,12 @@ struct lyth_sv {
     cudaStream_t copy_stream = nullptr;  // second copy-engine queue (the im halves of the pulls)
     cudaEvent_t ev_pull = nullptr, ev_copied = nullptr;
     // Further copy-engine queues: a pull is cut into `pull_queues` pieces per component, issued
-    // round-robin over comm_stream, copy_stream and these (lyth_sv_set_pull_queues).
+    // round-robin over comm_stream, copy_stream and these (lyth_sv_set_pull_queues); 0 (the
+    // default) gives every partner's two slices a queue of their own, up to 8 queues.
     static constexpr int kExtraQueues = 6;
     cudaStream_t xq[kExtraQueues] = {};
     cudaEvent_t ev_xq[kExtraQueues] = {};
-    int pull_queues = 2;
+    int pull_queues = 0;
     cudaEvent_t ev_recv[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_start = nullptr;
     cudaEvent_t ev_packed[2] = {nullptr, nullptr};
     ncclComm_t comm = nullptr;
@@ -763,13 +764,16 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
             // engines in flight
             if ((st = wait_own(sv, sv->comm_stream, partner, 0, b, seq))) return st;
             if ((st = status_of(cudaEventRecord(sv->ev_pull, sv->comm_stream)))) return st;
-            // the queues: comm_stream, copy_stream, then the extra ones; Q pieces per component
-            const int Q = sv->pull_queues;
+            // the queues: comm_stream, copy_stream, then the extra ones. A set count cuts each
+            // component's slice into Q pieces; by default (0) every partner's two slices get a
+            // queue each, up to all of them, so the pulls from several partners run at once.
+            const int Q = sv->pull_queues > 0 ? sv->pull_queues
+                                               : (int)std::min<uint32_t>(2u * P, 2u + lyth_sv::kExtraQueues);
             cudaStream_t qs[2 + lyth_sv::kExtraQueues] = {sv->comm_stream, sv->copy_stream};
             for (int i = 0; i < lyth_sv::kExtraQueues; i++) qs[2 + i] = sv->xq[i];
             for (int i = 1; i < Q; i++)
                 if ((st = status_of(cudaStreamWaitEvent(qs[i], sv->ev_pull, 0)))) return st;
-            const uint64_t piece = (C + (uint64_t)Q - 1) / (uint64_t)Q;
+            const uint64_t piece = sv->pull_queues > 0 ? (C + (uint64_t)Q - 1) / (uint64_t)Q : C;
             int next = 0;
             for (uint32_t y = 0; y < P; y++) {
                 const uint64_t off = (uint64_t)y * C, src = (uint64_t)myslice[y] * C;
@@ -1531,7 +1535,7 @@ int lyth_sv_plan_clear(lyth_sv *sv) {
 
 int lyth_sv_set_pull_queues(lyth_sv *sv, int queues) {
     if (!sv) return LYTH_E_INVALID;
-    if (queues < 1 || queues > 2 + lyth_sv::kExtraQueues) return LYTH_E_UNSUPPORTED;
+    if (queues < 0 || queues > 2 + lyth_sv::kExtraQueues) return LYTH_E_UNSUPPORTED;
     if (!sv->plan) {
         DeviceGuard guard(sv);
         const int st = drain_all(sv);

@@ -257,3 +257,15 @@ def test_deadline_setting_is_checked():
     with Plan(20, 0, 2) as p:
         assert lb.lib.lyth_sv_set_deadline(p._h, 0.5) == lb.E_UNSUPPORTED
         assert lb.lib.lyth_sv_set_deadline(p._h, 2000.0) == lb.OK
+
+
+def test_pull_queue_setting_range():
+    # 0 = one queue per partner slice (the default), 1..8 = that many pieces and queues
+    import lyth_b200 as lb
+    from lyth_b200.statevector import Plan
+
+    with Plan(12, 0, 4) as p:
+        for q in (0, 1, 5, 8):
+            assert lb.lib.lyth_sv_set_pull_queues(p._h, q) == 0
+        for q in (-1, 9):
+            assert lb.lib.lyth_sv_set_pull_queues(p._h, q) == lb.E_UNSUPPORTED
