@@ -36,7 +36,7 @@ int launch_permute(uint64_t len, const uint32_t *src, const uint32_t *dst, int k
                    cudaStream_t s);
 // Whether launch_permute takes these bits at this size (host only, no launch).
 bool permute_supported(uint64_t len, const uint32_t *src, int k);
-// LYTH_E_TIMEOUT (and clears the flag) if a staged pass gave up a bounded wait; else LYTH_OK.
+// LYTH_E_TIMEOUT (and clears the flag) if a tile pass gave up a bounded wait; else LYTH_OK.
 int fused_take_device_error();
 
 }  // namespace lyth

@@ -881,7 +881,7 @@ int physical_swap(lyth_sv *sv, uint32_t p1, uint32_t p2) {
 }
 
 // Move local bits src[j] -> dst[j] (j < k <= 6, dst a permutation of src) in one in-place pass
-// and update the map. LYTH_E_UNSUPPORTED: the state is below the staged pass's size.
+// and update the map. LYTH_E_UNSUPPORTED: the state is below the tile pass's size.
 int permute_local(lyth_sv *sv, const std::vector<uint32_t> &src, const std::vector<uint32_t> &dst) {
     const int k = (int)src.size();
     if (sv->plan) {
@@ -955,7 +955,7 @@ int normalize(lyth_sv *sv) {
     }
     if (!st) st = flush();
     if (st && st != LYTH_E_UNSUPPORTED) return st;
-    // below the staged pass's size: one swap pass per transposition
+    // below the tile pass's size: one swap pass per transposition
     for (uint32_t q = 0; q < L; q++)
         if (sv->pos[q] != q && (st = physical_swap(sv, q, sv->pos[q]))) return st;
     return LYTH_OK;

@@ -293,7 +293,7 @@ def test_plan_handle_needs_no_gpu():
 
 
 def test_readout_permutation_passes_replay_bit_exact():
-    # 16 qubits on one rank: the read-out undoes the qubit map with permutation passes (the staged
+    # 16 qubits on one rank: the read-out undoes the qubit map with permutation passes (the tile
     # pass's size); replayed with the oracle's gates and numpy, the result is the oracle's.
     import sys
 

@@ -4,7 +4,7 @@ bit for bit against the host evaluator applying that layer's gates unfused, in o
 same input (lyth-circuit's execute, crates/lyth-circuit/src/lib.rs:327-371; the fusion claim of
 crates/lyth-circuit/tests/fusion.rs:53-92 at full size).
 
-The engine runs the whole circuit as the benchmark does (fused, staged passes, SWAPs as
+The engine runs the whole circuit as the benchmark does (fused tile passes, SWAPs as
 relabels); the state is read out (qubit map undone) before layer 1, after layer 1, before layer
 20 and after layer 20. The evaluator applies layer 1 to the first read-out and layer 20 to the
 third, in place on all host cores. Host memory: 16 GiB at the peak; host time: about two
