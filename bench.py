@@ -110,7 +110,7 @@ def args_():
     ap.add_argument("--fuse", type=int, default=None, help="max qubits per fused pass (1..13; default: the engine's)")
     ap.add_argument("--swap-batch", type=int, default=None,
                     help="most rank-bit qubits per swap-in (1..6; default: the engine's)")
-    ap.add_argument("--transport", choices=["copy_engine", "nccl"], default=None,
+    ap.add_argument("--transport", choices=["copy_engine", "peer_load", "mixed", "nccl"], default=None,
                     help="swap-in transport at N > 1 (default: the engine's)")
     ap.add_argument("--pull-queues", type=int, default=None,
                     help="copy-engine queues per swap-in pull at N > 1 (1..8; default: the engine's, one per partner slice)")
@@ -686,7 +686,7 @@ def configure(sv, a, dist: Dist) -> None:
     if a.diagonal is not None:
         sv.set_diagonal(bool(a.diagonal))
     if a.transport and dist.world > 1:
-        sv.set_transport(a.transport == "copy_engine")
+        sv.set_transport(a.transport)
     if a.pull_queues and dist.world > 1:
         lb.check(lb.lib.lyth_sv_set_pull_queues(sv._h, a.pull_queues), "set_pull_queues")
 
@@ -795,7 +795,7 @@ def ours(a, dist: Dist) -> None:
     tim = sv.timing()
     launches = dist.sum(float(sv.stats()["launches"] - launches0))
     st = sv.stats()
-    sv_transport = sv.transport == "copy_engine"
+    sv_transport = sv.transport
     gates_timed = a.steps * per
     value = gates_timed / (ms * 1e-3)
 
@@ -896,7 +896,7 @@ def ours(a, dist: Dist) -> None:
             "engine": {"passes": st["passes"], "exchanges": st["exchanges"], "bytes_sent": st["bytes_sent"],
                        "settings": {"fusion": a.fuse or 13, "swap_batch": a.swap_batch or 6,
                                     "diagonal_rank_gates": "no exchange" if a.diagonal in (None, 1) else "exchange",
-                                    "transport": ("copy_engine" if sv_transport else "nccl") if dist.world > 1
+                                    "transport": sv_transport if dist.world > 1
                                     else None, "pull_queues": (a.pull_queues or "one per partner slice") if dist.world > 1
                                     else None}},
             "parity": parity,

@@ -186,6 +186,64 @@ __global__ void __launch_bounds__(1024) unpack_multi_kernel(uint64_t count, uint
     }
 }
 
+// A 128-bit load of a partner's memory through its CUDA IPC mapping (peer access over NVLink):
+// cached at L2 level only, so no L1 line of an earlier chunk in the same slot is ever read.
+LYTH_D float4 ld_peer4(const float *p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+LYTH_D float ld_peer(const float *p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+// Where partner y's packed slice for this rank starts in that partner's send slot (both
+// components), for the peer-load transport.
+struct PeerSrc {
+    const float *re[64];
+    const float *im[64];
+};
+// The peer-load transport's pull, fused with the unpack: block row y reads partner y's packed
+// slice straight out of the partner's memory (plain loads issued by the SMs: no copy engine, no
+// TMA, no multicast) and stores it into this rank's subset pattern[y], the positions whose own
+// amplitudes that partner takes from this rank's send slot -- packed there before this runs. No
+// receive buffer, and no separate unpack pass over HBM. Two groups of four per thread per trip
+// keep four 16-byte peer loads in flight.
+__global__ void __launch_bounds__(512) pull_unpack_kernel(uint64_t count, uint64_t k0, const __grid_constant__ MultiPat mp,
+                                                          const __grid_constant__ PeerSrc src, float *re, float *im) {
+    const uint32_t y = blockIdx.y, pat = mp.pattern[y];
+    const float *pre = src.re[y], *pim = src.im[y];
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t nth = (uint64_t)gridDim.x * blockDim.x;
+    if (mp.vs[0] >= 2 && (count & 3) == 0 && (k0 & 3) == 0) {
+        const uint64_t groups = count >> 2;
+        uint64_t g = tid;
+        for (; g + nth < groups; g += 2 * nth) {
+            const uint64_t h = g + nth;
+            const float4 a = ld_peer4(pre + 4 * g), b = ld_peer4(pim + 4 * g);
+            const float4 c = ld_peer4(pre + 4 * h), d = ld_peer4(pim + 4 * h);
+            const uint64_t i = insert_pattern(k0 + 4 * g, mp, pat), j = insert_pattern(k0 + 4 * h, mp, pat);
+            st4(re + i, a);
+            st4(im + i, b);
+            st4(re + j, c);
+            st4(im + j, d);
+        }
+        if (g < groups) {
+            const float4 a = ld_peer4(pre + 4 * g), b = ld_peer4(pim + 4 * g);
+            const uint64_t i = insert_pattern(k0 + 4 * g, mp, pat);
+            st4(re + i, a);
+            st4(im + i, b);
+        }
+        return;
+    }
+    for (uint64_t e = tid; e < count; e += nth) {
+        const uint64_t i = insert_pattern(k0 + e, mp, pat);
+        re[i] = ld_peer(pre + e);
+        im[i] = ld_peer(pim + e);
+    }
+}
+
 // Cross-GPU sequence flags of the copy-engine transport. Every rank polls only its own flag block
 // and peers signal it by remote stores into it, so every remote write is awaited by the rank it
 // targets before that rank frees anything.
@@ -311,6 +369,11 @@ struct lyth_sv {
     // this rank into its send slot b; [kPulledAt + r * 2 + b] = last chunk rank r pulled from this
     // rank's send slot b.
     bool ce = false;
+    // With `ce`: which swap-ins pull with SM-issued peer loads fused with the unpack
+    // (pull_unpack_kernel) instead of copy-engine copies into the receive chunks. 0 = none
+    // (lyth_sv_set_transport 1), 1 = all (2), 2 = the batched ones, with several partners (3).
+    // Same flags, same send slots, same sequence numbers, so the two kinds mix freely.
+    int peer_load = 0;
     uint64_t *flags = nullptr;
     std::vector<float *> peer_sre[2], peer_sim[2];
     std::vector<uint64_t *> peer_flags;  // every rank's flag block (own included)
@@ -732,6 +795,10 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
     unsigned gx = stream_grid(C / 4 + 1, 1024);
     if (gx * P > gx_cap) gx = gx_cap / P > 0 ? gx_cap / P : 1;
     const dim3 grid(gx, P);
+    // the peer-load pull: about two 512-thread blocks per SM over all partners, next to the pack
+    const bool pl = sv->ce && (sv->peer_load == 1 || (sv->peer_load == 2 && P > 1));
+    const unsigned pgx = std::max(1u, (unsigned)device_sms() * 2u / P);
+    const dim3 pgrid(std::min<unsigned>(pgx, stream_grid(C / 8 + 1, 512)), P);
     const int mk = mark_begin(sv, LYTH_SV_T_SWAP);
     int st = status_of(cudaEventRecord(sv->ev_start, sv->stream));
     if (st) return st;
@@ -758,8 +825,21 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
         const int b = (int)(c & 1);
         const uint64_t seq = seq0 + c + 1;
         // receive slot b is free once unpack(c - 2) has drained it
-        if (c >= 2 && (st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_done[b], 0)))) return st;
-        if (sv->ce) {
+        if (c >= 2 && !pl && (st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_done[b], 0)))) return st;
+        if (pl) {
+            // the pull overwrites the positions pack(c) read on the compute stream
+            if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_packed[b], 0)))) return st;
+            if ((st = wait_own(sv, sv->comm_stream, partner, 0, b, seq))) return st;
+            PeerSrc ps{};
+            for (uint32_t y = 0; y < P; y++) {
+                ps.re[y] = sv->peer_sre[b][partner[y]] + (uint64_t)myslice[y] * C;
+                ps.im[y] = sv->peer_sim[b][partner[y]] + (uint64_t)myslice[y] * C;
+            }
+            pull_unpack_kernel<<<pgrid, 512, 0, sv->comm_stream>>>(C, c * C, mp, ps, sv->re, sv->im);
+            sv->launches++;
+            if ((st = last_launch_status())) return st;
+            if ((st = put_peers(sv, sv->comm_stream, partner, kPulledAt, b, seq))) return st;
+        } else if (sv->ce) {
             // re halves on the communication stream, im halves on a second stream: two copy
             // engines in flight
             if ((st = wait_own(sv, sv->comm_stream, partner, 0, b, seq))) return st;
@@ -811,10 +891,12 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
         sv->bytes_sent += 2 * P * C * sizeof(float);
         if (c + 1 < nchunks && (st = pack(c + 1))) return st;
         if ((st = status_of(cudaStreamWaitEvent(sv->stream, sv->ev_recv[b], 0)))) return st;
-        unpack_multi_kernel<<<grid, 1024, 0, sv->stream>>>(C, c * C, mp, sv->re, sv->im, sv->rre[b], sv->rim[b]);
-        sv->launches++;
-        if ((st = last_launch_status())) return st;
-        if ((st = status_of(cudaEventRecord(sv->ev_done[b], sv->stream)))) return st;
+        if (!pl) {
+            unpack_multi_kernel<<<grid, 1024, 0, sv->stream>>>(C, c * C, mp, sv->re, sv->im, sv->rre[b], sv->rim[b]);
+            sv->launches++;
+            if ((st = last_launch_status())) return st;
+            if ((st = status_of(cudaEventRecord(sv->ev_done[b], sv->stream)))) return st;
+        }
     }
     sv->xseq = seq0 + nchunks;
     mark_end(sv, mk);
@@ -1079,6 +1161,7 @@ void close_ipc(lyth_sv *sv) {
     for (int b = 0; b < 2; b++) { sv->peer_sre[b].clear(); sv->peer_sim[b].clear(); }
     sv->peer_flags.clear();
     sv->ce = false;
+    sv->peer_load = 0;
 }
 
 int setup_ce(lyth_sv *sv) {
@@ -1393,6 +1476,7 @@ int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count) {
 
 int lyth_sv_set_transport(lyth_sv *sv, int copy_engine) {
     if (!sv) return LYTH_E_INVALID;
+    if (copy_engine < 0 || copy_engine > 3) return LYTH_E_INVALID;
     if (copy_engine && sv->peer_flags.empty()) return LYTH_E_UNSUPPORTED;
     if (!sv->plan) {
         DeviceGuard guard(sv);
@@ -1406,10 +1490,11 @@ int lyth_sv_set_transport(lyth_sv *sv, int copy_engine) {
         if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
     }
     sv->ce = copy_engine != 0;
+    sv->peer_load = copy_engine == 2 ? 1 : copy_engine == 3 ? 2 : 0;
     return LYTH_OK;
 }
 
-int lyth_sv_transport(const lyth_sv *sv) { return sv && sv->ce ? 1 : 0; }
+int lyth_sv_transport(const lyth_sv *sv) { return sv && sv->ce ? 1 + sv->peer_load : 0; }
 
 int lyth_sv_set_chunk(lyth_sv *sv, uint64_t elements) {
     if (!sv) return LYTH_E_INVALID;

@@ -125,10 +125,19 @@ class StateVector:
         Collective: every rank sets the same value at the same point."""
         check(lib.lyth_sv_set_swap_batch(self._h, max_qubits), "set_swap_batch")
 
-    def set_transport(self, copy_engine: bool) -> None:
-        """Swap-in transport: copy engines over CUDA IPC (True, the default when available) or
-        NCCL (False). Collective: every rank sets the same value at the same point."""
-        check(lib.lyth_sv_set_transport(self._h, int(copy_engine)), "set_transport")
+    TRANSPORTS = ("nccl", "copy_engine", "peer_load", "mixed")
+
+    def set_transport(self, kind) -> None:
+        """Swap-in transport: "copy_engine" (copy engines over CUDA IPC, the default when every
+        rank mapped every peer), "peer_load" (the same mappings, the SMs load the partners' packed
+        chunks straight into the shard), "mixed" (copy engines for pairwise swap-ins, peer loads
+        for batched ones) or "nccl". True / False mean "copy_engine" / "nccl".
+        Collective: every rank sets the same value at the same point."""
+        if isinstance(kind, bool):
+            kind = "copy_engine" if kind else "nccl"
+        if kind not in self.TRANSPORTS:
+            raise ValueError(f"transport {kind!r}: one of {self.TRANSPORTS}")
+        check(lib.lyth_sv_set_transport(self._h, self.TRANSPORTS.index(kind)), "set_transport")
 
     def set_chunk(self, elements: int) -> None:
         """Exchange pipeline chunk, amplitudes per component (power of two >= 1024). Collective."""
@@ -136,7 +145,7 @@ class StateVector:
 
     @property
     def transport(self) -> str:
-        return "copy_engine" if lib.lyth_sv_transport(self._h) else "nccl"
+        return self.TRANSPORTS[lib.lyth_sv_transport(self._h)]
 
     def timing(self) -> dict:
         """{class: (count, total ms)}: 'u' (1-qubit passes), 'cu' (2-qubit), 'exchange',

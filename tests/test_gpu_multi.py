@@ -91,7 +91,7 @@ def _run_ranks(nranks, q, case, remap, batch, tmp_path, ce=True, chunk=None, que
     for r, p in enumerate(procs):
         assert p.exitcode == 0, f"rank {r} exit {p.exitcode}"
         ok, ex, sent, same_plan, transport = open(tmp_path / f"r{r}.txt").read().split()
-        assert transport == ("copy_engine" if ce else "nccl")
+        assert transport == (ce if isinstance(ce, str) else "copy_engine" if ce else "nccl")
         assert ok == "1", f"rank {r}: shard differs from the evaluator"
         assert same_plan == "1", f"rank {r}: the plan handle's counters differ from the engine's"
         assert int(ex) > 0, "the circuit must exercise the exchange"
@@ -122,6 +122,15 @@ def test_two_ranks_pull_queues(queues, tmp_path):
 
 
 @pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("chunk", [None, 1024])
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_two_ranks_peer_load_transport(case, chunk, tmp_path):
+    # the SMs pull the partner's packed chunks and store them into the shard (no receive buffer);
+    # with 1024-amplitude chunks the send slots are reused many times within one exchange
+    _run_ranks(2, 18, case, True, 6, tmp_path, ce="peer_load", chunk=chunk)
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("case", [0, 2])
 def test_two_ranks_nccl_transport(case, tmp_path):
     _run_ranks(2, 18, case, True, 6, tmp_path, ce=False)
@@ -142,6 +151,15 @@ def test_four_ranks_many_chunks(batch, tmp_path):
 
 
 @pytest.mark.skipif(_ngpus() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("kind", ["peer_load", "mixed"])
+@pytest.mark.parametrize("batch", [6, 1])
+def test_four_ranks_peer_load_transport(batch, kind, tmp_path):
+    # batched swap-ins pull from 3 partners at once with SM loads, in short chunks; "mixed" takes
+    # the copy engines for the pairwise ones in between
+    _run_ranks(4, 19, 0, True, batch, tmp_path, ce=kind, chunk=1024)
+
+
+@pytest.mark.skipif(_ngpus() < 4, reason="needs 4 GPUs")
 def test_four_ranks_nccl_transport(tmp_path):
     _run_ranks(4, 19, 0, True, 6, tmp_path, ce=False)
 
@@ -151,3 +169,9 @@ def test_four_ranks_nccl_transport(tmp_path):
 def test_eight_ranks_bit_exact(case, tmp_path):
     # three rank bits: batched swap-ins among up to 8 ranks over the copy engines
     _run_ranks(8, 20, case, True, 6, tmp_path)
+
+
+@pytest.mark.skipif(_ngpus() < 8, reason="needs 8 GPUs")
+@pytest.mark.parametrize("kind", ["peer_load", "mixed"])
+def test_eight_ranks_peer_load_transport(kind, tmp_path):
+    _run_ranks(8, 20, 0, True, 6, tmp_path, ce=kind, chunk=1024)
