@@ -128,10 +128,10 @@ class StateVector:
     TRANSPORTS = ("nccl", "copy_engine", "peer_load", "mixed")
 
     def set_transport(self, kind) -> None:
-        """Swap-in transport: "copy_engine" (copy engines over CUDA IPC, the default when every
-        rank mapped every peer), "peer_load" (the same mappings, the SMs load the partners' packed
-        chunks straight into the shard), "mixed" (copy engines for pairwise swap-ins, peer loads
-        for batched ones) or "nccl". True / False mean "copy_engine" / "nccl".
+        """Swap-in transport: "copy_engine" (copy engines over CUDA IPC), "peer_load" (the same
+        mappings, the SMs load the partners' packed chunks straight into the shard), "mixed" (copy
+        engines for pairwise swap-ins, peer loads for batched ones; the default when every rank
+        mapped every peer) or "nccl". True / False mean "copy_engine" / "nccl".
         Collective: every rank sets the same value at the same point."""
         if isinstance(kind, bool):
             kind = "copy_engine" if kind else "nccl"
