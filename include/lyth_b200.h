@@ -725,9 +725,10 @@ int lyth_sv_set_swap_batch(lyth_sv *sv, int max_qubits);
  * flags; the SMs read the partners' packed chunks and store them straight into the shard, the
  * unpack fused into the pull), 3 = mixed (copy engines for a pairwise swap-in, peer loads for a
  * batched one with several partners; the default when every rank could map every peer),
- * 0 = NCCL send / recv. 1-3 need the IPC mappings
- * (LYTH_E_UNSUPPORTED without them); other values LYTH_E_INVALID. Collective: every rank sets the
- * same value at the same point. lyth_sv_transport reports the one in use (0-3). */
+ * 4 = peer stores (the SMs store this rank's packed chunks straight into the partners' shards,
+ * once each partner has packed the positions they go to), 0 = NCCL send / recv. 1-4 need the IPC
+ * mappings (LYTH_E_UNSUPPORTED without them); other values LYTH_E_INVALID. Collective: every rank
+ * sets the same value at the same point. lyth_sv_transport reports the one in use (0-4). */
 int lyth_sv_set_transport(lyth_sv *sv, int kind);
 /* The exchanges' pipeline chunk in amplitudes per component (a power of two from 1024 up to the
  * allocated 2^28, or the shard if smaller; the default is the largest). Collective. Smaller

@@ -244,6 +244,53 @@ __global__ void __launch_bounds__(512) pull_unpack_kernel(uint64_t count, uint64
     }
 }
 
+// Partner y's shard (both components), for the push form.
+struct PeerDst {
+    float *re[64];
+    float *im[64];
+};
+// The push form of a swap-in: block row y reads this rank's packed slice y (local, contiguous)
+// and stores it into partner y's shard at the positions of subset `pat` there -- the subset whose
+// own amplitudes that partner packed for this rank before this runs (plain SM stores over NVLink
+// through the CUDA IPC mapping: no copy engine, no TMA, no multicast). Every partner takes this
+// rank's data at the same pattern. Two groups of four per thread per trip.
+__global__ void __launch_bounds__(512) push_kernel(uint64_t count, uint64_t k0, const __grid_constant__ MultiPat mp,
+                                                   uint32_t pat, const float *sre, const float *sim,
+                                                   const __grid_constant__ PeerDst dst) {
+    const uint32_t y = blockIdx.y;
+    sre += (uint64_t)y * count;
+    sim += (uint64_t)y * count;
+    float *dre = dst.re[y], *dim = dst.im[y];
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t nth = (uint64_t)gridDim.x * blockDim.x;
+    if (mp.vs[0] >= 2 && (count & 3) == 0 && (k0 & 3) == 0) {
+        const uint64_t groups = count >> 2;
+        uint64_t g = tid;
+        for (; g + nth < groups; g += 2 * nth) {
+            const uint64_t h = g + nth;
+            const float4 a = ld_stream4(sre + 4 * g), b = ld_stream4(sim + 4 * g);
+            const float4 c = ld_stream4(sre + 4 * h), d = ld_stream4(sim + 4 * h);
+            const uint64_t i = insert_pattern(k0 + 4 * g, mp, pat), j = insert_pattern(k0 + 4 * h, mp, pat);
+            st4(dre + i, a);
+            st4(dim + i, b);
+            st4(dre + j, c);
+            st4(dim + j, d);
+        }
+        if (g < groups) {
+            const float4 a = ld_stream4(sre + 4 * g), b = ld_stream4(sim + 4 * g);
+            const uint64_t i = insert_pattern(k0 + 4 * g, mp, pat);
+            st4(dre + i, a);
+            st4(dim + i, b);
+        }
+        return;
+    }
+    for (uint64_t e = tid; e < count; e += nth) {
+        const uint64_t i = insert_pattern(k0 + e, mp, pat);
+        dre[i] = sre[e];
+        dim[i] = sim[e];
+    }
+}
+
 // Cross-GPU sequence flags of the copy-engine transport. Every rank polls only its own flag block
 // and peers signal it by remote stores into it, so every remote write is awaited by the rank it
 // targets before that rank frees anything.
@@ -369,14 +416,17 @@ struct lyth_sv {
     // this rank into its send slot b; [kPulledAt + r * 2 + b] = last chunk rank r pulled from this
     // rank's send slot b.
     bool ce = false;
-    // With `ce`: which swap-ins pull with SM-issued peer loads fused with the unpack
-    // (pull_unpack_kernel) instead of copy-engine copies into the receive chunks. 0 = none
-    // (lyth_sv_set_transport 1), 1 = all (2), 2 = the batched ones, with several partners (3).
-    // Same flags, same send slots, same sequence numbers, so the two kinds mix freely.
-    int peer_load = 0;
+    // With `ce`, how swap-ins move (lyth_sv_set_transport 1-4): kPeerNone -- copy-engine pulls
+    // into the receive chunks; kPeerLoad -- SM-issued peer loads fused with the unpack
+    // (pull_unpack_kernel); kPeerMixed -- copy engines pairwise, peer loads for batched swap-ins
+    // (several partners); kPeerStore -- SM stores of this rank's packed chunks straight into the
+    // partners' shards (push_kernel). Every form leaves the flags and send slots as the next one
+    // expects, so they mix freely.
+    int peer_mode = 0;
     uint64_t *flags = nullptr;
     std::vector<float *> peer_sre[2], peer_sim[2];
     std::vector<uint64_t *> peer_flags;  // every rank's flag block (own included)
+    std::vector<float *> peer_re, peer_im;  // every rank's shard (the push form's destinations)
     std::vector<void *> ipc_opened;
     uint64_t xseq = 0;                       // chunk sequence number, identical on every rank
     uint64_t slot_seq[2] = {0, 0};           // last chunk packed into send slot b
@@ -697,7 +747,10 @@ int add_local(lyth_sv *sv, int c, uint32_t t, const U8 &m) {
     return LYTH_OK;
 }
 
-constexpr int kFlagRanks = 64, kPulledAt = 2 * kFlagRanks, kFlagWords = 4 * kFlagRanks;
+// [kLandedAt + r * 2 + b]: last chunk rank r stored into this rank's shard from its send slot b
+// (the push form).
+constexpr int kFlagRanks = 64, kPulledAt = 2 * kFlagRanks, kLandedAt = 4 * kFlagRanks, kFlagWords = 6 * kFlagRanks;
+constexpr int kPeerNone = 0, kPeerLoad = 1, kPeerMixed = 2, kPeerStore = 3;
 
 // Wait on `stream` until this rank's own flags [base + r * 2 + b] for the listed ranks are >= target.
 int wait_own(lyth_sv *sv, cudaStream_t stream, const std::vector<int> &ranks, int base, int b, uint64_t target) {
@@ -795,8 +848,14 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
     unsigned gx = stream_grid(C / 4 + 1, 1024);
     if (gx * P > gx_cap) gx = gx_cap / P > 0 ? gx_cap / P : 1;
     const dim3 grid(gx, P);
-    // the peer-load pull: about two 512-thread blocks per SM over all partners, next to the pack
-    const bool pl = sv->ce && (sv->peer_load == 1 || (sv->peer_load == 2 && P > 1));
+    const bool pl = sv->ce && (sv->peer_mode == kPeerLoad || (sv->peer_mode == kPeerMixed && P > 1));
+    // the push form: this rank stores its packed slices into the partners' shards once their own
+    // pack of the chunk has read the positions it overwrites
+    const bool ps = sv->ce && sv->peer_mode == kPeerStore;
+    uint32_t patself = 0;  // the subset pattern this rank's data takes in every partner's shard
+    for (uint32_t s = 0; s < k; s++) patself |= ((qself >> order[s]) & 1u) << s;
+    // the peer-load pull and the push: about two 512-thread blocks per SM over all partners, next
+    // to the pack
     const unsigned pgx = std::max(1u, (unsigned)device_sms() * 2u / P);
     const dim3 pgrid(std::min<unsigned>(pgx, stream_grid(C / 8 + 1, 512)), P);
     const int mk = mark_begin(sv, LYTH_SV_T_SWAP);
@@ -810,13 +869,17 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
         // the send slot is re-packed once every rank that pulls its last chunk has done so
         if (sv->ce && sv->slot_seq[b] && (r = wait_own(sv, sv->stream, sv->slot_partners[b], kPulledAt, b, sv->slot_seq[b])))
             return r;
+        // (the push form's own push of chunk c - 2 from this slot is ordered before this on the
+        // compute stream: see the wait on ev_recv below)
         pack_multi_kernel<<<grid, 1024, 0, sv->stream>>>(C, c * C, mp, sv->re, sv->im, sv->sre[b], sv->sim[b]);
         sv->launches++;
         if ((r = last_launch_status())) return r;
         if (sv->ce) {
+            // "packed": the slot holds chunk c, and this rank's chunk-c positions are free
             if ((r = put_peers(sv, sv->stream, partner, 0, b, seq0 + c + 1))) return r;
-            sv->slot_seq[b] = seq0 + c + 1;
-            sv->slot_partners[b] = partner;
+            sv->slot_seq[b] = ps ? 0 : seq0 + c + 1;  // nobody pulls a pushed slot
+            if (ps) sv->slot_partners[b].clear();
+            else sv->slot_partners[b] = partner;
         }
         return status_of(cudaEventRecord(sv->ev_packed[b], sv->stream));
     };
@@ -825,17 +888,31 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
         const int b = (int)(c & 1);
         const uint64_t seq = seq0 + c + 1;
         // receive slot b is free once unpack(c - 2) has drained it
-        if (c >= 2 && !pl && (st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_done[b], 0)))) return st;
-        if (pl) {
+        if (c >= 2 && !pl && !ps && (st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_done[b], 0)))) return st;
+        if (ps) {
+            // this rank's slices of chunk c are packed, and every partner has packed (read) the
+            // positions they go to
+            if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_packed[b], 0)))) return st;
+            if ((st = wait_own(sv, sv->comm_stream, partner, 0, b, seq))) return st;
+            PeerDst pd{};
+            for (uint32_t y = 0; y < P; y++) {
+                pd.re[y] = sv->peer_re[partner[y]];
+                pd.im[y] = sv->peer_im[partner[y]];
+            }
+            push_kernel<<<pgrid, 512, 0, sv->comm_stream>>>(C, c * C, mp, patself, sv->sre[b], sv->sim[b], pd);
+            sv->launches++;
+            if ((st = last_launch_status())) return st;
+            if ((st = put_peers(sv, sv->comm_stream, partner, kLandedAt, b, seq))) return st;
+        } else if (pl) {
             // the pull overwrites the positions pack(c) read on the compute stream
             if ((st = status_of(cudaStreamWaitEvent(sv->comm_stream, sv->ev_packed[b], 0)))) return st;
             if ((st = wait_own(sv, sv->comm_stream, partner, 0, b, seq))) return st;
-            PeerSrc ps{};
+            PeerSrc srcs{};
             for (uint32_t y = 0; y < P; y++) {
-                ps.re[y] = sv->peer_sre[b][partner[y]] + (uint64_t)myslice[y] * C;
-                ps.im[y] = sv->peer_sim[b][partner[y]] + (uint64_t)myslice[y] * C;
+                srcs.re[y] = sv->peer_sre[b][partner[y]] + (uint64_t)myslice[y] * C;
+                srcs.im[y] = sv->peer_sim[b][partner[y]] + (uint64_t)myslice[y] * C;
             }
-            pull_unpack_kernel<<<pgrid, 512, 0, sv->comm_stream>>>(C, c * C, mp, ps, sv->re, sv->im);
+            pull_unpack_kernel<<<pgrid, 512, 0, sv->comm_stream>>>(C, c * C, mp, srcs, sv->re, sv->im);
             sv->launches++;
             if ((st = last_launch_status())) return st;
             if ((st = put_peers(sv, sv->comm_stream, partner, kPulledAt, b, seq))) return st;
@@ -891,12 +968,19 @@ int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::
         sv->bytes_sent += 2 * P * C * sizeof(float);
         if (c + 1 < nchunks && (st = pack(c + 1))) return st;
         if ((st = status_of(cudaStreamWaitEvent(sv->stream, sv->ev_recv[b], 0)))) return st;
-        if (!pl) {
+        if (!pl && !ps) {
             unpack_multi_kernel<<<grid, 1024, 0, sv->stream>>>(C, c * C, mp, sv->re, sv->im, sv->rre[b], sv->rim[b]);
             sv->launches++;
             if ((st = last_launch_status())) return st;
             if ((st = status_of(cudaEventRecord(sv->ev_done[b], sv->stream)))) return st;
         }
+    }
+    if (ps) {
+        // every partner's stores into this shard have landed: a partner raises "landed" for its
+        // chunks in order, so the last chunk of each slot covers the earlier ones
+        const int bl = (int)((nchunks - 1) & 1);
+        if ((st = wait_own(sv, sv->stream, partner, kLandedAt, bl, seq0 + nchunks))) return st;
+        if (nchunks >= 2 && (st = wait_own(sv, sv->stream, partner, kLandedAt, bl ^ 1, seq0 + nchunks - 1))) return st;
     }
     sv->xseq = seq0 + nchunks;
     mark_end(sv, mk);
@@ -1152,7 +1236,7 @@ int apply_one(lyth_sv *sv, const lyth_gate *gates, uint64_t count, uint64_t i) {
 // and flag block through CUDA IPC. Every rank ends with the same `ce` (false: NCCL for swaps).
 struct IpcRec {
     int32_t ok, pad;
-    cudaIpcMemHandle_t h[5];  // sre[0], sre[1], sim[0], sim[1], flags
+    cudaIpcMemHandle_t h[7];  // sre[0], sre[1], sim[0], sim[1], flags, re, im
 };
 
 void close_ipc(lyth_sv *sv) {
@@ -1160,8 +1244,10 @@ void close_ipc(lyth_sv *sv) {
     sv->ipc_opened.clear();
     for (int b = 0; b < 2; b++) { sv->peer_sre[b].clear(); sv->peer_sim[b].clear(); }
     sv->peer_flags.clear();
+    sv->peer_re.clear();
+    sv->peer_im.clear();
     sv->ce = false;
-    sv->peer_load = 0;
+    sv->peer_mode = kPeerNone;
 }
 
 int setup_ce(lyth_sv *sv) {
@@ -1174,8 +1260,8 @@ int setup_ce(lyth_sv *sv) {
     } else if (cudaMemset(sv->flags, 0, kFlagWords * sizeof(uint64_t)) != cudaSuccess) {
         mine.ok = 0;
     }
-    void *exported[5] = {sv->sre[0], sv->sre[1], sv->sim[0], sv->sim[1], sv->flags};
-    for (int i = 0; i < 5 && mine.ok; i++)
+    void *exported[7] = {sv->sre[0], sv->sre[1], sv->sim[0], sv->sim[1], sv->flags, sv->re, sv->im};
+    for (int i = 0; i < 7 && mine.ok; i++)
         if (cudaIpcGetMemHandle(&mine.h[i], exported[i]) != cudaSuccess) mine.ok = 0;
     if (n > kFlagRanks) mine.ok = 0;
     cudaGetLastError();
@@ -1196,14 +1282,18 @@ int setup_ce(lyth_sv *sv) {
     if (every) {
         for (int b = 0; b < 2; b++) { sv->peer_sre[b].assign(n, nullptr); sv->peer_sim[b].assign(n, nullptr); }
         sv->peer_flags.assign(n, nullptr);
+        sv->peer_re.assign(n, nullptr);
+        sv->peer_im.assign(n, nullptr);
         for (int r = 0; r < n && opened; r++) {
             if (r == sv->rank) {
                 for (int b = 0; b < 2; b++) { sv->peer_sre[b][r] = sv->sre[b]; sv->peer_sim[b][r] = sv->sim[b]; }
                 sv->peer_flags[r] = sv->flags;
+                sv->peer_re[r] = sv->re;
+                sv->peer_im[r] = sv->im;
                 continue;
             }
-            void *p[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
-            for (int i = 0; i < 5; i++) {
+            void *p[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+            for (int i = 0; i < 7; i++) {
                 if (cudaIpcOpenMemHandle(&p[i], all[r].h[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
                     cudaGetLastError();
                     opened = 0;
@@ -1215,6 +1305,8 @@ int setup_ce(lyth_sv *sv) {
             sv->peer_sre[0][r] = (float *)p[0]; sv->peer_sre[1][r] = (float *)p[1];
             sv->peer_sim[0][r] = (float *)p[2]; sv->peer_sim[1][r] = (float *)p[3];
             sv->peer_flags[r] = (uint64_t *)p[4];
+            sv->peer_re[r] = (float *)p[5];
+            sv->peer_im[r] = (float *)p[6];
         }
     }
     // every rank must agree: the transport is used only if every rank mapped every peer
@@ -1228,7 +1320,7 @@ int setup_ce(lyth_sv *sv) {
     if (st) { close_ipc(sv); return st; }
     // mixed by default: copy engines for pairwise swap-ins, peer loads for batched ones (measured
     // on 4 B200s: a batched swap-in 5 % shorter with peer loads, a pairwise one 20 % longer)
-    if (agreed) { sv->ce = true; sv->peer_load = 2; }
+    if (agreed) { sv->ce = true; sv->peer_mode = kPeerMixed; }
     else close_ipc(sv);
     return LYTH_OK;
 }
@@ -1478,7 +1570,7 @@ int lyth_sv_apply(lyth_sv *sv, const lyth_gate *gates, uint64_t count) {
 
 int lyth_sv_set_transport(lyth_sv *sv, int kind) {
     if (!sv) return LYTH_E_INVALID;
-    if (kind < 0 || kind > 3) return LYTH_E_INVALID;
+    if (kind < 0 || kind > 4) return LYTH_E_INVALID;
     if (kind && sv->peer_flags.empty()) return LYTH_E_UNSUPPORTED;
     if (!sv->plan) {
         DeviceGuard guard(sv);
@@ -1492,11 +1584,11 @@ int lyth_sv_set_transport(lyth_sv *sv, int kind) {
         if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
     }
     sv->ce = kind != 0;
-    sv->peer_load = kind == 2 ? 1 : kind == 3 ? 2 : 0;
+    sv->peer_mode = kind == 2 ? kPeerLoad : kind == 3 ? kPeerMixed : kind == 4 ? kPeerStore : kPeerNone;
     return LYTH_OK;
 }
 
-int lyth_sv_transport(const lyth_sv *sv) { return sv && sv->ce ? 1 + sv->peer_load : 0; }
+int lyth_sv_transport(const lyth_sv *sv) { return sv && sv->ce ? 1 + sv->peer_mode : 0; }
 
 int lyth_sv_set_chunk(lyth_sv *sv, uint64_t elements) {
     if (!sv) return LYTH_E_INVALID;

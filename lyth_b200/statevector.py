@@ -125,13 +125,14 @@ class StateVector:
         Collective: every rank sets the same value at the same point."""
         check(lib.lyth_sv_set_swap_batch(self._h, max_qubits), "set_swap_batch")
 
-    TRANSPORTS = ("nccl", "copy_engine", "peer_load", "mixed")
+    TRANSPORTS = ("nccl", "copy_engine", "peer_load", "mixed", "peer_store")
 
     def set_transport(self, kind) -> None:
         """Swap-in transport: "copy_engine" (copy engines over CUDA IPC), "peer_load" (the same
         mappings, the SMs load the partners' packed chunks straight into the shard), "mixed" (copy
         engines for pairwise swap-ins, peer loads for batched ones; the default when every rank
-        mapped every peer) or "nccl". True / False mean "copy_engine" / "nccl".
+        mapped every peer), "peer_store" (the SMs store this rank's packed chunks straight into
+        the partners' shards) or "nccl". True / False mean "copy_engine" / "nccl".
         Collective: every rank sets the same value at the same point."""
         if isinstance(kind, bool):
             kind = "copy_engine" if kind else "nccl"

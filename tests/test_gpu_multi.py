@@ -122,12 +122,14 @@ def test_two_ranks_pull_queues(queues, tmp_path):
 
 
 @pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("kind", ["peer_load", "peer_store"])
 @pytest.mark.parametrize("chunk", [None, 1024])
 @pytest.mark.parametrize("case", [0, 1, 2])
-def test_two_ranks_peer_load_transport(case, chunk, tmp_path):
-    # the SMs pull the partner's packed chunks and store them into the shard (no receive buffer);
-    # with 1024-amplitude chunks the send slots are reused many times within one exchange
-    _run_ranks(2, 18, case, True, 6, tmp_path, ce="peer_load", chunk=chunk)
+def test_two_ranks_peer_transport(case, chunk, kind, tmp_path):
+    # the SMs pull the partner's packed chunks and store them into the shard (no receive buffer),
+    # or store this rank's packed chunks into the partner's shard; with 1024-amplitude chunks the
+    # send slots are reused many times within one exchange
+    _run_ranks(2, 18, case, True, 6, tmp_path, ce=kind, chunk=chunk)
 
 
 @pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
@@ -151,9 +153,9 @@ def test_four_ranks_many_chunks(batch, tmp_path):
 
 
 @pytest.mark.skipif(_ngpus() < 4, reason="needs 4 GPUs")
-@pytest.mark.parametrize("kind", ["peer_load", "mixed"])
+@pytest.mark.parametrize("kind", ["peer_load", "mixed", "peer_store"])
 @pytest.mark.parametrize("batch", [6, 1])
-def test_four_ranks_peer_load_transport(batch, kind, tmp_path):
+def test_four_ranks_peer_transport(batch, kind, tmp_path):
     # batched swap-ins pull from 3 partners at once with SM loads, in short chunks; "mixed" takes
     # the copy engines for the pairwise ones in between
     _run_ranks(4, 19, 0, True, batch, tmp_path, ce=kind, chunk=1024)
@@ -172,6 +174,6 @@ def test_eight_ranks_bit_exact(case, tmp_path):
 
 
 @pytest.mark.skipif(_ngpus() < 8, reason="needs 8 GPUs")
-@pytest.mark.parametrize("kind", ["peer_load", "mixed"])
-def test_eight_ranks_peer_load_transport(kind, tmp_path):
+@pytest.mark.parametrize("kind", ["peer_load", "mixed", "peer_store"])
+def test_eight_ranks_peer_transport(kind, tmp_path):
     _run_ranks(8, 20, 0, True, 6, tmp_path, ce=kind, chunk=1024)

@@ -173,7 +173,8 @@ def test_plan_handle_settings_are_validated_on_the_host():
         assert lb.lib.lyth_sv_set_transport(p._h, 1) == lb.E_UNSUPPORTED
         assert lb.lib.lyth_sv_set_transport(p._h, 2) == lb.E_UNSUPPORTED
         assert lb.lib.lyth_sv_set_transport(p._h, 3) == lb.E_UNSUPPORTED
-        assert lb.lib.lyth_sv_set_transport(p._h, 4) == lb.E_INVALID
+        assert lb.lib.lyth_sv_set_transport(p._h, 4) == lb.E_UNSUPPORTED
+        assert lb.lib.lyth_sv_set_transport(p._h, 5) == lb.E_INVALID
         assert lb.lib.lyth_sv_set_transport(p._h, -1) == lb.E_INVALID
         assert lb.lib.lyth_sv_set_transport(p._h, 0) == lb.OK
         assert lb.lib.lyth_sv_transport(p._h) == 0
