@@ -17,10 +17,11 @@
 //    diagonal gate whose target is a rank bit is a scalar on each shard and moves no data. Any
 //    other gate whose target is a rank bit first swaps that qubit into a local bit (the local bit
 //    needed furthest ahead leaves): half the shard is packed, moved to the partner and unpacked into
-//    the positions it vacated, chunk by chunk, the move on the copy engines (cudaMemcpyAsync
-//    pulls through CUDA IPC mappings, ordered by sequence flags) or NCCL. With remap off the
-//    pair exchanges whole shards instead and each computes its own row of the gate as chunks
-//    land. Receive-then-compute throughout: no kernel loads a peer's memory.
+//    the positions it vacated, chunk by chunk, the move through CUDA IPC mappings ordered by
+//    sequence flags -- copy-engine pulls (cudaMemcpyAsync), SM peer loads fused with the unpack,
+//    or SM stores into the partners' shards -- or over NCCL. With remap off the pair exchanges
+//    whole shards instead and each computes its own row of the gate as chunks land. Peer memory
+//    is touched only by those copies and plain loads and stores: no TMA, no multicast.
 //
 // NCCL is opened with dlopen on first use by a multi-rank handle, so the library itself loads
 // (and serves every single-GPU entry point) without it.
@@ -782,7 +783,12 @@ int put_peers(lyth_sv *sv, cudaStream_t stream, const std::vector<int> &ranks, i
 // pulls its slice of each partner's packed chunk with cudaMemcpyAsync -- copy engines over NVLink,
 // no SMs -- after the partner's `packed` flag reaches the chunk's sequence number, then raises its
 // own `pulled` flag; a rank re-packs a send slot only after every partner that pulls from it has
-// raised `pulled` past it. Otherwise NCCL send / recv in one group per chunk. NCCL's transfer runs
+// raised `pulled` past it. The peer-load form keeps that protocol with pull_unpack_kernel in place
+// of the copies and the unpack (it also waits for this rank's own pack of the chunk, whose
+// positions it overwrites). The push form reads `packed` as "these positions are free": once
+// every partner has packed chunk c, a rank stores its packed slices into their shards
+// (push_kernel) and raises `landed` in each; the swap-in ends on the compute stream when every
+// partner's last `landed` has arrived. Otherwise NCCL send / recv in one group per chunk. NCCL's transfer runs
 // on SMs: measured on B200, its point-to-point bandwidth halves when a memory-bound kernel shares
 // every SM with it, so on that path pack / unpack take half the SMs.
 int physical_swap_multi(lyth_sv *sv, const std::vector<uint32_t> &V, const std::vector<uint32_t> &Gp) {
