@@ -776,6 +776,7 @@ def ours(a, dist: Dist) -> None:
     stream = torch.cuda.ExternalStream(sv.stream)
     clocks = Clocks(gpu_id_for(dist.local))
     launches0 = sv.stats()["launches"]
+    sent0 = sv.stats()["bytes_sent"]
     sv.reset_timing()
     sv.set_timing(True)
     dist.barrier()
@@ -828,8 +829,11 @@ def ours(a, dist: Dist) -> None:
                              "avg_ms": round(tim["exchange"][1] / tim["exchange"][0], 4) if tim["exchange"][0] else None},
                 "swap_in": {"count": tim["swap"][0],
                             "avg_ms": round(tim["swap"][1] / tim["swap"][0], 4) if tim["swap"][0] else None,
-                            "GB_s_each_way": round(4.0 * sv.local_len / (tim["swap"][1] / tim["swap"][0] * 1e-3) / 1e9, 1)
-                            if tim["swap"][0] else None,
+                            # what this rank sent in its swap-ins (half the shard for a pairwise
+                            # one, (2^k - 1) / 2^k for a batched one among 2^k ranks) over their
+                            # device time; as much arrives
+                            "GB_s_each_way": round((st["bytes_sent"] - sent0) / (tim["swap"][1] * 1e-3) / 1e9, 1)
+                            if tim["swap"][0] and not tim["exchange"][0] else None,
                             "share_of_timed_region": round(tim["swap"][1] / ms, 4) if ms else None}}
     mf = machine_file_peak()
     if mf and achieved:
