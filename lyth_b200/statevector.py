@@ -36,6 +36,10 @@ def gates_array(gates) -> "C.Array[Gate]":
     return arr
 
 
+# lyth_sv_set_transport's kinds, by index
+TRANSPORTS = ("nccl", "copy_engine", "peer_load", "mixed", "peer_store")
+
+
 class StateVector:
     """One rank's shard. ``nranks`` must be a power of two; ``nccl_id`` is required when > 1."""
 
@@ -125,7 +129,7 @@ class StateVector:
         Collective: every rank sets the same value at the same point."""
         check(lib.lyth_sv_set_swap_batch(self._h, max_qubits), "set_swap_batch")
 
-    TRANSPORTS = ("nccl", "copy_engine", "peer_load", "mixed", "peer_store")
+    TRANSPORTS = TRANSPORTS
 
     def set_transport(self, kind) -> None:
         """Swap-in transport: "copy_engine" (copy engines over CUDA IPC), "peer_load" (the same
@@ -136,9 +140,9 @@ class StateVector:
         Collective: every rank sets the same value at the same point."""
         if isinstance(kind, bool):
             kind = "copy_engine" if kind else "nccl"
-        if kind not in self.TRANSPORTS:
-            raise ValueError(f"transport {kind!r}: one of {self.TRANSPORTS}")
-        check(lib.lyth_sv_set_transport(self._h, self.TRANSPORTS.index(kind)), "set_transport")
+        if kind not in TRANSPORTS:
+            raise ValueError(f"transport {kind!r}: one of {TRANSPORTS}")
+        check(lib.lyth_sv_set_transport(self._h, TRANSPORTS.index(kind)), "set_transport")
 
     def set_chunk(self, elements: int) -> None:
         """Exchange pipeline chunk, amplitudes per component (power of two >= 1024). Collective."""
@@ -146,7 +150,7 @@ class StateVector:
 
     @property
     def transport(self) -> str:
-        return self.TRANSPORTS[lib.lyth_sv_transport(self._h)]
+        return TRANSPORTS[lib.lyth_sv_transport(self._h)]
 
     def timing(self) -> dict:
         """{class: (count, total ms)}: 'u' (1-qubit passes), 'cu' (2-qubit), 'exchange',

@@ -274,3 +274,23 @@ def test_pull_queue_setting_range():
             assert lb.lib.lyth_sv_set_pull_queues(p._h, q) == 0
         for q in (-1, 9):
             assert lb.lib.lyth_sv_set_pull_queues(p._h, q) == lb.E_UNSUPPORTED
+
+
+def test_transport_names_map_onto_the_c_abi_kinds():
+    # StateVector.set_transport / .transport are the names of lyth_sv_set_transport's kinds
+    # 0..4; a handle without IPC mappings (a plan handle here) takes only NCCL, and an unknown
+    # name is refused before any call
+    import lyth_b200 as lb
+    from lyth_b200.statevector import Plan, StateVector
+
+    assert StateVector.TRANSPORTS == ("nccl", "copy_engine", "peer_load", "mixed", "peer_store")
+    with Plan(16, 0, 2) as p:
+        StateVector.set_transport(p, "nccl")
+        StateVector.set_transport(p, False)
+        assert StateVector.transport.fget(p) == "nccl"
+        for kind in ("copy_engine", "peer_load", "mixed", "peer_store", True):
+            with pytest.raises(lb.LythError):
+                StateVector.set_transport(p, kind)
+        with pytest.raises(ValueError):
+            StateVector.set_transport(p, "shared_memory")
+        assert StateVector.transport.fget(p) == "nccl"
