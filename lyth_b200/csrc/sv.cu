@@ -356,6 +356,11 @@ int wait_with_deadline(const WaitHooks &h, double deadline_ms, uint32_t poll_us,
     }
 }
 
+// One rank's CUDA IPC handles, all-gathered at set-up of the IPC transports.
+struct IpcRec {
+    int32_t ok, pad;
+    cudaIpcMemHandle_t h[7];  // sre[0], sre[1], sim[0], sim[1], flags, re, im
+};
 }  // namespace lyth
 
 using namespace lyth;
@@ -428,6 +433,9 @@ struct lyth_sv {
     std::vector<float *> peer_sre[2], peer_sim[2];
     std::vector<uint64_t *> peer_flags;  // every rank's flag block (own included)
     std::vector<float *> peer_re, peer_im;  // every rank's shard (the push form's destinations)
+    // every rank's IPC handles from set-up: the shards are opened only when the push form is
+    // selected (lyth_sv_set_transport 4), so the other forms map just the chunks and flags
+    std::vector<IpcRec> ipc_all;
     std::vector<void *> ipc_opened;
     uint64_t xseq = 0;                       // chunk sequence number, identical on every rank
     uint64_t slot_seq[2] = {0, 0};           // last chunk packed into send slot b
@@ -1238,12 +1246,9 @@ int apply_one(lyth_sv *sv, const lyth_gate *gates, uint64_t count, uint64_t i) {
     }
 }
 
-// Copy-engine transport set-up (collective over the handle's ranks): map every rank's send chunks
-// and flag block through CUDA IPC. Every rank ends with the same `ce` (false: NCCL for swaps).
-struct IpcRec {
-    int32_t ok, pad;
-    cudaIpcMemHandle_t h[7];  // sre[0], sre[1], sim[0], sim[1], flags, re, im
-};
+// IPC transport set-up (collective over the handle's ranks): all-gather every rank's handles and
+// map every rank's send chunks and flag block through CUDA IPC (the shards wait for open_shards).
+// Every rank ends with the same `ce` (false: NCCL for swaps).
 
 void close_ipc(lyth_sv *sv) {
     for (void *p : sv->ipc_opened) cudaIpcCloseMemHandle(p);
@@ -1252,6 +1257,7 @@ void close_ipc(lyth_sv *sv) {
     sv->peer_flags.clear();
     sv->peer_re.clear();
     sv->peer_im.clear();
+    sv->ipc_all.clear();
     sv->ce = false;
     sv->peer_mode = kPeerNone;
 }
@@ -1288,18 +1294,14 @@ int setup_ce(lyth_sv *sv) {
     if (every) {
         for (int b = 0; b < 2; b++) { sv->peer_sre[b].assign(n, nullptr); sv->peer_sim[b].assign(n, nullptr); }
         sv->peer_flags.assign(n, nullptr);
-        sv->peer_re.assign(n, nullptr);
-        sv->peer_im.assign(n, nullptr);
         for (int r = 0; r < n && opened; r++) {
             if (r == sv->rank) {
                 for (int b = 0; b < 2; b++) { sv->peer_sre[b][r] = sv->sre[b]; sv->peer_sim[b][r] = sv->sim[b]; }
                 sv->peer_flags[r] = sv->flags;
-                sv->peer_re[r] = sv->re;
-                sv->peer_im[r] = sv->im;
                 continue;
             }
-            void *p[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
-            for (int i = 0; i < 7; i++) {
+            void *p[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+            for (int i = 0; i < 5; i++) {
                 if (cudaIpcOpenMemHandle(&p[i], all[r].h[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
                     cudaGetLastError();
                     opened = 0;
@@ -1311,8 +1313,6 @@ int setup_ce(lyth_sv *sv) {
             sv->peer_sre[0][r] = (float *)p[0]; sv->peer_sre[1][r] = (float *)p[1];
             sv->peer_sim[0][r] = (float *)p[2]; sv->peer_sim[1][r] = (float *)p[3];
             sv->peer_flags[r] = (uint64_t *)p[4];
-            sv->peer_re[r] = (float *)p[5];
-            sv->peer_im[r] = (float *)p[6];
         }
     }
     // every rank must agree: the transport is used only if every rank mapped every peer
@@ -1326,8 +1326,53 @@ int setup_ce(lyth_sv *sv) {
     if (st) { close_ipc(sv); return st; }
     // mixed by default: copy engines for pairwise swap-ins, peer loads for batched ones (measured
     // on 4 B200s: a batched swap-in 5 % shorter with peer loads, a pairwise one 20 % longer)
-    if (agreed) { sv->ce = true; sv->peer_mode = kPeerMixed; }
-    else close_ipc(sv);
+    if (agreed) {
+        sv->ce = true;
+        sv->peer_mode = kPeerMixed;
+        sv->ipc_all = all;
+    } else {
+        close_ipc(sv);
+    }
+    return LYTH_OK;
+}
+
+// Map every partner's shard for the push form (collective: lyth_sv_set_transport 4 on every rank,
+// after the drain). Every rank agrees through an NCCL min, as at set-up; on a refusal nothing
+// stays mapped and LYTH_E_UNSUPPORTED is returned on every rank.
+int open_shards(lyth_sv *sv) {
+    if (!sv->peer_re.empty()) return LYTH_OK;
+    if (sv->comm_aborted) return LYTH_E_NCCL;
+    const int n = sv->nranks;
+    int32_t opened = (int)sv->ipc_all.size() == n ? 1 : 0;
+    std::vector<void *> mapped;
+    std::vector<float *> pre(n, nullptr), pim(n, nullptr);
+    for (int r = 0; r < n && opened; r++) {
+        if (r == sv->rank) { pre[r] = sv->re; pim[r] = sv->im; continue; }
+        void *p[2] = {nullptr, nullptr};
+        for (int i = 0; i < 2; i++) {
+            if (cudaIpcOpenMemHandle(&p[i], sv->ipc_all[r].h[5 + i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                opened = 0;
+                break;
+            }
+            mapped.push_back(p[i]);
+        }
+        if (opened) { pre[r] = (float *)p[0]; pim[r] = (float *)p[1]; }
+    }
+    // the norm scratch holds the vote (nothing is in flight after the drain)
+    int32_t *dok = reinterpret_cast<int32_t *>(sv->scratch);
+    int st = status_of(cudaMemcpy(dok, &opened, sizeof opened, cudaMemcpyHostToDevice));
+    if (!st) st = nccl_status(g_nccl.AllReduce(dok, dok, 1, ncclInt32, ncclMin, sv->comm, sv->stream));
+    if (!st) st = sync_stream(sv, sv->stream);
+    int32_t agreed = 0;
+    if (!st) st = status_of(cudaMemcpy(&agreed, dok, sizeof agreed, cudaMemcpyDeviceToHost));
+    if (st || !agreed) {
+        for (void *p : mapped) cudaIpcCloseMemHandle(p);
+        return st ? st : LYTH_E_UNSUPPORTED;
+    }
+    sv->peer_re = pre;
+    sv->peer_im = pim;
+    sv->ipc_opened.insert(sv->ipc_opened.end(), mapped.begin(), mapped.end());
     return LYTH_OK;
 }
 
@@ -1588,6 +1633,7 @@ int lyth_sv_set_transport(lyth_sv *sv, int kind) {
             for (int b = 0; b < 2; b++)
                 if (sv->slot_seq[b]) wait_own(sv, sv->stream, sv->slot_partners[b], kPulledAt, b, sv->slot_seq[b]);
         if ((st = status_of(cudaStreamSynchronize(sv->stream)))) return st;
+        if (kind == 4 && (st = open_shards(sv))) return st;
     }
     sv->ce = kind != 0;
     sv->peer_mode = kind == 2 ? kPeerLoad : kind == 3 ? kPeerMixed : kind == 4 ? kPeerStore : kPeerNone;
