@@ -5,7 +5,10 @@ chunks ("ce"), SM peer loads fused with the unpack ("pl"), SM stores into the pa
 ("ps") -- and consecutive swap-ins that mix the forms as the "mixed" default does. Kernels run one
 cell at a time in a random order and interleave with every other stream, so a read that could see
 a cell before its writer (or after its overwriter) shows up as a wrong final shard; a wait that
-could never end shows up as a deadlock. Each shard must end as a sequential swap of bits leaves it.
+could never end shows up as a deadlock. Each shard, read out on its own compute stream after the
+swap-ins, must be what a sequential swap of bits leaves, and a rank's teardown (teardown_ce: streams
+drained, its send slots' "pulled" flags awaited, then its memory freed) must never precede a
+peer's access to that memory.
 
 The model is a statement of the protocol, not the CUDA code: it follows the engine's issue order,
 and the comments name the step of physical_swap_multi each group of ops mirrors."""
@@ -19,22 +22,43 @@ class Event:
         self.latest = None
 
 
+class Mem(dict):
+    """One rank's device memory (a shard, a chunk slot or a flag block): any access after the rank
+    freed it is a use after free by a peer."""
+    freed = False
+
+    def _check(self):
+        assert not self.freed, "a peer touched memory its owner had freed"
+
+    def __getitem__(self, k):
+        self._check()
+        return dict.__getitem__(self, k)
+
+    def __setitem__(self, k, v):
+        self._check()
+        dict.__setitem__(self, k, v)
+
+    def get(self, k, d=None):
+        self._check()
+        return dict.get(self, k, d)
+
+
 class World:
     def __init__(self, nranks, nbits, nchunks, seed):
         self.R, self.G, self.N = nranks, nbits, nchunks
         self.rng = random.Random(seed)
-        self.state = [{(cls, c): (r, cls, c) for cls in range(1 << nbits) for c in range(nchunks)}
+        self.state = [Mem({(cls, c): (r, cls, c) for cls in range(1 << nbits) for c in range(nchunks)})
                       for r in range(nranks)]
-        self.sre = [[{}, {}] for _ in range(nranks)]
-        self.rre = [[{}, {}] for _ in range(nranks)]
-        self.flags = [dict() for _ in range(nranks)]
+        self.sre = [[Mem(), Mem()] for _ in range(nranks)]
+        self.rre = [[Mem(), Mem()] for _ in range(nranks)]
+        self.flags = [Mem() for _ in range(nranks)]
         self.streams = [{"S": [], "M": []} for _ in range(nranks)]
         self.done_records = set()
         self.next_rid = 0
         self.xseq = [0] * nranks
         self.slot_seq = [[0, 0] for _ in range(nranks)]
         self.slot_partners = [[[], []] for _ in range(nranks)]
-        self.ev = [{k: Event() for k in ("start", "packed0", "packed1", "recv0", "recv1", "done0", "done1")}
+        self.ev = [{k: Event() for k in ("start", "packed0", "packed1", "recv0", "recv1", "done0", "done1", "drained")}
                    for _ in range(nranks)]
 
     # ---- ops
@@ -58,6 +82,9 @@ class World:
     def flag_put(self, r, s, kind, dsts, b, value):
         self.streams[r][s].append(("flag_put", r, kind, tuple(dsts), b, value))
 
+    def free(self, r, s):
+        self.streams[r][s].append(("free", r))
+
     def ready(self, op):
         if op[0] == "wait_event":
             return op[1] is None or op[1] in self.done_records
@@ -69,6 +96,10 @@ class World:
     def step(self, op, queue):
         if op[0] == "record":
             self.done_records.add(op[1])
+        elif op[0] == "free":
+            r = op[1]
+            for m in [self.state[r], self.flags[r], *self.sre[r], *self.rre[r]]:
+                m.freed = True
         elif op[0] == "flag_put":
             _, r, kind, dsts, b, value = op
             for d in dsts:
@@ -214,6 +245,18 @@ def issue_swap(w, K, form_of):
         w.xseq[r] = seq0 + N
 
 
+def issue_teardown(w, wait_pulled=True):
+    """teardown_ce: both streams drained, then every partner has pulled the last chunk of each send
+    slot, then the rank's buffers and flag block go."""
+    for r in range(w.R):
+        w.record(r, "M", "drained")
+        w.wait_event(r, "S", "drained")
+        for b in range(2):
+            if wait_pulled and w.slot_seq[r][b]:
+                w.flag_wait(r, "S", "pulled", w.slot_partners[r][b], b, w.slot_seq[r][b])
+        w.free(r, "S")
+
+
 def sequential(state, nbits, K):
     out = [dict() for _ in state]
     for r, shard in enumerate(state):
@@ -232,7 +275,7 @@ FORMS = {
 }
 
 
-def run_case(nbits, nchunks, swaps, transports, seed):
+def run_case(nbits, nchunks, swaps, transports, seed, teardown_waits=True):
     R = 1 << nbits
     w = World(R, nbits, nchunks, seed)
     want = [dict(s) for s in w.state]
@@ -240,9 +283,14 @@ def run_case(nbits, nchunks, swaps, transports, seed):
     for K, t in zip(swaps, transports):
         issue_swap(w, K, FORMS[t])
         want = sequential(want, nbits, K)
+    got = [dict(s) for s in w.state]
+    # each rank reads its shard out after its own streams have finished the swap-ins
+    for r in range(R):
+        w.streams[r]["S"].append(("kernel", [lambda r=r: got[r].update(dict.items(w.state[r]))]))
+    issue_teardown(w, teardown_waits)
     w.run()
     for r in range(R):
-        assert w.state[r] == want[r], f"rank {r}: shard differs from the sequential swaps"
+        assert got[r] == want[r], f"rank {r}: shard differs from the sequential swaps"
 
 
 @pytest.mark.parametrize("form", ["ce", "pl", "ps", "mixed"])
@@ -287,3 +335,16 @@ def test_the_model_catches_a_missing_wait():
     finally:
         World.flag_wait = original
     assert failed, "the model did not detect the missing wait"
+
+
+def test_the_model_catches_a_teardown_that_does_not_wait_for_the_pulls():
+    # with peer loads a partner reads this rank's send slot after this rank's own streams are
+    # done; freeing without waiting for its "pulled" flags lets that read land on freed memory
+    caught = False
+    for seed in range(80):
+        try:
+            run_case(1, 1, [[0]], ["pl"], seed, teardown_waits=False)
+        except AssertionError:
+            caught = True
+            break
+    assert caught, "the model did not detect the early free"
