@@ -111,7 +111,7 @@ def args_():
     ap.add_argument("--swap-batch", type=int, default=None,
                     help="most rank-bit qubits per swap-in (1..6; default: the engine's)")
     ap.add_argument("--transport", choices=["copy_engine", "peer_load", "mixed", "peer_store", "nccl"], default=None,
-                    help="swap-in transport at N > 1 (default: the engine's)")
+                    help="swap-in transport at N > 1 (default: the engine's, mixed when every rank maps every peer)")
     ap.add_argument("--pull-queues", type=int, default=None,
                     help="copy-engine queues per swap-in pull at N > 1 (1..8; default: the engine's, one per partner slice)")
     ap.add_argument("--diagonal", type=int, choices=[0, 1], default=None,
